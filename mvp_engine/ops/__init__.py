@@ -1,0 +1,457 @@
+"""Hot-path operators of the engine.
+
+On CUDA every operator here runs a hand-written sm_100a kernel from
+``mvp_engine._C`` (tcgen05 GEMM, fused norms, RoPE, SwiGLU, cross-entropy,
+AdamW, embedding); a missing extension raises.  On CPU the same operators
+run plain PyTorch math with identical semantics, which is what the CPU test
+suite and the gloo multi-process tests exercise.
+
+Weight gradients: a weight tensor may carry a ``_mvp_grad_acc`` attribute
+(an fp32 tensor of the same shape, usually a view into a flat gradient
+buffer owned by the data-parallel wrapper).  When present, the backward of
+:func:`linear` / :func:`embedding` accumulates the weight gradient straight
+into it with the GEMM's fp32 accumulate epilogue, and no per-parameter
+gradient tensor is materialised.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _ext
+
+__all__ = [
+    "gemm",
+    "linear",
+    "rms_norm",
+    "qk_norm_rope",
+    "RopeCache",
+    "swiglu",
+    "embedding",
+    "fused_linear_cross_entropy",
+    "adamw_step_",
+    "sumsq",
+]
+
+
+def _native(t: torch.Tensor) -> bool:
+    if not t.is_cuda:
+        return False
+    if not _ext.native_required():
+        return _ext.available()
+    return True
+
+
+# --------------------------------------------------------------------- GEMM
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    out: Optional[torch.Tensor] = None,
+    accumulate: bool = False,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> torch.Tensor:
+    """C (+)= A * B^T on the tcgen05 tensor core.
+
+    ``a`` is ``[M, K]`` (or ``[K, M]`` when ``a_mn``), ``b`` is ``[N, K]`` (or
+    ``[K, N]`` when ``b_mn``).  The result is ``[M, N]`` in ``out_dtype`` (bf16 or
+    fp32); ``accumulate=True`` adds into an fp32 ``out``.
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if not _native(a):
+        A = a.t() if a_mn else a
+        B = b if b_mn else b.t()
+        res = A.float() @ B.float()
+        if out is None:
+            return res.to(out_dtype)
+        if accumulate:
+            out.add_(res)
+        else:
+            out.copy_(res)
+        return out
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _ext.ext().gemm(a, a_mn, b, b_mn, out, accumulate, _ext.status_buffer(a.device).data_ptr())
+    return out
+
+
+def _wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor) -> Optional[torch.Tensor]:
+    """dW = dY^T X, accumulated into ``w._mvp_grad_acc`` when present."""
+    acc = getattr(w, "_mvp_grad_acc", None)
+    if acc is not None:
+        gemm(dy2, x2, a_mn=True, b_mn=True, out=acc, accumulate=True)
+        return None
+    return gemm(dy2, x2, a_mn=True, b_mn=True, out_dtype=w.dtype if w.dtype != torch.float32 else torch.float32)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, w: torch.Tensor):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0:
+            x2 = x2.contiguous()
+        y = gemm(x2, w)
+        ctx.save_for_backward(x2, w)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        x2, w = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dy2, w, b_mn=True).view(*dy.shape[:-1], w.shape[1])
+        dw = None
+        if getattr(w, "_mvp_grad_acc", None) is not None or ctx.needs_input_grad[1]:
+            dw = _wgrad(dy2, x2, w)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` (no bias) on the tcgen05 GEMM; eager ``F.linear`` on CPU."""
+    if not _native(x):
+        return F.linear(x, w.to(x.dtype))
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if w.dtype != torch.bfloat16:
+        raise TypeError("linear: the CUDA path expects bf16 weights (cast by the data-parallel wrapper)")
+    return _Linear.apply(x, w)
+
+
+# ------------------------------------------------------------------ RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, residual, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        r2 = residual.reshape(-1, shape[-1]).contiguous() if residual is not None else None
+        outs = _ext.ext().rmsnorm_fwd(x2, r2, w, eps)
+        y, rstd = outs[0], outs[1]
+        h = outs[2] if residual is not None else x2
+        ctx.save_for_backward(h, rstd, w)
+        ctx.has_res = residual is not None
+        ctx.shape = shape
+        return y.view(shape), h.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy, dh):
+        h, rstd, w = ctx.saved_tensors
+        H = ctx.shape[-1]
+        dy2 = dy.reshape(-1, H).contiguous()
+        dh2 = dh.reshape(-1, H).contiguous() if dh is not None else None
+        outs = _ext.ext().rmsnorm_bwd(dy2, h, rstd, w, dh2, True)
+        dx = outs[0].view(ctx.shape)
+        dw = outs[1]
+        acc = getattr(w, "_mvp_grad_acc", None)
+        if acc is not None:
+            acc.add_(dw)
+            dw = None
+        else:
+            dw = dw.to(w.dtype)
+        return dx, dw, (dx if ctx.has_res else None), None
+
+
+def _rms_norm_eager(x, w, eps):
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return w.to(x.dtype) * (xf * torch.rsqrt(var + eps)).to(x.dtype)
+
+
+def rms_norm(
+    x: torch.Tensor, w: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Return ``(rmsnorm(h) * w, h)`` with ``h = x + residual`` (or ``x``)."""
+    if not _native(x):
+        h = x if residual is None else (x + residual)
+        return _rms_norm_eager(h, w, eps), h
+    return _RMSNorm.apply(x, w, residual, float(eps))
+
+
+# ------------------------------------------------------------ QK-norm + RoPE
+class RopeCache:
+    """cos/sin tables for (M-)RoPE, built the way HF's rotary embedding builds them.
+
+    ``inv_freq = 1 / theta^(arange(0, D, 2)/D)`` in fp32 and
+    ``angle[p, i] = p * inv_freq[i]`` in fp32; the kernels round cos/sin to
+    bf16 at use, as HF casts them to the activation dtype.  ``mrope_section``
+    (Qwen3-VL, e.g. ``[24, 20, 20]``) assigns each frequency to the t/h/w
+    position axis with the interleaved layout.
+    """
+
+    def __init__(
+        self, head_dim: int, theta: float, mrope_section: Optional[list[int]] = None, max_positions: int = 32768
+    ):
+        self.head_dim = head_dim
+        self.max_positions = int(max_positions)
+        self.theta = float(theta)
+        self.mrope_section = list(mrope_section) if mrope_section else None
+        self.inv_freq = 1.0 / (self.theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+        axis = torch.zeros(head_dim // 2, dtype=torch.int8)
+        if self.mrope_section:
+            for dim, offset in ((1, 1), (2, 2)):
+                length = self.mrope_section[dim] * 3
+                axis[offset:length:3] = dim
+        self.axis_of = axis
+        self._tables: dict[torch.device, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+
+    def tables(self, device: torch.device, max_pos: int = 0):
+        """Device tables covering positions [0, max(max_positions, max_pos+1))."""
+        cached = self._tables.get(device)
+        if cached is None or cached[0].shape[0] <= max_pos:
+            n = max(self.max_positions, 1 << int(math.ceil(math.log2(max_pos + 1))))
+            p = torch.arange(n, dtype=torch.float32)
+            ang = torch.outer(p, self.inv_freq)
+            cached = (ang.cos().to(device), ang.sin().to(device), self.axis_of.to(device))
+            self._tables[device] = cached
+        return cached
+
+    def cos_sin(self, pos: torch.Tensor, dtype: torch.dtype):
+        """Eager [T, D] cos/sin for positions ``pos`` of shape [A, T] (HF layout)."""
+        inv = self.inv_freq.to(pos.device)
+        ang = pos.float().unsqueeze(-1) * inv  # [A, T, D/2]
+        axis = self.axis_of.to(pos.device).long()
+        if pos.shape[0] > 1:
+            ang = ang.gather(0, axis.view(1, 1, -1).expand(1, ang.shape[1], -1)).squeeze(0)
+        else:
+            ang = ang[0]
+        emb = torch.cat([ang, ang], dim=-1)
+        return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, pos, hq, hkv, cache, eps):
+        cos_t, sin_t, axis = cache.tables(qkv.device)
+        q, k, rstd = _ext.ext().qk_norm_rope_fwd(qkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, eps)
+        ctx.save_for_backward(qkv, wq, wk, pos, rstd)
+        ctx.meta = (hq, hkv, cache)
+        return q, k
+
+    @staticmethod
+    def backward(ctx, dq, dk):
+        qkv, wq, wk, pos, rstd = ctx.saved_tensors
+        hq, hkv, cache = ctx.meta
+        cos_t, sin_t, axis = cache.tables(qkv.device, 0)
+        dqkv = _QKNormRope.pending_dqkv(qkv)
+        dwq, dwk = _ext.ext().qk_norm_rope_bwd(
+            dq.contiguous(), dk.contiguous(), qkv, dqkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, rstd
+        )
+        out_w = []
+        for w, dw in ((wq, dwq), (wk, dwk)):
+            acc = getattr(w, "_mvp_grad_acc", None)
+            if acc is not None:
+                acc.add_(dw)
+                out_w.append(None)
+            else:
+                out_w.append(dw.to(w.dtype))
+        return dqkv, out_w[0], out_w[1], None, None, None, None, None
+
+    @staticmethod
+    def pending_dqkv(qkv):
+        # The v slice is filled by the attention backward through the same buffer
+        # when both run in one fused block; standalone use gets zeros there.
+        return torch.zeros_like(qkv)
+
+
+def _rotate_half(x):
+    x1, x2 = x.chunk(2, dim=-1)
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def qk_norm_rope(
+    qkv: torch.Tensor,
+    n_q: int,
+    n_kv: int,
+    wq: torch.Tensor,
+    wk: torch.Tensor,
+    pos: torch.Tensor,
+    cache: RopeCache,
+    eps: float,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-head RMSNorm of q and k followed by RoPE.
+
+    ``qkv`` is ``[T, (n_q + 2 n_kv) * D]``; ``pos`` is ``[A, T]`` int (A = 1
+    for RoPE, 3 for M-RoPE).  Returns ``q [T, n_q, D]`` and ``k [T, n_kv, D]``.
+    """
+    D = cache.head_dim
+    T = qkv.shape[0]
+    if not _native(qkv):
+        q = qkv[:, : n_q * D].reshape(T, n_q, D)
+        k = qkv[:, n_q * D : (n_q + n_kv) * D].reshape(T, n_kv, D)
+        q = _rms_norm_eager(q, wq, eps)
+        k = _rms_norm_eager(k, wk, eps)
+        cos, sin = cache.cos_sin(pos, qkv.dtype)
+        cos = cos.unsqueeze(1)
+        sin = sin.unsqueeze(1)
+        return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin
+    if D != 128:
+        raise ValueError("qk_norm_rope: the CUDA kernel is specialised for head_dim 128")
+    pos = pos.to(torch.int32).contiguous()
+    return _QKNormRope.apply(qkv, wq, wk, pos, n_q, n_kv, cache, float(eps))
+
+
+# ------------------------------------------------------------------- SwiGLU
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        gu = gu.contiguous()
+        ctx.save_for_backward(gu)
+        return _ext.ext().swiglu_fwd(gu)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (gu,) = ctx.saved_tensors
+        return _ext.ext().swiglu_bwd(gu, dout.contiguous())
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` for ``gu = [T, 2F]`` (gate columns first)."""
+    if not _native(gu):
+        g, u = gu.chunk(2, dim=-1)
+        return F.silu(g) * u
+    return _SwiGLU.apply(gu)
+
+
+# ---------------------------------------------------------------- embedding
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, w, anchor):
+        ctx.save_for_backward(ids, w)
+        return _ext.ext().embedding_fwd(w, ids.reshape(-1).contiguous()).view(*ids.shape, w.shape[1])
+
+    @staticmethod
+    def backward(ctx, dout):
+        ids, w = ctx.saved_tensors
+        acc = getattr(w, "_mvp_grad_acc", None)
+        dw = None
+        if acc is not None:
+            _ext.ext().embedding_bwd_(acc, dout.reshape(-1, w.shape[1]).contiguous(), ids.reshape(-1).contiguous())
+        elif ctx.needs_input_grad[1]:
+            g = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+            _ext.ext().embedding_bwd_(g, dout.reshape(-1, w.shape[1]).contiguous(), ids.reshape(-1).contiguous())
+            dw = g.to(w.dtype)
+        return None, dw, None
+
+
+def embedding(ids: torch.Tensor, w: torch.Tensor, anchor: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Row gather ``w[ids]``; ``anchor`` (a tensor requiring grad) forces the backward to run
+    when ``w`` itself does not require grad but accumulates through ``_mvp_grad_acc``."""
+    if not _native(w):
+        return F.embedding(ids, w)
+    return _Embedding.apply(ids, w, anchor)
+
+
+# ------------------------------------------------- fused linear cross-entropy
+class _LinearCE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, w, labels, chunk):
+        T = h.shape[0]
+        losses = torch.empty(T, dtype=torch.float32, device=h.device)
+        lses = torch.empty(T, dtype=torch.float32, device=h.device)
+        for s in range(0, T, chunk):
+            e = min(T, s + chunk)
+            logits = gemm(h[s:e], w)
+            loss, lse = _ext.ext().ce_fwd(logits, labels[s:e])
+            losses[s:e] = loss
+            lses[s:e] = lse
+            del logits
+        ctx.save_for_backward(h, w, labels, lses)
+        ctx.chunk = chunk
+        return losses
+
+    @staticmethod
+    def backward(ctx, g):
+        h, w, labels, lses = ctx.saved_tensors
+        chunk = ctx.chunk
+        g = g.float()
+        if g.dim() == 0 or g.numel() == 1:
+            g = g.reshape(1).expand(h.shape[0])
+        g = g.contiguous()
+        dh = torch.empty_like(h)
+        acc = getattr(w, "_mvp_grad_acc", None)
+        dw = None
+        if acc is None and ctx.needs_input_grad[1]:
+            dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        target = acc if acc is not None else dw
+        for s in range(0, h.shape[0], chunk):
+            e = min(h.shape[0], s + chunk)
+            logits = gemm(h[s:e], w)
+            _ext.ext().ce_bwd_(logits, labels[s:e], lses[s:e], g[s:e])
+            gemm(logits, w, b_mn=True, out=dh[s:e])
+            if target is not None:
+                gemm(logits, h[s:e], a_mn=True, b_mn=True, out=target, accumulate=True)
+            del logits
+        return dh, (dw.to(w.dtype) if dw is not None else None), None, None
+
+
+def fused_linear_cross_entropy(
+    h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, chunk_size: int = 4096
+) -> torch.Tensor:
+    """Per-token CE of ``h @ w.T`` against ``labels`` (ignore index -100), chunked so the
+    full ``[T, V]`` logits never exist; the backward recomputes each logits chunk."""
+    if not _native(h):
+        out = []
+        for s in range(0, h.shape[0], chunk_size):
+            lg = F.linear(h[s : s + chunk_size], w.to(h.dtype))
+            out.append(F.cross_entropy(lg.float(), labels[s : s + chunk_size], ignore_index=-100, reduction="none"))
+        return torch.cat(out) if out else h.new_zeros(0, dtype=torch.float32)
+    return _LinearCE.apply(h.contiguous(), w, labels.contiguous(), int(chunk_size))
+
+
+# ------------------------------------------------------------ optimizer ops
+def adamw_step_(
+    p: torch.Tensor,
+    g: torch.Tensor,
+    m: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    lr: float,
+    beta1: float,
+    beta2: float,
+    eps: float,
+    weight_decay: float,
+    step: int,
+    grad_scale: float = 1.0,
+    norm_sq: Optional[torch.Tensor] = None,
+    max_norm: float = 0.0,
+    p_bf16: Optional[torch.Tensor] = None,
+) -> None:
+    """Decoupled-weight-decay Adam on flat fp32 buffers, mirroring ``torch.optim.AdamW``
+    (single-tensor path).  The gradient is multiplied by ``grad_scale`` and, when
+    ``norm_sq`` is given, by the clip coefficient ``min(1, max_norm / (sqrt(norm_sq)*grad_scale + 1e-6))``."""
+    if not _native(p):
+        with torch.no_grad():
+            scale = grad_scale
+            if norm_sq is not None:
+                total = float(norm_sq.sqrt()) * grad_scale
+                scale *= min(1.0, max_norm / (total + 1e-6))
+            gg = g * scale
+            p.mul_(1 - lr * weight_decay)
+            m.lerp_(gg, 1 - beta1)
+            v.mul_(beta2).addcmul_(gg, gg, value=1 - beta2)
+            bc1 = 1 - beta1**step
+            bc2 = 1 - beta2**step
+            denom = (v.sqrt() / math.sqrt(bc2)).add_(eps)
+            p.addcdiv_(m, denom, value=-lr / bc1)
+            if p_bf16 is not None:
+                p_bf16.copy_(p)
+        return
+    _ext.ext().adamw_step_(
+        p, g, m, v, p_bf16, lr, beta1, beta2, eps, weight_decay, int(step), grad_scale, norm_sq, max_norm
+    )
+
+
+def sumsq(x: torch.Tensor) -> torch.Tensor:
+    """Sum of squares of a contiguous fp32/bf16 buffer (fp32 result, deterministic order)."""
+    if not _native(x):
+        return x.float().pow(2).sum()
+    return _ext.ext().sumsq(x.contiguous())

@@ -1,0 +1,49 @@
+// Python bindings of the sm_100a kernels (module mvp_engine._C).
+#include <torch/extension.h>
+
+void gemm_sm100(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                bool accumulate, int64_t status_ptr);
+
+std::vector<torch::Tensor> rmsnorm_fwd(const torch::Tensor& x, const c10::optional<torch::Tensor>& res,
+                                       const torch::Tensor& w, double eps);
+std::vector<torch::Tensor> rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& h, const torch::Tensor& rstd,
+                                       const torch::Tensor& w, const c10::optional<torch::Tensor>& dres, bool need_dw);
+std::vector<torch::Tensor> qk_norm_rope_fwd(const torch::Tensor& qkv, int64_t Hq, int64_t Hkv,
+                                            const torch::Tensor& wq, const torch::Tensor& wk,
+                                            const torch::Tensor& pos, const torch::Tensor& axis_of,
+                                            const torch::Tensor& cos_tab, const torch::Tensor& sin_tab, double eps);
+std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk,
+                                            const torch::Tensor& qkv, torch::Tensor& dqkv, int64_t Hq, int64_t Hkv,
+                                            const torch::Tensor& wq, const torch::Tensor& wk,
+                                            const torch::Tensor& pos, const torch::Tensor& axis_of,
+                                            const torch::Tensor& cos_tab, const torch::Tensor& sin_tab,
+                                            const torch::Tensor& rstd);
+torch::Tensor swiglu_fwd(const torch::Tensor& gu);
+torch::Tensor swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& dout);
+
+std::vector<torch::Tensor> ce_fwd(const torch::Tensor& logits, const torch::Tensor& labels);
+void ce_bwd_(torch::Tensor& logits, const torch::Tensor& labels, const torch::Tensor& lse, const torch::Tensor& g);
+void adamw_step_(torch::Tensor& p, const torch::Tensor& g, torch::Tensor& m, torch::Tensor& v,
+                 const c10::optional<torch::Tensor>& p_bf16, double lr, double beta1, double beta2, double eps,
+                 double wd, int64_t step, double grad_scale, const c10::optional<torch::Tensor>& norm_sq,
+                 double max_norm);
+torch::Tensor sumsq(const torch::Tensor& x);
+torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids);
+void embedding_bwd_(torch::Tensor& dw, const torch::Tensor& dout, const torch::Tensor& ids);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mvp_engine sm_100a kernels";
+  m.def("gemm", &gemm_sm100, "tcgen05 bf16 GEMM C (+)= A * B^T with K- or MN-major operands");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd_", &ce_bwd_);
+  m.def("adamw_step_", &adamw_step_);
+  m.def("sumsq", &sumsq);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd_", &embedding_bwd_);
+}

@@ -1,0 +1,105 @@
+"""Kernel microbenchmarks timed with CUDA events (warm-up, L2 flush between runs).
+
+Usage::
+
+    python -m mvp_engine.ops.microbench gemm            # Qwen3-8B layer shapes, ours vs cuBLAS
+    python -m mvp_engine.ops.microbench gemm --shape 8192,24576,4096 --iters 20
+
+Prints one JSON line per case with the kernel time and achieved TFLOP/s.
+cuBLAS (``torch.matmul``) is timed alongside only as the comparison column.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+L2_FLUSH_BYTES = 256 << 20  # twice the B200 L2
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+QWEN3_8B_SHAPES = {
+    # name: (M, N, K) of Y[M,N] = X[M,K] W[N,K]^T for an 8192-token micro-batch
+    "qkv": (8192, 6144, 4096),
+    "o_proj": (8192, 4096, 4096),
+    "gate_up": (8192, 24576, 4096),
+    "down": (8192, 4096, 12288),
+    "lm_head_chunk": (4096, 151936, 4096),
+}
+
+
+def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
+    from mvp_engine import ops
+
+    for name, (M, N, K) in shapes.items():
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = torch.randn(N, K, device="cuda").bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        flops = 2.0 * M * N * K
+        cases = {
+            "fwd": (lambda: ops.gemm(x, w), lambda: torch.matmul(x, w.t())),
+            "dgrad": (lambda: ops.gemm(dy, w, b_mn=True), lambda: torch.matmul(dy, w)),
+            "wgrad": (
+                lambda: ops.gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32),
+                lambda: torch.matmul(dy.t(), x),
+            ),
+        }
+        for kind, (ours, ref) in cases.items():
+            t_ours = _time(ours, iters)
+            t_ref = _time(ref, iters)
+            print(
+                json.dumps(
+                    {
+                        "kernel": "gemm_bf16_sm100",
+                        "case": f"{name}.{kind}",
+                        "M": M,
+                        "N": N,
+                        "K": K,
+                        "ms": round(t_ours, 4),
+                        "tflops": round(flops / t_ours / 1e9, 1),
+                        "cublas_ms": round(t_ref, 4),
+                        "cublas_tflops": round(flops / t_ref / 1e9, 1),
+                    }
+                ),
+                flush=True,
+            )
+        del x, w, dy
+        torch.cuda.empty_cache()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm"])
+    ap.add_argument("--shape", default=None, help="M,N,K")
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    if args.what == "gemm":
+        shapes = QWEN3_8B_SHAPES
+        if args.shape:
+            M, N, K = (int(v) for v in args.shape.split(","))
+            shapes = {"custom": (M, N, K)}
+        bench_gemm(shapes, args.iters)
+
+
+if __name__ == "__main__":
+    main()
