@@ -1,0 +1,813 @@
+// Varlen (packed-document) flash attention for sm_100a on tcgen05.
+//
+// Layout: tokens of all documents are packed into one stream of T rows;
+// cu_seqlens[d] .. cu_seqlens[d+1] delimit document d.  Row i attends to keys
+// j with start(i) <= j <= i (causal) or start(i) <= j < end(i) (bidirectional,
+// used by the vision tower).  No mask tensor is ever built.
+//
+// q: [T, Hq, 128], k: [T, Hkv, 128], v: [T, Hkv, 128] (any row strides that
+// are multiples of 8 elements), o: [T, Hq, 128] bf16, lse: [Hq, T] fp32
+// (natural-log LSE of the scaled logits, for the backward pass).
+//
+// Forward CTA = one 128-row query block of one head (grid = q blocks x Hq):
+//   warps 0-3  softmax: each thread owns one query row = one TMEM lane; it
+//              reads S from TMEM, applies the document mask, keeps a running
+//              max / sum, rescales O in TMEM only when the max grows by more
+//              than 2^8 (lazy rescale), and writes P (bf16) into a 128-byte
+//              swizzled shared-memory tile that feeds the next MMA.
+//   warp 4     TMA producer: Q once, then K/V blocks into a 2-deep ring.
+//   warp 5     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before waiting for
+//              P_j so the tensor core overlaps the softmax; then O += P_j V_j.
+// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace mvp {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int BLK = 128;               // query rows and keys per block
+constexpr int TILE_BYTES = BLK * D * 2;  // 32 KB: [128 rows][128 d] as two 64-wide swizzled chunks
+constexpr int CHUNK_BYTES = BLK * 64 * 2;  // 16 KB
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdParams {
+  __nv_bfloat16* o;
+  int64_t o_row_stride;
+  float* lse;
+  const int* cu_seqlens;
+  int n_docs;
+  int T, Hq, Hkv;
+  float scale_log2;
+  int causal;
+  int* status;
+};
+
+__device__ __forceinline__ void doc_bounds(const int* cu, int n_docs, int i, int& start, int& end) {
+  // largest d with cu[d] <= i
+  int lo = 0, hi = n_docs;  // cu has n_docs + 1 entries
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(cu + mid) <= i) lo = mid;
+    else hi = mid;
+  }
+  start = __ldg(cu + lo);
+  end = __ldg(cu + lo + 1);
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// K-major operand descriptor for a [128 rows][128 k] tile stored as two 64-wide
+// 128-byte-swizzled chunks; k-step s covers k = 16s .. 16s+15.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int s) {
+  return make_smem_desc_sw128(base + (s >> 2) * CHUNK_BYTES + (s & 3) * 32, 16, 1024);
+}
+// MN-major operand descriptor for V ([keys][128 d], d contiguous) used as B with
+// N = d and K = keys; k-step s covers keys 16s .. 16s+15.
+__device__ __forceinline__ uint64_t vmajor_desc(uint32_t base, int s) {
+  return make_smem_desc_sw128(base + s * 2048, CHUNK_BYTES, 1024);
+}
+
+__global__ void __launch_bounds__(192, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + TILE_BYTES;       // [2]
+  uint8_t* sV = sK + 2 * TILE_BYTES;   // [2]
+  uint8_t* sP = sV + 2 * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2]
+  uint64_t* s_empty = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_ready = bars + 12;
+  uint64_t* done_bar = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int qb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qb * BLK;
+
+  // KV range of this query block.
+  int first_start, first_end;
+  doc_bounds(p.cu_seqlens, p.n_docs, q0, first_start, first_end);
+  const int q_last = min(q0 + BLK, p.T) - 1;
+  int last_start, last_end;
+  doc_bounds(p.cu_seqlens, p.n_docs, q_last, last_start, last_end);
+  const int kv_lo = first_start;
+  const int kv_hi = p.causal ? (q_last + 1) : last_end;
+  const int n_blocks = (kv_hi - kv_lo + BLK - 1) / BLK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&k_full[b], 1);
+      mbar_init(&v_full[b], 1);
+      mbar_init(&kv_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_ready, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;         // [2] x 128 columns
+  const uint32_t tO = tmem + 256;   // 128 columns
+
+  if (warp == 4) {
+    // --------------------------------------------------------------- TMA
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(sQ, &tmQ, q_full, h * D, q0);
+      tma_load_2d(sQ + CHUNK_BYTES, &tmQ, q_full, h * D + 64, q0);
+      uint32_t issued = 0;  // bit b: a load into slot b has been issued
+      uint32_t issued_phase = 0;
+      bool ok = true;
+      for (int j = 0; j < n_blocks; ++j) {
+        const int b = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(&kv_empty[b], ph ^ 1, abort_flag, p.status, kTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const int k0 = kv_lo + j * BLK;
+        mbar_arrive_expect_tx(&k_full[b], TILE_BYTES);
+        tma_load_2d(sK + b * TILE_BYTES, &tmK, &k_full[b], hk * D, k0);
+        tma_load_2d(sK + b * TILE_BYTES + CHUNK_BYTES, &tmK, &k_full[b], hk * D + 64, k0);
+        mbar_arrive_expect_tx(&v_full[b], TILE_BYTES);
+        tma_load_2d(sV + b * TILE_BYTES, &tmV, &v_full[b], hk * D, k0);
+        tma_load_2d(sV + b * TILE_BYTES + CHUNK_BYTES, &tmV, &v_full[b], hk * D + 64, k0);
+        issued |= 1u << b;
+        issued_phase = (issued_phase & ~(1u << b)) | (ph << b);
+      }
+      if (!ok || *abort_flag) {
+        // Let in-flight copies land before the CTA can exit.
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < 200000000ull) {
+        }
+        for (int b = 0; b < 2; ++b) {
+          if (!((issued >> b) & 1u)) continue;
+          const uint32_t par = (issued_phase >> b) & 1u;
+          const uint64_t t1 = globaltimer();
+          while ((!mbar_try_wait(&k_full[b], par) || !mbar_try_wait(&v_full[b], par)) &&
+                 globaltimer() - t1 < 200000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // --------------------------------------------------------------- MMA
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BLK, BLK, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BLK, D, false, true);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t p_base = smem_u32(sP);
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kTimeoutMma);
+      auto issue_s = [&](int j) -> bool {
+        const int b = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(&k_full[b], ph, abort_flag, p.status, kTimeoutMma)) return false;
+        if (!mbar_wait_bounded(&s_empty[b], ph ^ 1, abort_flag, p.status, kTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sK + b * TILE_BYTES);
+#pragma unroll
+        for (int s = 0; s < D / 16; ++s)
+          mma_bf16_ss(tS + b * BLK, kmajor_desc(q_base, s), kmajor_desc(k_base, s), idesc_s, s > 0 ? 1u : 0u);
+        mma_commit(&s_full[b]);
+        return true;
+      };
+      if (ok && n_blocks > 0) ok = issue_s(0);
+      for (int j = 0; j < n_blocks && ok; ++j) {
+        if (j + 1 < n_blocks && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        const int b = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(p_full, j & 1, abort_flag, p.status, kTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_bounded(&v_full[b], ph, abort_flag, p.status, kTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(sV + b * TILE_BYTES);
+#pragma unroll
+        for (int s = 0; s < BLK / 16; ++s)
+          mma_bf16_ss(tO, kmajor_desc(p_base, s), vmajor_desc(v_base, s), idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+        mma_commit(o_ready);
+        mma_commit(&kv_empty[b]);
+      }
+      // Retire everything issued before TMEM is released.
+      mma_commit(done_bar);
+      mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
+    }
+  } else {
+    // ----------------------------------------------------------- softmax
+    const int r = warp * 32 + lane;
+    const int i = q0 + r;
+    const bool valid = i < p.T;
+    int start_i = 0, end_i = 0;
+    if (valid) doc_bounds(p.cu_seqlens, p.n_docs, i, start_i, end_i);
+    const int hi_i = p.causal ? i : end_i - 1;  // last allowed key (inclusive)
+    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_blocks; ++j) {
+      const int b = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[b], ph, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      float s[BLK];
+#pragma unroll
+      for (int c = 0; c < BLK / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld_32x32b_x32(tS + b * BLK + lane_addr + c * 32, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(rr[t]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[b]);
+      const int k0 = kv_lo + j * BLK;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BLK; ++c) {
+        const int key = k0 + c;
+        const bool allowed = valid && key >= start_i && key <= hi_i;
+        s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
+        mb = fmaxf(mb, s[c]);
+      }
+      const float m_new = fmaxf(m, mb);
+      float m_use = m, alpha = 1.f;
+      if (m_new > m + kRescaleThreshold || (m == -INFINITY && m_new != -INFINITY)) {
+        m_use = m_new;
+        alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+      }
+      // O and the P tile are free once PV_{j-1} has retired.
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_bounded(o_ready, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t rr[16];
+            tmem_ld_32x32b_x16(tO + lane_addr + c * 16, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) rr[t] = __float_as_uint(__uint_as_float(rr[t]) * alpha);
+            tmem_st_32x32b_x16(tO + lane_addr + c * 16, rr);
+          }
+          tmem_wait_st();
+        }
+      }
+      m = m_use;
+      float rowsum = 0.f;
+      // P = exp2(s - m) as bf16 into the swizzled K-major tile: row r, key chunk c.
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint8_t* row_base = sP + c * CHUNK_BYTES + r * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float e[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float x = s[c * 64 + u * 8 + t];
+            e[t] = (m == -INFINITY || x == -INFINITY) ? 0.f : exp2f(x - m);
+            rowsum += e[t];
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(e[0], e[1]);
+          pk.y = pack_bf16x2(e[2], e[3]);
+          pk.z = pack_bf16x2(e[4], e[5]);
+          pk.w = pack_bf16x2(e[6], e[7]);
+          *reinterpret_cast<uint4*>(row_base + ((u ^ (r & 7)) << 4)) = pk;
+        }
+      }
+      l = l * alpha + rowsum;
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && n_blocks > 0) {
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait_bounded(o_ready, (n_blocks - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(i) * p.o_row_stride + h * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rr[32];
+        if (n_blocks > 0) {
+          tmem_ld_32x32b_x32(tO + lane_addr + c * 32, rr);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) rr[t] = 0u;
+        }
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+            pk.y = pack_bf16x2(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+            pk.z = pack_bf16x2(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+            pk.w = pack_bf16x2(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = pk;
+          }
+        }
+      }
+      if (valid) p.lse[static_cast<int64_t>(h) * p.T + i] = (l > 0.f) ? (m + log2f(l)) / kLog2e : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 256;
+
+}  // namespace attn
+}  // namespace mvp
+
+// q [T, Hq, 128], k/v [T, Hkv, 128] (row strides multiple of 8, unit head/dim
+// strides), cu_seqlens int32 [n+1] on device.  Returns (o [T, Hq, 128], lse [Hq, T]).
+std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                                          const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
+                                          int64_t status_ptr) {
+  using namespace mvp::attn;
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+              "flash_attn_fwd: bf16 inputs");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3 && q.size(2) == D && k.size(2) == D && v.size(2) == D,
+              "flash_attn_fwd: [T, H, 128] inputs");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1 && q.stride(1) == D && k.stride(1) == D &&
+                  v.stride(1) == D,
+              "flash_attn_fwd: heads must be contiguous within a token");
+  TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_cuda(), "flash_attn_fwd: int32 cu_seqlens");
+  const int T = static_cast<int>(q.size(0));
+  const int Hq = static_cast<int>(q.size(1));
+  const int Hkv = static_cast<int>(k.size(1));
+  TORCH_CHECK(Hq % Hkv == 0, "flash_attn_fwd: Hq must be a multiple of Hkv");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto o = torch::empty({T, Hq, D}, q.options());
+  auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
+  if (T == 0) return {o, lse};
+  CUtensorMap tq, tk, tv;
+  mvp::make_tmap_2d_bf16(&tq, q.data_ptr(), static_cast<int64_t>(Hq) * D, T, q.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, T, k.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, T, v.stride(0), 64, BLK);
+  FwdParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.o_row_stride = o.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.n_docs = static_cast<int>(cu_seqlens.numel() - 1);
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
+  p.causal = causal ? 1 : 0;
+  p.status = reinterpret_cast<int*>(status_ptr);
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
+    configured = true;
+  }
+  dim3 grid((T + BLK - 1) / BLK, Hq);
+  fwd_kernel<<<grid, 192, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+// ============================================================== backward
+//
+// CTA = one 128-key block of one KV head (grid = kv blocks x Hkv).  It loops
+// over the Hq/Hkv query heads of its group and over every 128-row query block
+// that can see its keys, keeping dK and dV in TMEM for the whole loop:
+//   S^T  = K Q^T          (TMEM, lane = key)       dP^T = V dO^T (TMEM)
+//   P^T  = exp(S^T*scale - lse),  dS^T = P^T * (dP^T - delta) * scale
+//   dV  += P^T dO,  dK += dS^T Q   (TMEM accumulators)
+//   dQ   = dS K  -> TMEM (lane = query row) -> fp32 vector atomics into dq_acc
+// P^T and dS^T are written once into 128-byte-swizzled smem tiles; the dS^T
+// tile serves both as the K-major A operand of dK and, read MN-major, as the
+// A operand of dQ.  Q/dO tiles serve as K-major B (S^T, dP^T) and as MN-major
+// B (dK, dV).  TMEM: S^T | dP^T | dV | dK (4 x 128 columns); dQ reuses S^T.
+namespace mvp {
+namespace attn {
+
+struct BwdParams {
+  float* dq_acc;  // [T, Hq, 128] fp32, zero-initialised
+  __nv_bfloat16* dk;
+  int64_t dk_row_stride;
+  __nv_bfloat16* dv;
+  int64_t dv_row_stride;
+  const float* lse;    // [Hq, T]
+  const float* delta;  // [Hq, T]
+  const int* cu_seqlens;
+  int n_docs;
+  int T, Hq, Hkv;
+  float scale, scale_log2;
+  int causal;
+  int* status;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;
+  uint8_t* sdO = sQ + TILE_BYTES;
+  uint8_t* sPt = sdO + TILE_BYTES;
+  uint8_t* sdSt = sPt + TILE_BYTES;
+  float* s_lse = reinterpret_cast<float*>(sdSt + TILE_BYTES);  // [2][128]
+  float* s_delta = s_lse + 2 * BLK;                             // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 2 * BLK);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* mma2_done = bars + 5;
+  uint64_t* dq_read = bars + 6;
+  uint64_t* done_bar = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int hk = blockIdx.y;
+  const int rep = p.Hq / p.Hkv;
+  const int k0 = blockIdx.x * BLK;
+  const int k_last = min(k0 + BLK, p.T) - 1;
+  int ks0, ke0, ksl, kel;
+  doc_bounds(p.cu_seqlens, p.n_docs, k0, ks0, ke0);
+  doc_bounds(p.cu_seqlens, p.n_docs, k_last, ksl, kel);
+  const int q_lo = p.causal ? k0 : ks0;
+  const int q_hi = kel;
+  const int nq = (q_hi - q_lo + BLK - 1) / BLK;
+  const int n_iter = nq * rep;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qd_full, 1);
+    mbar_init(qd_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(mma2_done, 1);
+    mbar_init(dq_read, 128);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
+
+  if (warp == 4) {
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(sK, &tmK, kv_full, hk * D, k0);
+      tma_load_2d(sK + CHUNK_BYTES, &tmK, kv_full, hk * D + 64, k0);
+      tma_load_2d(sV, &tmV, kv_full, hk * D, k0);
+      tma_load_2d(sV + CHUNK_BYTES, &tmV, kv_full, hk * D + 64, k0);
+      int issued = 0;
+      for (int n = 0; n < n_iter; ++n) {
+        if (!mbar_wait_bounded(qd_empty, (n & 1) ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
+        const int h = hk * rep + n / nq;
+        const int q0 = q_lo + (n % nq) * BLK;
+        mbar_arrive_expect_tx(qd_full, 2 * TILE_BYTES);
+        tma_load_2d(sQ, &tmQ, qd_full, h * D, q0);
+        tma_load_2d(sQ + CHUNK_BYTES, &tmQ, qd_full, h * D + 64, q0);
+        tma_load_2d(sdO, &tmdO, qd_full, h * D, q0);
+        tma_load_2d(sdO + CHUNK_BYTES, &tmdO, qd_full, h * D + 64, q0);
+        issued = n + 1;
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(kv_full, 0) && globaltimer() - t0 < 200000000ull) {
+        }
+        if (issued > 0) {
+          const uint64_t t1 = globaltimer();
+          while (!mbar_try_wait(qd_full, (issued - 1) & 1) && globaltimer() - t1 < 200000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (elect_one_sync()) {
+      constexpr uint32_t id_kk = make_idesc_bf16(BLK, BLK, false, false);
+      constexpr uint32_t id_km = make_idesc_bf16(BLK, D, false, true);
+      constexpr uint32_t id_mm = make_idesc_bf16(BLK, D, true, true);
+      const uint32_t bK = smem_u32(sK), bV = smem_u32(sV), bQ = smem_u32(sQ), bdO = smem_u32(sdO);
+      const uint32_t bPt = smem_u32(sPt), bdSt = smem_u32(sdSt);
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, p.status, kTimeoutMma);
+      for (int n = 0; n < n_iter && ok; ++n) {
+        ok = mbar_wait_bounded(qd_full, n & 1, abort_flag, p.status, kTimeoutMma) &&
+             mbar_wait_bounded(dq_read, (n & 1) ^ 1, abort_flag, p.status, kTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < D / 16; ++s) mma_bf16_ss(tS, kmajor_desc(bK, s), kmajor_desc(bQ, s), id_kk, s > 0);
+#pragma unroll
+        for (int s = 0; s < D / 16; ++s) mma_bf16_ss(tdP, kmajor_desc(bV, s), kmajor_desc(bdO, s), id_kk, s > 0);
+        mma_commit(s_full);
+        ok = mbar_wait_bounded(p_full, n & 1, abort_flag, p.status, kTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < BLK / 16; ++s)
+          mma_bf16_ss(tdV, kmajor_desc(bPt, s), vmajor_desc(bdO, s), id_km, (n > 0 || s > 0) ? 1u : 0u);
+#pragma unroll
+        for (int s = 0; s < BLK / 16; ++s)
+          mma_bf16_ss(tdK, kmajor_desc(bdSt, s), vmajor_desc(bQ, s), id_km, (n > 0 || s > 0) ? 1u : 0u);
+#pragma unroll
+        for (int s = 0; s < BLK / 16; ++s) mma_bf16_ss(tS, vmajor_desc(bdSt, s), vmajor_desc(bK, s), id_mm, s > 0);
+        mma_commit(mma2_done);
+        mma_commit(qd_empty);
+      }
+      mma_commit(done_bar);
+      mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
+    }
+  } else {
+    // warps 0-3: one key row (S^T/dP^T/dK/dV lane) and one query row (dQ lane) per thread
+    const int c = warp * 32 + lane;
+    const int kc = k0 + c;
+    const bool kvalid = kc < p.T;
+    int ks = 0, ke = 0;
+    if (kvalid) doc_bounds(p.cu_seqlens, p.n_docs, kc, ks, ke);
+    const int lo_c = p.causal ? kc : ks;
+    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    bool ok = true;
+    for (int n = 0; n < n_iter; ++n) {
+      const int h = hk * rep + n / nq;
+      const int q0 = q_lo + (n % nq) * BLK;
+      float* lse_b = s_lse + (n & 1) * BLK;
+      float* del_b = s_delta + (n & 1) * BLK;
+      {
+        const int qi = q0 + c;
+        const bool qv = qi < p.T;
+        lse_b[c] = qv ? p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e : INFINITY;
+        del_b[c] = qv ? p.delta[static_cast<int64_t>(h) * p.T + qi] : 0.f;
+      }
+      named_barrier_sync(1, 128);
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int ch = 0; ch < BLK / 32; ++ch) {
+        uint32_t sr[32], dr[32];
+        tmem_ld_32x32b_x32(tS + lane_addr + ch * 32, sr);
+        tmem_ld_32x32b_x32(tdP + lane_addr + ch * 32, dr);
+        tmem_wait_ld();
+        float pv[32], ds[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int r = ch * 32 + t;
+          const int qr = q0 + r;
+          const bool allowed = kvalid && qr >= lo_c && qr < ke && qr < p.T;
+          const float pe = allowed ? exp2f(__uint_as_float(sr[t]) * p.scale_log2 - lse_b[r]) : 0.f;
+          pv[t] = pe;
+          ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+        }
+        // 32 q columns = half of one 64-wide chunk = four 16-byte units.
+        const int chunk = ch >> 1;
+        const int u0 = (ch & 1) * 4;
+        uint8_t* prow = sPt + chunk * CHUNK_BYTES + c * 128;
+        uint8_t* drow = sdSt + chunk * CHUNK_BYTES + c * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 a, b;
+          a.x = pack_bf16x2(pv[8 * u + 0], pv[8 * u + 1]);
+          a.y = pack_bf16x2(pv[8 * u + 2], pv[8 * u + 3]);
+          a.z = pack_bf16x2(pv[8 * u + 4], pv[8 * u + 5]);
+          a.w = pack_bf16x2(pv[8 * u + 6], pv[8 * u + 7]);
+          b.x = pack_bf16x2(ds[8 * u + 0], ds[8 * u + 1]);
+          b.y = pack_bf16x2(ds[8 * u + 2], ds[8 * u + 3]);
+          b.z = pack_bf16x2(ds[8 * u + 4], ds[8 * u + 5]);
+          b.w = pack_bf16x2(ds[8 * u + 6], ds[8 * u + 7]);
+          const int off = ((u0 + u) ^ (c & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + off) = a;
+          *reinterpret_cast<uint4*>(drow + off) = b;
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(mma2_done, n & 1, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      // dQ rows: thread c now owns query row q0 + c.
+      const int qi = q0 + c;
+      float* dst = p.dq_acc + (static_cast<int64_t>(qi) * p.Hq + h) * D;
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {
+        uint32_t rr[32];
+        tmem_ld_32x32b_x32(tS + lane_addr + ch * 32, rr);
+        tmem_wait_ld();
+        if (qi < p.T) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            atomicAdd(reinterpret_cast<float4*>(dst + ch * 32) + v,
+                      make_float4(__uint_as_float(rr[4 * v]), __uint_as_float(rr[4 * v + 1]),
+                                  __uint_as_float(rr[4 * v + 2]), __uint_as_float(rr[4 * v + 3])));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_read);
+    }
+    if (ok && n_iter > 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tacc = which == 0 ? tdK : tdV;
+        __nv_bfloat16* out = which == 0 ? p.dk + static_cast<int64_t>(kc) * p.dk_row_stride + hk * D
+                                        : p.dv + static_cast<int64_t>(kc) * p.dv_row_stride + hk * D;
+#pragma unroll
+        for (int ch = 0; ch < D / 32; ++ch) {
+          uint32_t rr[32];
+          tmem_ld_32x32b_x32(tacc + lane_addr + ch * 32, rr);
+          tmem_wait_ld();
+          if (kvalid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(rr[8 * v + 0]), __uint_as_float(rr[8 * v + 1]));
+              pk.y = pack_bf16x2(__uint_as_float(rr[8 * v + 2]), __uint_as_float(rr[8 * v + 3]));
+              pk.z = pack_bf16x2(__uint_as_float(rr[8 * v + 4]), __uint_as_float(rr[8 * v + 5]));
+              pk.w = pack_bf16x2(__uint_as_float(rr[8 * v + 6]), __uint_as_float(rr[8 * v + 7]));
+              *reinterpret_cast<uint4*>(out + ch * 32 + v * 8) = pk;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[h, i] = sum_d dO[i, h, d] * O[i, h, d]; one warp per (i, h).
+__global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                 float* __restrict__ delta, int T, int Hq) {
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (item >= static_cast<int64_t>(T) * Hq) return;
+  const int i = static_cast<int>(item / Hq), h = static_cast<int>(item % Hq);
+  const int64_t off = item * D + lane * 4;
+  const uint2 a = *reinterpret_cast<const uint2*>(dout + off);
+  const uint2 b = *reinterpret_cast<const uint2*>(out + off);
+  const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  const float2 b0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.x));
+  const float2 b1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.y));
+  float s = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) delta[static_cast<int64_t>(h) * T + i] = s;
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
+  for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(x + i);
+    uint2 u;
+    u.x = pack_bf16x2(v.x, v.y);
+    u.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(y + i) = u;
+  }
+}
+
+constexpr int kBwdSmem = 6 * TILE_BYTES + 4 * BLK * 4 + 1024 + 256;
+
+}  // namespace attn
+}  // namespace mvp
+
+// Returns (dq [T, Hq, 128], dk, dv); dk/dv are written into the given buffers when
+// provided (e.g. the k/v column slices of a fused dqkv gradient).
+std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch::Tensor& q, const torch::Tensor& k,
+                                          const torch::Tensor& v, const torch::Tensor& out, const torch::Tensor& lse,
+                                          const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
+                                          int64_t status_ptr, const c10::optional<torch::Tensor>& dk_out,
+                                          const c10::optional<torch::Tensor>& dv_out) {
+  using namespace mvp::attn;
+  TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && q.is_contiguous(), "flash_attn_bwd: contiguous q/o/do");
+  TORCH_CHECK(k.stride(2) == 1 && v.stride(2) == 1 && k.stride(1) == D && v.stride(1) == D,
+              "flash_attn_bwd: k/v head layout");
+  const int T = static_cast<int>(q.size(0));
+  const int Hq = static_cast<int>(q.size(1));
+  const int Hkv = static_cast<int>(k.size(1));
+  const at::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto dq_acc = torch::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
+  auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
+  torch::Tensor dk = dk_out.has_value() ? *dk_out : torch::empty({T, Hkv, D}, q.options());
+  torch::Tensor dv = dv_out.has_value() ? *dv_out : torch::empty({T, Hkv, D}, q.options());
+  TORCH_CHECK(dk.stride(2) == 1 && dv.stride(2) == 1 && dk.stride(1) == D && dv.stride(1) == D,
+              "flash_attn_bwd: dk/dv head layout");
+  auto dq = torch::empty({T, Hq, D}, q.options());
+  if (T == 0) return {dq, dk, dv};
+  {
+    const int64_t items = static_cast<int64_t>(T) * Hq;
+    bwd_delta_kernel<<<static_cast<int>((items + 7) / 8), 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+        delta.data_ptr<float>(), T, Hq);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  CUtensorMap tq, tk, tv, tdo;
+  mvp::make_tmap_2d_bf16(&tq, q.data_ptr(), static_cast<int64_t>(Hq) * D, T, q.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, T, k.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, T, v.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tdo, dout.data_ptr(), static_cast<int64_t>(Hq) * D, T, dout.stride(0), 64, BLK);
+  BwdParams p;
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dk_row_stride = dk.stride(0);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.dv_row_stride = dv.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.n_docs = static_cast<int>(cu_seqlens.numel() - 1);
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = static_cast<float>(softmax_scale);
+  p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
+  p.causal = causal ? 1 : 0;
+  p.status = reinterpret_cast<int*>(status_ptr);
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
+    configured = true;
+  }
+  dim3 grid((T + BLK - 1) / BLK, Hkv);
+  bwd_kernel<<<grid, 192, kBwdSmem, stream>>>(tq, tk, tv, tdo, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t n = static_cast<int64_t>(T) * Hq * D;
+  f32_to_bf16_kernel<<<static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 16)), 256, 0, stream>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dq, dk, dv};
+}

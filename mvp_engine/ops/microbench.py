@@ -87,9 +87,57 @@ def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
         torch.cuda.empty_cache()
 
 
+def _doc_lens(total: int, lo: int, hi: int, seed: int = 0) -> list[int]:
+    g = torch.Generator().manual_seed(seed)
+    lens, used = [], 0
+    while used < total:
+        n = int(torch.randint(lo, hi + 1, (1,), generator=g))
+        n = min(n, total - used)
+        lens.append(n)
+        used += n
+    return lens
+
+
+def bench_attention(T: int, Hq: int, Hkv: int, iters: int, lo: int = 256, hi: int = 4096) -> None:
+    from mvp_engine.ops import _ext
+
+    lens = _doc_lens(T, lo, hi)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    q = torch.randn(T, Hq, 128, device="cuda").bfloat16()
+    k = torch.randn(T, Hkv, 128, device="cuda").bfloat16()
+    v = torch.randn(T, Hkv, 128, device="cuda").bfloat16()
+    do = torch.randn(T, Hq, 128, device="cuda").bfloat16()
+    pairs = sum(n * (n + 1) // 2 for n in lens)
+    fwd_flops = 4.0 * pairs * 128 * Hq
+    ext = _ext.ext()
+    st = _ext.status_buffer().data_ptr()
+    scale = 128**-0.5
+    o, lse = ext.flash_attn_fwd(q, k, v, cu, scale, True, st)
+    t_f = _time(lambda: ext.flash_attn_fwd(q, k, v, cu, scale, True, st), iters)
+    t_b = _time(lambda: ext.flash_attn_bwd(do, q, k, v, o, lse, cu, scale, True, st), iters)
+    row = {"kernel": "flash_attn_varlen_sm100", "T": T, "Hq": Hq, "Hkv": Hkv, "docs": len(lens),
+           "fwd_ms": round(t_f, 4), "fwd_tflops": round(fwd_flops / t_f / 1e9, 1),
+           "bwd_ms": round(t_b, 4), "bwd_tflops": round(2.5 * fwd_flops / t_b / 1e9, 1)}
+    try:  # comparison column: the FlashAttention-2 library the reference trains with
+        from flash_attn import flash_attn_varlen_func
+
+        mx = max(lens)
+        qq, kk, vv = (t.clone().requires_grad_() for t in (q, k, v))
+        t_rf = _time(lambda: flash_attn_varlen_func(q, k, v, cu, cu, mx, mx, causal=True), iters)
+        out = flash_attn_varlen_func(qq, kk, vv, cu, cu, mx, mx, causal=True)
+        t_rb = _time(lambda: torch.autograd.grad(out, (qq, kk, vv), do, retain_graph=True), iters)
+        row.update({"fa2_fwd_ms": round(t_rf, 4), "fa2_fwd_tflops": round(fwd_flops / t_rf / 1e9, 1),
+                    "fa2_bwd_ms": round(t_rb, 4), "fa2_bwd_tflops": round(2.5 * fwd_flops / t_rb / 1e9, 1)})
+    except Exception as exc:  # pragma: no cover - library availability
+        row["fa2"] = f"unavailable: {type(exc).__name__}: {exc}"[:200]
+    print(json.dumps(row), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm"])
+    ap.add_argument("what", choices=["gemm", "attention"])
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--heads", default="32,8")
     ap.add_argument("--shape", default=None, help="M,N,K")
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args()
@@ -99,6 +147,9 @@ def main() -> None:
             M, N, K = (int(v) for v in args.shape.split(","))
             shapes = {"custom": (M, N, K)}
         bench_gemm(shapes, args.iters)
+    elif args.what == "attention":
+        hq, hkv = (int(v) for v in args.heads.split(","))
+        bench_attention(args.tokens, hq, hkv, args.iters)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,524 @@
+"""Native flat-buffer fully-sharded data parallelism.
+
+This is the engine's B200 data-parallel runtime; torch FSDP2 stays available
+as the reference-equivalent backend (``parallel.backend_kwargs.impl=torch``,
+reference: mvp_engine/distributed/fsdp2.py:50-176).
+
+Layout.  Parameters are grouped into *units*: one per ``_no_split_modules``
+block (a decoder layer) plus a root unit with everything else.  A unit owns
+
+* ``full``   the unsharded compute weights, one contiguous buffer in
+             ``param_dtype`` (bf16); every parameter becomes a view into it,
+             so q/k/v (and gate/up) are adjacent and usable as one fused GEMM
+             operand;
+* ``grad``   an fp32 buffer of the same layout where weight gradients
+             accumulate across micro-batches (the GEMM epilogue adds into it
+             directly, see ``mvp_engine.ops``);
+* ``master``, ``exp_avg``, ``exp_avg_sq``, ``grad_shard``: this rank's
+             contiguous 1/W slice, fp32.
+
+Because shards are contiguous slices of the full layout, the parameter
+all-gather is an in-place ``all_gather_into_tensor`` into ``full`` and the
+gradient reduce-scatter reads ``grad`` as is: no copy-in / copy-out kernels.
+The optimizer writes its bf16 output straight into this rank's slice of
+``full``.  Full weights stay resident between steps (``reshard_after_forward``
+is not needed at the memory budget of a 180 GB B200), so each parameter crosses
+NVLink once per optimizer step, not twice per micro-batch.
+
+Overlap.  Gradient reduce-scatter of a unit starts on a side stream as soon as
+that unit's backward finishes (a hook on the unit's inputs), only on the
+micro-batch that syncs.  Parameter all-gathers of the next step are issued per
+unit in forward order right after the optimizer step; each unit's forward
+waits only for its own gather.
+
+Checkpoints.  ``checkpoint_state_dict`` returns HF-named tensors; on more than
+one rank they are DTensors with ``Shard(0)`` placements over the shard mesh,
+exactly the layout torch FSDP2 checkpoints with, rebuilt transiently from the
+flat shards (one unit at a time, offloaded to CPU).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Any, Callable, Iterable, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..utils.log import logger
+
+_ALIGN = 64  # elements; keeps every parameter view 128-byte aligned for TMA
+
+
+@dataclass
+class _Entry:
+    fqns: list[str]  # all names that alias this parameter (tied weights)
+    owners: list[tuple[nn.Module, str]]
+    shape: torch.Size
+    numel: int
+    offset: int  # in the unit's full layout
+    requires_grad: bool
+
+
+@dataclass
+class FlatUnit:
+    index: int
+    name: str
+    module: Optional[nn.Module]
+    entries: list[_Entry] = field(default_factory=list)
+    total: int = 0
+    padded: int = 0
+    shard: int = 0
+    trainable: bool = True
+    full: Optional[torch.Tensor] = None
+    grad: Optional[torch.Tensor] = None
+    master: Optional[torch.Tensor] = None
+    grad_shard: Optional[torch.Tensor] = None
+    exp_avg: Optional[torch.Tensor] = None
+    exp_avg_sq: Optional[torch.Tensor] = None
+    ag_event: Optional[torch.cuda.Event] = None
+    rs_event: Optional[torch.cuda.Event] = None
+    rs_pending: bool = False
+    views: dict[str, torch.Tensor] = field(default_factory=dict)
+
+    def local_range(self, rank: int) -> tuple[int, int]:
+        return rank * self.shard, (rank + 1) * self.shard
+
+
+class _UnitBackwardHook(torch.autograd.Function):
+    """Identity on the unit's inputs; its backward runs after every op of the unit."""
+
+    @staticmethod
+    def forward(ctx, owner, unit_index, *xs):
+        ctx.owner = owner
+        ctx.unit_index = unit_index
+        return xs if len(xs) > 1 else xs[0]
+
+    @staticmethod
+    def backward(ctx, *grads):
+        ctx.owner._on_unit_backward_done(ctx.unit_index)
+        return (None, None) + grads
+
+
+def _dtype(d: Any) -> torch.dtype:
+    if isinstance(d, torch.dtype):
+        return d
+    return {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32, "bf16": torch.bfloat16,
+            "fp32": torch.float32}[str(d)]
+
+
+class NativeFSDP(nn.Module):
+    """Wrap ``model`` with flat-buffer sharded data parallelism over ``group``.
+
+    Args:
+        model: the module (parameters may be fp32 masters; they are copied).
+        group: data-parallel process group (None -> single rank).
+        device: compute device.
+        param_dtype: dtype of compute weights (bf16 under mixed precision).
+        unit_classes: class names that form their own unit (default: the
+            model's ``_no_split_modules``).
+        comm: ``"nccl"`` (torch.distributed collectives) or ``"fused"`` (the
+            engine's own NVLink kernels where available).
+    """
+
+    def __init__(self, model: nn.Module, group: Optional[dist.ProcessGroup] = None,
+                 device: Optional[torch.device] = None, param_dtype: Any = torch.bfloat16,
+                 unit_classes: Optional[Iterable[str]] = None, comm: str = "nccl",
+                 shard_mesh: Any = None) -> None:
+        super().__init__()
+        self.module = model
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
+        self.rank = dist.get_rank(group) if (group is not None and dist.is_initialized()) else 0
+        self.device = torch.device(device) if device is not None else next(model.parameters()).device
+        self.param_dtype = _dtype(param_dtype)
+        self.comm = comm
+        self.shard_mesh = shard_mesh
+        self._sync_grads = True
+        self._grad_scale = 1.0
+        self._norm_sq: Optional[torch.Tensor] = None
+        self._max_norm: Optional[float] = None
+        cls_names = set(unit_classes) if unit_classes else set(getattr(model, "_no_split_modules", []) or [])
+        self.units: list[FlatUnit] = []
+        self._comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        self._build_units(cls_names)
+        self._install_hooks()
+        self._gather_all(initial=True)
+
+    # ----------------------------------------------------------- layout
+    def _build_units(self, cls_names: set[str]) -> None:
+        model = self.module
+        unit_of_module: dict[int, int] = {}
+        ordered: list[tuple[str, nn.Module]] = []
+        for name, mod in model.named_modules():
+            if type(mod).__name__ in cls_names and not any(name.startswith(p + ".") for p, _ in ordered):
+                ordered.append((name, mod))
+        # The root unit (index 0) gathers first: embeddings run before any block.
+        self.units.append(FlatUnit(0, "<root>", None))
+        for i, (name, mod) in enumerate(ordered):
+            self.units.append(FlatUnit(i + 1, name, mod))
+            unit_of_module[id(mod)] = i + 1
+
+        def owning_unit(fqn: str) -> int:
+            best, best_len = 0, -1
+            for u in self.units[1:]:
+                if (fqn == u.name or fqn.startswith(u.name + ".")) and len(u.name) > best_len:
+                    best, best_len = u.index, len(u.name)
+            return best
+
+        seen: dict[int, _Entry] = {}
+        for mod_name, mod in model.named_modules():
+            for pname, p in list(mod._parameters.items()):
+                if p is None:
+                    continue
+                fqn = f"{mod_name}.{pname}" if mod_name else pname
+                if id(p) in seen:
+                    seen[id(p)].fqns.append(fqn)
+                    seen[id(p)].owners.append((mod, pname))
+                    continue
+                unit = self.units[owning_unit(fqn)]
+                e = _Entry([fqn], [(mod, pname)], p.shape, p.numel(), 0, p.requires_grad)
+                seen[id(p)] = e
+                unit.entries.append(e)
+        # Frozen parameters of a unit move to a sibling unit without optimizer state.
+        extra: list[FlatUnit] = []
+        for u in self.units:
+            frozen = [e for e in u.entries if not e.requires_grad]
+            if frozen and len(frozen) < len(u.entries):
+                u.entries = [e for e in u.entries if e.requires_grad]
+                extra.append(FlatUnit(-1, u.name + "<frozen>", u.module, frozen, trainable=False))
+            elif frozen:
+                u.trainable = False
+        for x in extra:
+            x.index = len(self.units)
+            self.units.append(x)
+        params = {id(p): p for p in model.parameters()}
+        by_entry = {id(e): params_id for params_id, e in seen.items()}
+        for u in self.units:
+            off = 0
+            for e in u.entries:
+                e.offset = off
+                off += int(math.ceil(e.numel / _ALIGN) * _ALIGN)
+            u.total = off
+            quantum = _ALIGN * self.world
+            u.padded = max(quantum, int(math.ceil(off / quantum) * quantum))
+            u.shard = u.padded // self.world
+            self._materialise(u, {id(e): params[by_entry[id(e)]] for e in u.entries})
+
+    def _materialise(self, u: FlatUnit, src: dict[int, torch.Tensor]) -> None:
+        dev = self.device
+        u.full = torch.zeros(u.padded, dtype=self.param_dtype, device=dev)
+        lo, hi = u.local_range(self.rank)
+        if u.trainable:
+            u.master = torch.zeros(u.shard, dtype=torch.float32, device=dev)
+        with torch.no_grad():
+            for e in u.entries:
+                p = src[id(e)]
+                flat = p.detach().reshape(-1)
+                u.full[e.offset:e.offset + e.numel].copy_(flat)
+                if u.trainable:
+                    a, b = max(lo, e.offset), min(hi, e.offset + e.numel)
+                    if a < b:
+                        u.master[a - lo:b - lo].copy_(flat[a - e.offset:b - e.offset].float())
+        if u.trainable:
+            u.grad = torch.zeros(u.padded, dtype=torch.float32, device=dev)
+            u.grad_shard = u.grad if self.world == 1 else torch.zeros(u.shard, dtype=torch.float32, device=dev)
+            u.exp_avg = torch.zeros_like(u.master)
+            u.exp_avg_sq = torch.zeros_like(u.master)
+        native_grads = dev.type == "cuda"
+        for e in u.entries:
+            view = u.full[e.offset:e.offset + e.numel].view(e.shape)
+            if u.trainable:
+                gview = u.grad[e.offset:e.offset + e.numel].view(e.shape)
+                view._mvp_grad_acc = gview
+                if not native_grads:
+                    # CPU / eager ops: autograd accumulates into .grad; fold it into the flat buffer.
+                    view.requires_grad_(True)
+                    view.register_post_accumulate_grad_hook(_make_fold_hook(gview))
+            for mod, pname in e.owners:
+                del mod._parameters[pname]
+                setattr(mod, pname, view)
+            u.views[e.fqns[0]] = view
+        if u.module is not None:
+            self._publish_fused(u)
+
+    def _publish_fused(self, u: FlatUnit) -> None:
+        """Expose contiguous q/k/v and gate/up as single GEMM operands when laid out back to back."""
+        mod = u.module
+        if not hasattr(mod, "_fused"):
+            return
+        fused: dict[str, torch.Tensor] = {}
+        for key, names in (("qkv", ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight")),
+                           ("gate_up", ("mlp.gate_proj.weight", "mlp.up_proj.weight"))):
+            full_names = [f"{u.name}.{n}" for n in names]
+            ents = [next((e for e in u.entries if e.fqns[0] == fn), None) for fn in full_names]
+            if any(e is None for e in ents):
+                continue
+            contiguous = all(ents[i].offset + ents[i].numel == ents[i + 1].offset for i in range(len(ents) - 1))
+            if not contiguous or len({e.shape[1] for e in ents}) != 1:
+                continue
+            rows = sum(e.shape[0] for e in ents)
+            view = u.full[ents[0].offset:ents[0].offset + rows * ents[0].shape[1]].view(rows, ents[0].shape[1])
+            if u.trainable:
+                view._mvp_grad_acc = u.grad[ents[0].offset:ents[0].offset + view.numel()].view(view.shape)
+            fused[key] = view
+        mod._fused = fused or None
+
+    # ------------------------------------------------------------ hooks
+    def _install_hooks(self) -> None:
+        for u in self.units[1:]:
+            if u.module is None or "<frozen>" in u.name:
+                continue
+            u.module.register_forward_pre_hook(self._make_pre_hook(u.index), with_kwargs=False)
+
+    def _make_pre_hook(self, idx: int) -> Callable:
+        def hook(module, args):
+            self._wait_gather(idx)
+            for sib in self._siblings(idx):
+                self._wait_gather(sib)
+            if not torch.is_grad_enabled() or not self.module.training:
+                return None
+            tensors = [a for a in args if isinstance(a, torch.Tensor) and a.requires_grad]
+            if not tensors:
+                return None
+            hooked = _UnitBackwardHook.apply(self, idx, *tensors)
+            hooked = hooked if isinstance(hooked, tuple) else (hooked,)
+            it = iter(hooked)
+            return tuple(next(it) if (isinstance(a, torch.Tensor) and a.requires_grad) else a for a in args)
+
+        return hook
+
+    def _siblings(self, idx: int) -> list[int]:
+        name = self.units[idx].name
+        return [u.index for u in self.units if u.name == name + "<frozen>"]
+
+    def _on_unit_backward_done(self, idx: int) -> None:
+        if self._sync_grads:
+            self._reduce_scatter(idx)
+
+    # --------------------------------------------------- collectives
+    def _wait_gather(self, idx: int) -> None:
+        ev = self.units[idx].ag_event
+        if ev is not None and self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).wait_event(ev)
+            self.units[idx].ag_event = None
+
+    def _gather(self, u: FlatUnit) -> None:
+        if self.world == 1:
+            return
+        lo, hi = u.local_range(self.rank)
+        if self._comm_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self._comm_stream.wait_event(ev)
+            with torch.cuda.stream(self._comm_stream):
+                dist.all_gather_into_tensor(u.full, u.full[lo:hi], group=self.group)
+                u.ag_event = torch.cuda.Event()
+                u.ag_event.record(self._comm_stream)
+                u.full.record_stream(self._comm_stream)
+        else:
+            parts = list(u.full.chunk(self.world))
+            dist.all_gather(parts, u.full[lo:hi].clone(), group=self.group)
+
+    def _gather_all(self, initial: bool = False) -> None:
+        for u in self.units:
+            if initial and self.world > 1 and u.trainable:
+                # masters were copied from the full init; refresh this rank's slice
+                lo, hi = u.local_range(self.rank)
+                u.full[lo:hi].copy_(u.master)
+            self._gather(u)
+
+    def _reduce_scatter(self, idx: int) -> None:
+        u = self.units[idx]
+        if not u.trainable or u.rs_pending:
+            return
+        u.rs_pending = True
+        if self.world == 1:
+            return
+        if self._comm_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self._comm_stream.wait_event(ev)
+            with torch.cuda.stream(self._comm_stream):
+                dist.reduce_scatter_tensor(u.grad_shard, u.grad, op=dist.ReduceOp.SUM, group=self.group)
+                u.rs_event = torch.cuda.Event()
+                u.rs_event.record(self._comm_stream)
+        else:
+            buf = u.grad.clone()
+            dist.all_reduce(buf, group=self.group)
+            lo, hi = u.local_range(self.rank)
+            u.grad_shard.copy_(buf[lo:hi])
+
+    def finish_grad_sync(self) -> None:
+        """Reduce-scatter units whose hook did not fire (root, embeddings) and wait for all."""
+        for u in reversed(self.units):
+            if u.trainable and not u.rs_pending:
+                self._reduce_scatter(u.index)
+        cur = torch.cuda.current_stream(self.device) if self.device.type == "cuda" else None
+        for u in self.units:
+            if u.rs_event is not None and cur is not None:
+                cur.wait_event(u.rs_event)
+                u.rs_event = None
+
+    # --------------------------------------------------------- API
+    def set_requires_gradient_sync(self, requires_gradient_sync: bool, *, recurse: bool = True) -> None:
+        self._sync_grads = bool(requires_gradient_sync)
+
+    def forward(self, *args, **kwargs):
+        self._wait_gather(0)
+        for sib in self._siblings(0):
+            self._wait_gather(sib)
+        if self.module.training and torch.is_grad_enabled():
+            emb_anchor = getattr(self.module, "model", None)
+            if emb_anchor is not None and self.device.type == "cuda":
+                # gives the embedding backward a tensor that requires grad, so it runs
+                emb_anchor._embed_anchor = self._anchor
+        return self.module(*args, **kwargs)
+
+    @property
+    def _anchor(self) -> torch.Tensor:
+        a = getattr(self, "_anchor_t", None)
+        if a is None:
+            a = torch.zeros((), device=self.device, requires_grad=True)
+            self._anchor_t = a
+        return a
+
+    def grad_shards(self) -> list[torch.Tensor]:
+        return [u.grad_shard for u in self.units if u.trainable]
+
+    def scale_gradients_(self, factor: float) -> None:
+        """Fold a gradient multiplier (token normalisation) into the next optimizer update."""
+        self._grad_scale *= float(factor)
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0) -> torch.Tensor:
+        """Global norm of (scaled) gradients; the clip itself is folded into the optimizer update."""
+        if norm_type != 2.0:
+            raise NotImplementedError("native FSDP clips with the 2-norm")
+        self.finish_grad_sync()
+        from .. import ops
+
+        parts = [ops.sumsq(g) for g in self.grad_shards()]
+        nsq = torch.stack(parts).sum().reshape(1) if parts else torch.zeros(1, device=self.device)
+        if self.world > 1:
+            dist.all_reduce(nsq, group=self.group)
+        self._norm_sq = nsq
+        self._max_norm = float(max_norm)
+        return nsq.sqrt()[0] * self._grad_scale
+
+    def after_optimizer_step(self) -> None:
+        """Zero gradient buffers, reset per-step state and start next step's all-gathers."""
+        for u in self.units:
+            if u.trainable:
+                u.grad.zero_()
+                if u.grad_shard is not u.grad:
+                    u.grad_shard.zero_()
+            u.rs_pending = False
+        self._grad_scale = 1.0
+        self._norm_sq = None
+        self._max_norm = None
+        for u in self.units:
+            if u.trainable:
+                self._gather(u)
+
+    def logical_parameter_counts(self) -> tuple[int, int]:
+        total = sum(e.numel for u in self.units for e in u.entries)
+        trainable = sum(e.numel for u in self.units if u.trainable for e in u.entries)
+        return total, trainable
+
+    # ---------------------------------------------------- checkpoints
+    def _shard_rows(self, full: torch.Tensor) -> torch.Tensor:
+        """This rank's Shard(0) chunk of a full tensor (torch.chunk semantics, as DTensor uses)."""
+        chunks = torch.chunk(full, self.world, dim=0)
+        return chunks[self.rank] if self.rank < len(chunks) else full.new_zeros((0,) + tuple(full.shape[1:]))
+
+    def _to_dtensor(self, local: torch.Tensor, shape: torch.Size):
+        from torch.distributed.tensor import DTensor, Shard
+
+        return DTensor.from_local(local, self.shard_mesh, [Shard(0)], run_check=False, shape=shape,
+                                  stride=torch.empty(shape, device="meta").stride())
+
+    def _full_fp32(self, u: FlatUnit, flat_shard: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return flat_shard
+        out = torch.empty(u.padded, dtype=flat_shard.dtype, device=flat_shard.device)
+        dist.all_gather_into_tensor(out, flat_shard.contiguous(), group=self.group)
+        return out
+
+    def _iter_tensors(self, which: str, full: bool):
+        for u in self.units:
+            if which != "param" and not u.trainable:
+                continue
+            if which == "param":
+                src = self._full_fp32(u, u.master) if u.trainable else u.full.float()
+            else:
+                src = self._full_fp32(u, getattr(u, which))
+            for e in u.entries:
+                t = src[e.offset:e.offset + e.numel].view(e.shape)
+                if full or self.world == 1:
+                    yield e, t.detach().to("cpu", copy=True)
+                else:
+                    yield e, self._to_dtensor(self._shard_rows(t).detach().clone().cpu(), e.shape)
+
+    def checkpoint_state_dict(self, full: bool = False) -> dict[str, Any]:
+        out: dict[str, Any] = {}
+        for e, t in self._iter_tensors("param", full):
+            for fqn in e.fqns:
+                out[fqn] = t
+        return out
+
+    @torch.no_grad()
+    def load_checkpoint_state_dict(self, sd: dict[str, Any], full: bool = False) -> None:
+        for u in self.units:
+            stage = torch.zeros(u.padded, dtype=torch.float32, device=self.device)
+            for e in u.entries:
+                key = next((f for f in e.fqns if f in sd), None)
+                if key is None:
+                    continue
+                stage[e.offset:e.offset + e.numel].copy_(self._full_from_value(sd[key], e.shape).reshape(-1))
+            lo, hi = u.local_range(self.rank)
+            if u.trainable:
+                u.master.copy_(stage[lo:hi])
+            u.full.copy_(stage.to(u.full.dtype))
+
+    def _full_from_value(self, v: Any, shape: torch.Size) -> torch.Tensor:
+        try:
+            from torch.distributed.tensor import DTensor
+
+            if isinstance(v, DTensor):
+                v = v.full_tensor()
+        except ImportError:  # pragma: no cover
+            pass
+        return v.to(self.device, torch.float32).reshape(shape)
+
+    def optimizer_state_views(self, full: bool = False):
+        """(fqns, step-independent tensors) for exp_avg / exp_avg_sq in checkpoint layout."""
+        avg = list(self._iter_tensors("exp_avg", full))
+        sq = list(self._iter_tensors("exp_avg_sq", full))
+        return [(e.fqns, a, s) for (e, a), (_, s) in zip(avg, sq)]
+
+    @torch.no_grad()
+    def load_optimizer_views(self, state: dict[str, dict[str, Any]]) -> None:
+        for u in self.units:
+            if not u.trainable:
+                continue
+            for name in ("exp_avg", "exp_avg_sq"):
+                stage = torch.zeros(u.padded, dtype=torch.float32, device=self.device)
+                for e in u.entries:
+                    key = next((f for f in e.fqns if f in state and name in state[f]), None)
+                    if key is not None:
+                        stage[e.offset:e.offset + e.numel].copy_(
+                            self._full_from_value(state[key][name], e.shape).reshape(-1))
+                lo, hi = u.local_range(self.rank)
+                getattr(u, name).copy_(stage[lo:hi])
+
+
+def _make_fold_hook(gview: torch.Tensor) -> Callable:
+    def hook(t: torch.Tensor) -> None:
+        if t.grad is not None:
+            gview.add_(t.grad.to(gview.dtype))
+            t.grad = None
+
+    return hook
