@@ -1,0 +1,12 @@
+#!/usr/bin/env bash
+# Offline install of the reference into baseline/_ref (its pyproject declares
+# dependencies that are not in the wheelhouse, so --no-deps), plus an unmodified
+# copy of its recipes/ tree, which the wheel does not package.
+set -euo pipefail
+HERE="$(cd "$(dirname "$0")" && pwd)"
+SRC="${1:-/root/reference}"
+python -m pip install --no-index --no-build-isolation --no-deps --find-links /opt/wheelhouse \
+    --target "$HERE/_ref" "$SRC"
+rm -rf "$HERE/_ref/recipes"
+cp -r "$SRC/recipes" "$HERE/_ref/recipes"
+echo "reference installed under $HERE/_ref"

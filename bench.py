@@ -1,0 +1,345 @@
+#!/usr/bin/env python
+"""Headline benchmark: Qwen3-8B dense-decoder pretraining throughput with FSDP on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Workload (weak scaling, fixed per-GPU work): Qwen3-8B architecture (36 layers,
+hidden 4096, 32 q / 8 kv heads, head_dim 128, SwiGLU 12288, QK-norm, RoPE 1e6,
+vocab 151936, untied), random-init weights, bf16 compute with fp32 master
+weights and AdamW; synthetic data: token ids uniform over the vocabulary,
+documents with lengths uniform in [256, 4096] packed into 8192-token sequences
+with a causal mask per document; 8 sequences per GPU per optimizer step
+(micro-batch 1 x 8 accumulation steps), i.e. a global batch of 64 sequences on
+8 GPUs.  Every step runs forward, backward, the gradient reduce-scatter,
+global-norm clip and the AdamW update.
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and
+``torch.cuda.synchronize()`` on both sides and timed with CUDA events on the
+compute stream; the reported step time is the max over ranks.  Weights,
+optimizer state and activations are far larger than the 126 MB L2, so no
+explicit flush is needed between steps.  A second timed pass measures the same
+steps end to end through ``Engine.train_step`` (host batches in pinned memory
+copied to the device every step, the step's loss read back to the host).
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQ_LEN = 8192
+PER_GPU_SEQS = 8
+MODEL = "Qwen/Qwen3-8B-Base"
+METRIC = "tokens/s (Qwen3-8B FSDP pretraining, 8192-token packed sequences; whole job)"
+
+
+def _env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices: list[int]):
+        self.gpus = gpu_indices
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:  # type: ignore[union-attr]
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if self.gpus and idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        loaded = [s for s in sm if s > 500] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _measured_peak() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def _bytes_of(batch: dict) -> int:
+    import torch
+
+    return sum(v.numel() * v.element_size() for v in batch.values() if isinstance(v, torch.Tensor))
+
+
+def _vocab_of(model: str) -> int:
+    from mvp_engine.models.qwen3 import load_qwen3_config
+
+    return load_qwen3_config(model).vocab_size
+
+
+def run_ours(args) -> None:
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+    import torch
+    import torch.distributed as dist
+
+    from mvp_engine.config.loader import compose_config
+    from mvp_engine.engine import TrainStepContext
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.ops import _ext
+
+    world = _env_int("WORLD_SIZE", 1)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    rank = _env_int("RANK", 0)
+    import_recipe_modules(__import__("pathlib").Path(ROOT) / "recipes" / "qwen3")
+    from recipes.qwen3.engine.qwen3_engine import Qwen3Engine
+
+    steps_total = args.warmup + 2 * args.steps + 2
+    overrides = [
+        f"model.pretrained_model_name_or_path={args.model}",
+        f"data.train_path=synthetic://text?vocab={_vocab_of(args.model)}&min_len=256&max_len=4096",
+        f"data.max_seq_len={args.seq_len}",
+        f"optim.global_batch_size={PER_GPU_SEQS * world}",
+        "data.batch_size=1",
+        "optim.gradient_accumulation_steps=-1",
+        f"loop.total_steps={steps_total}",
+        "log.backends=[terminal]",
+        "log.interval=1000000",
+        f"project.dir={os.environ.get('MVP_BENCH_OUT', '/tmp/mvp_bench')}",
+        "checkpoint.interval=1000000",
+        "data.num_workers=0",
+        "model.gradient_checkpointing.enabled=false",
+    ] + list(args.override or [])
+    cfg = compose_config(os.path.join(ROOT, "recipes/qwen3/configs/synthetic_8b.yaml"), overrides)
+    engine = Qwen3Engine(cfg)
+    ga = int(engine.config.optim.gradient_accumulation_steps)
+
+    # Decide how many layers recompute activations from the memory left after
+    # weights and optimizer state: build, measure, then enable checkpointing.
+    engine.train_loader = engine.prepare_dataloader("train")
+    engine.model = engine.prepare_model()
+    engine.optimizer = engine.prepare_optimizer()
+    from mvp_engine.utils.training import GradientAccumulationState, GradientScaler
+    from mvp_engine.utils.log.timer import Timer
+
+    engine.ga_state = GradientAccumulationState(ga)
+    engine.scheduler = engine.prepare_scheduler()
+    engine.scaler = GradientScaler(enabled=True, dtype=engine.dtype, device=engine.device_type)
+    engine.timer = Timer(total_progress=engine.total_steps)
+    inner = engine.unwrapped_model
+    cfgm = inner.config
+    torch.cuda.synchronize()
+    free, _total = torch.cuda.mem_get_info()
+    H, F, L = cfgm.hidden_size, cfgm.intermediate_size, cfgm.num_hidden_layers
+    qkv = (cfgm.num_attention_heads + 2 * cfgm.num_key_value_heads) * cfgm.head_dim
+    per_layer = args.seq_len * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
+                                    cfgm.head_dim + 3 * F) * 1.1
+    head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
+    budget = free - head_ws - (10 << 30)
+    keep = max(0, min(L, int(budget // per_layer)))
+    ckpt_layers = L - keep if args.ckpt_layers < 0 else args.ckpt_layers
+    if ckpt_layers > 0:
+        inner.gradient_checkpointing_enable({"num_layers": ckpt_layers})
+    engine.model.train()
+
+    it = iter(engine.train_loader)
+    n_host = (args.warmup + 2 * args.steps) * ga  # the end-to-end pass gets fresh batches
+    host_batches = [next(it) for _ in range(n_host)]
+    h2d_bytes = sum(_bytes_of(b) for b in host_batches[:ga])
+    tokens_per_step = sum(int(b["total_tokens"]) for b in host_batches[:ga]) * world
+
+    def step_host(i: int) -> dict:
+        return engine.train_step(host_batches[i * ga:(i + 1) * ga])
+
+    for i in range(args.warmup):
+        step_host(i)
+    torch.cuda.synchronize()
+
+    # ---- device-timed pass: inputs staged on the device beforehand
+    staged = []
+    for i in range(args.steps):
+        row = []
+        for b in host_batches[(args.warmup + i) * ga:(args.warmup + i + 1) * ga]:
+            ctx = TrainStepContext(data=b, step=0, epoch=0, micro_step=0)
+            engine.train_pre_step(ctx)
+            row.append(ctx.data)
+        staged.append(row)
+    torch.cuda.synchronize()
+    sampler = ClockSampler([_env_int("LOCAL_RANK", 0)] if world == 1 else list(range(world)))
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.5)
+    engine.mfu_kit.reset()
+    _ext.start_counting()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for row in staged:
+        for d in row:
+            ctx = TrainStepContext(data=d, step=engine.step, epoch=0, micro_step=engine.ga_state.micro_step)
+            engine.train_exec_step(ctx)
+        engine.step += 1
+    end.record()
+    torch.cuda.synchronize()
+    launches = _ext.stop_counting()
+    if dist.is_initialized():
+        dist.barrier()
+    clocks = sampler.stop() if rank == 0 else {}
+    ms = start.elapsed_time(end) / args.steps
+    ms_t = torch.tensor([ms], device=engine.device, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    fl = torch.tensor([engine.mfu_kit._accumulated_model_flops], device=engine.device, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(fl)
+    flops_per_step = float(fl.item()) / args.steps  # logical FLOPs summed over ranks (reference formula)
+    engine.mfu_kit.reset()
+
+    # ---- end-to-end pass through the public step API (H2D from pinned memory, loss read back)
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    losses = []
+    for i in range(args.steps):
+        out = step_host(args.warmup + args.steps + i)
+        losses.append(float(out["global_loss_sum"]) / max(1, int(out["global_effective_token_count"])))
+    e_end.record()
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_end) / args.steps
+    e_t = torch.tensor([e_ms], device=engine.device, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e_ms = float(e_t.item())
+
+    peaks = _measured_peak()
+    value = tokens_per_step / (ms / 1e3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform token ids over 151936, document lengths U[256,4096] packed to 8192 tokens "
+                "(causal mask per document); random-init Qwen3-8B weights",
+        "config": {"model": "Qwen3-8B", "global_batch": PER_GPU_SEQS * world, "seq_len": args.seq_len,
+                   "parallelism": f"fsdp{world}", "micro_batch": 1, "grad_accum": ga,
+                   "activation_checkpoint_layers": ckpt_layers,
+                   "l2": "no flush: weights, optimizer state and activations >> 126 MB L2",
+                   "optimizer": "AdamW (fp32 master, fused flat-shard kernel), clip 1.0, cosine"},
+        "tokens_per_s_per_gpu": round(value / world, 1),
+        "mfu": round(flops_per_step / (ms / 1e3) / (2250e12 * world), 4),
+        "mfu_vs_measured_bf16_sustained": (round(flops_per_step / (ms / 1e3) / (peaks["bf16_tflops_sustained"] * 1e12
+                                                                                 * world), 4)
+                                           if peaks.get("bf16_tflops_sustained") else None),
+        "clocks": clocks,
+        "e2e": {"value": round(tokens_per_step / (e_ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(e_ms, 3),
+                "h2d_bytes_per_step": int(h2d_bytes),
+                "d2h_bytes_per_step": 8 * 2 + 4 * 1,
+                "api": "recipes.qwen3 Qwen3Engine.train_step(host micro-batches)"},
+        "gpu_launches": int(launches),
+        "loss_last": round(losses[-1], 4) if losses else None,
+        "impl": "ours",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    from baseline.reference_arm import run as ref_run
+
+    ref_run(args)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default=MODEL)
+    ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
+    ap.add_argument("--ckpt-layers", type=int, default=-1, help="-1: choose from free memory")
+    ap.add_argument("--override", action="append", help="extra config override k=v (repeatable)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -68,6 +68,20 @@ def _delete(tree: dict, dotted: str) -> None:
     node.pop(keys[-1], None)
 
 
+def _parse_value(raw: str) -> Any:
+    """YAML scalar/collection parsing; YAML 1.1 leaves '1e-3' a string, so numbers are retried."""
+    if raw == "":
+        return ""
+    value = yaml.safe_load(raw)
+    if isinstance(value, str):
+        for cast in (int, float):
+            try:
+                return cast(value)
+            except ValueError:
+                continue
+    return value
+
+
 def apply_dotlist(tree: dict, overrides: Iterable[str]) -> dict:
     out = copy.deepcopy(tree)
     for item in overrides:
@@ -80,7 +94,7 @@ def apply_dotlist(tree: dict, overrides: Iterable[str]) -> dict:
         if "=" not in item:
             raise ValueError(f"override {item!r} must look like key=value")
         key, raw = item.split("=", 1)
-        value = yaml.safe_load(raw) if raw != "" else ""
+        value = _parse_value(raw)
         if key.startswith("++"):
             _set(out, key[2:], value, must_exist=None)
         elif key.startswith("+"):

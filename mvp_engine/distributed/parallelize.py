@@ -1,0 +1,109 @@
+"""Model wrapping entry point (reference: mvp_engine/distributed/parallelize.py:27-140).
+
+``parallelize_model(model, parallel_mesh, backend_kwargs)`` picks the backend
+from the mesh like the reference (shard == tensor == 1 -> DDP; otherwise
+TP/SP first, then FSDP) with one extra switch, ``backend_kwargs.impl``:
+
+* ``"native"`` (default on CUDA): the engine's flat-buffer FSDP
+  (:class:`mvp_engine.parallel.fsdp.NativeFSDP`) over the data-parallel
+  group, with native kernels and fused collectives; also used on a single
+  rank so the same optimizer path runs everywhere;
+* ``"torch"``: torch DDP / FSDP2 / DTensor TP exactly as the reference does.
+
+A context-parallel degree > 1 attaches the ring or Ulysses runtime
+(:mod:`mvp_engine.parallel.context`) to the model.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+import torch.nn as nn
+
+from ..config.loader import to_container
+from ..utils.log import logger
+from .parallel_mesh import ParallelMesh
+
+
+def _set_default(d: dict, key: str, value: Any) -> dict:
+    d.setdefault(key, value)
+    return d
+
+
+def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwargs: Optional[dict] = None,
+                      device: Optional[torch.device] = None) -> nn.Module:
+    kw = dict(to_container(backend_kwargs) if backend_kwargs is not None else {})
+    impl = kw.pop("impl", "native")
+    sequence_parallel = bool(kw.pop("sequence_parallel", False))
+    cp_cfg = kw.pop("context_parallel", {}) or {}
+    comm_cfg = kw.pop("comm", {}) or {}
+    tp = parallel_mesh.tp
+    if sequence_parallel and not tp.active:
+        raise ValueError("Sequence parallel requires an active tensor mesh with parallel.mesh.tensor > 1.")
+    shard_active = parallel_mesh.has_dim("shard") and parallel_mesh.role("shard").active
+    if not shard_active and tp.active:
+        raise ValueError(f"Invalid device mesh shape {parallel_mesh.summary()['shape']}. "
+                         "Tensor/sequence parallel should be used with FSDP rather than the pure DDP")
+
+    if parallel_mesh.has_dim("context") and parallel_mesh.cp.active:
+        from ..parallel.context import attach_context_parallel
+
+        attach_context_parallel(model, parallel_mesh, impl=cp_cfg.get("impl", "ring"),
+                                fused=bool(comm_cfg.get("fused", True)))
+
+    if impl == "native":
+        from ..parallel.fsdp import NativeFSDP
+
+        if tp.active:
+            from ..parallel.tensor_parallel import apply_native_tensor_parallel
+
+            apply_native_tensor_parallel(model, parallel_mesh, sequence_parallel=sequence_parallel,
+                                         fused=bool(comm_cfg.get("fused", True)))
+        mp = (kw.get("fsdp2") or {}).get("mp_policy") or {}
+        param_dtype = mp.get("param_dtype", "bfloat16") if isinstance(mp, dict) else "bfloat16"
+        dev = device or next(model.parameters()).device
+        if dev.type != "cuda" and param_dtype == "bfloat16":
+            param_dtype = "float32" if next(model.parameters()).dtype == torch.float32 else param_dtype
+        dp = parallel_mesh.dp
+        shard_mesh = parallel_mesh.submesh("dp") if dp.active else None
+        if shard_mesh is not None and len(dp.dim_names) > 1:
+            shard_mesh = parallel_mesh.device_mesh[dp.dim_names]._flatten("_".join(dp.dim_names))
+        logger.info(f"Wrapping {type(model).__name__} with native flat FSDP over {dp.world_size} rank(s)...")
+        return NativeFSDP(model, group=dp.group, device=dev, param_dtype=param_dtype,
+                          comm="fused" if comm_cfg.get("fused", True) else "nccl", shard_mesh=shard_mesh)
+
+    if not shard_active and not tp.active:
+        from torch.nn.parallel import DistributedDataParallel
+
+        logger.info(f"Wrapping {type(model).__name__} with DistributedDataParallel...")
+        ddp_kw = dict(kw.get("ddp", {}) or {})
+        if parallel_mesh.device_mesh is None:
+            return model
+        _set_default(ddp_kw, "device_mesh", parallel_mesh.ddp.mesh)
+        return DistributedDataParallel(model, **ddp_kw)
+
+    if tp.active:
+        from .tp import parallelize_model_with_tensor_parallel
+
+        logger.info(f"Wrapping {type(model).__name__} with Tensor Parallel...")
+        parallelize_model_with_tensor_parallel(model, tp.mesh, sequence_parallel=sequence_parallel)
+    if shard_active:
+        from torch.distributed.fsdp import CPUOffloadPolicy
+
+        from .fsdp2 import parallelize_model_with_fsdp2
+
+        logger.info(f"Wrapping {type(model).__name__} with FSDP2...")
+        fkw = dict(kw.get("fsdp2", {}) or {})
+        _set_default(fkw, "target_classes", [])
+        _set_default(fkw, "mesh", parallel_mesh.fsdp.mesh)
+        _set_default(fkw, "reshard_after_forward", True)
+        _set_default(fkw, "mp_policy", {"param_dtype": "bfloat16", "reduce_dtype": "float32",
+                                        "buffer_dtype": "bfloat16"})
+        if fkw.pop("offload_policy", False):
+            fkw["offload_policy"] = CPUOffloadPolicy()
+        mp = fkw.get("mp_policy")
+        if isinstance(mp, dict):
+            mp.pop("buffer_dtype", None)
+        return parallelize_model_with_fsdp2(model, fkw)
+    return model

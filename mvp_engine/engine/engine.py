@@ -319,6 +319,24 @@ class Engine(ABC):
                 self.epoch += 1
                 logger.info(f"Starting epoch {self.epoch}...")
 
+    def train_step(self, micro_batches: list[Any]) -> dict[str, Any]:
+        """One optimizer step over ``micro_batches`` (host batches as the dataloader yields them):
+        each goes through ``train_pre_step`` and ``train_exec_step``; the step's outputs are returned.
+        This is the public single-step API the training loop, benchmarks and tests share."""
+        if len(micro_batches) != int(self.config.optim.gradient_accumulation_steps):
+            raise ValueError(f"expected {self.config.optim.gradient_accumulation_steps} micro-batches, "
+                             f"got {len(micro_batches)}")
+        ctx = None
+        for data in micro_batches:
+            ctx = TrainStepContext(data=data, step=self.step, epoch=self.epoch, micro_step=self.ga_state.micro_step)
+            prepared = self.train_pre_step(ctx)
+            if prepared is not None and prepared is not ctx:
+                ctx.data = prepared
+            self.train_exec_step(ctx)
+        assert ctx is not None and ctx.optimizer_step_completed, "the last micro-batch must complete a step"
+        self.step += 1
+        return ctx.outputs or {}
+
     def train_pre_step(self, ctx: TrainStepContext) -> Optional[TrainStepContext]:
         return None
 

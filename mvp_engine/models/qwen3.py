@@ -288,19 +288,34 @@ class Qwen3ForCausalLM(nn.Module):
             self.lm_head.weight = self.model.embed_tokens.weight
         self.loss_chunk_size = 4096
 
+    def gradient_checkpointing_enable(self, gradient_checkpointing_kwargs: Optional[dict] = None) -> None:
+        """Recompute decoder layers in backward (all, or the first ``num_layers``)."""
+        kw = gradient_checkpointing_kwargs or {}
+        self.model.gradient_checkpointing = True
+        self.model.checkpoint_layers = kw.get("num_layers")
+
+    def gradient_checkpointing_disable(self) -> None:
+        self.model.gradient_checkpointing = False
+
     # ------------------------------------------------------------------ init
     @torch.no_grad()
+    def init_param_(self, fqn: str, t: torch.Tensor, seed: Optional[int] = None) -> None:
+        """HF-style init of one parameter in place: ones for norms, N(0, initializer_range)
+        otherwise; the stream is seeded per (seed, name) so sharded and unsharded builds agree."""
+        if fqn.endswith("norm.weight") or "layernorm" in fqn:
+            t.fill_(1.0)
+            return
+        gen = torch.Generator(device=t.device)
+        gen.manual_seed(_param_seed(seed, fqn))
+        t.copy_(torch.randn(t.shape, generator=gen, device=t.device, dtype=torch.float32)
+                .mul_(self.config.initializer_range))
+
+    @torch.no_grad()
     def init_weights(self, seed: Optional[int] = None) -> None:
-        """HF-style init: normal(0, initializer_range) linears/embeddings, ones for norms."""
-        gen = torch.Generator(device="cpu")
-        if seed is not None:
-            gen.manual_seed(int(seed))
-        std = self.config.initializer_range
         for name, p in self.named_parameters():
-            if name.endswith("norm.weight") or "layernorm" in name:
-                p.fill_(1.0)
-            else:
-                p.copy_(torch.randn(p.shape, generator=gen, dtype=torch.float32).mul_(std).to(p.dtype))
+            buf = torch.empty(p.shape, dtype=torch.float32, device=p.device)
+            self.init_param_(name, buf, seed)
+            p.copy_(buf)
 
     # ----------------------------------------------------------------- inputs
     def packed_context(self, input_ids: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
@@ -348,6 +363,12 @@ class Qwen3ForCausalLM(nn.Module):
         return qwen3_flops(self.config, batch_size, seq_len, attention_mask, is_training, freeze_llm)
 
 
+def _param_seed(seed: Optional[int], fqn: str) -> int:
+    import zlib
+
+    return (int(seed or 0) * 1_000_003 + zlib.crc32(fqn.encode())) % (1 << 62)
+
+
 def attention_pairs(batch: int, tokens: int, attention_mask: Optional[torch.Tensor]) -> int:
     """Σ len² over documents (packed segment ids > 1) or valid lengths (0/1 masks)."""
     if attention_mask is None or attention_mask.dim() != 2:
@@ -382,6 +403,7 @@ def build_qwen3(name_or_path: str = "Qwen/Qwen3-8B-Base", *, seed: Optional[int]
     cfg = load_qwen3_config(name_or_path, **overrides)
     with torch.device(device or "cpu"):
         model = Qwen3ForCausalLM(cfg).to(dtype)
+    model._init_seed = seed
     if device is None or torch.device(device).type != "meta":
         model.init_weights(seed)
     return model

@@ -194,8 +194,9 @@ class RopeCache:
         self.max_positions = int(max_positions)
         self.theta = float(theta)
         self.mrope_section = list(mrope_section) if mrope_section else None
-        self.inv_freq = 1.0 / (self.theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
-        axis = torch.zeros(head_dim // 2, dtype=torch.int8)
+        ar = torch.arange(0, head_dim, 2, dtype=torch.int64, device="cpu").float()
+        self.inv_freq = 1.0 / (self.theta ** (ar / head_dim))
+        axis = torch.zeros(head_dim // 2, dtype=torch.int8, device="cpu")
         if self.mrope_section:
             for dim, offset in ((1, 1), (2, 2)):
                 length = self.mrope_section[dim] * 3
@@ -208,7 +209,7 @@ class RopeCache:
         cached = self._tables.get(device)
         if cached is None or cached[0].shape[0] <= max_pos:
             n = max(self.max_positions, 1 << int(math.ceil(math.log2(max_pos + 1))))
-            p = torch.arange(n, dtype=torch.float32)
+            p = torch.arange(n, dtype=torch.float32, device="cpu")
             ang = torch.outer(p, self.inv_freq)
             cached = (ang.cos().to(device), ang.sin().to(device), self.axis_of.to(device))
             self._tables[device] = cached
@@ -326,7 +327,8 @@ class _Embedding(torch.autograd.Function):
     @staticmethod
     def forward(ctx, ids, w, anchor):
         ctx.save_for_backward(ids, w)
-        return _ext.ext().embedding_fwd(w, ids.reshape(-1).contiguous()).view(*ids.shape, w.shape[1])
+        return _ext.ext().embedding_fwd(w, ids.reshape(-1).contiguous(),
+                                        _ext.status_buffer(w.device).data_ptr()).view(*ids.shape, w.shape[1])
 
     @staticmethod
     def backward(ctx, dout):

@@ -16,6 +16,47 @@ import torch
 _EXT = None
 _ERR: Exception | None = None
 
+# Kernels launched per extension call (for launch accounting in benchmarks).
+KERNELS_PER_CALL = {
+    "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 1, "swiglu_fwd": 1,
+    "swiglu_bwd": 1, "ce_fwd": 1, "ce_bwd_": 1, "adamw_step_": 1, "sumsq": 1, "embedding_fwd": 1,
+    "embedding_bwd_": 1, "flash_attn_fwd": 1, "flash_attn_bwd": 3,
+}
+launch_count = 0
+counting = False
+
+
+class _Counting:
+    """Forwards to the extension module and counts native kernel launches while enabled."""
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        k = KERNELS_PER_CALL.get(name)
+        if k is None or not callable(fn):
+            return fn
+
+        def wrapped(*a, **kw):
+            global launch_count
+            if counting:
+                launch_count += k
+            return fn(*a, **kw)
+
+        return wrapped
+
+
+def start_counting() -> None:
+    global counting, launch_count
+    counting, launch_count = True, 0
+
+
+def stop_counting() -> int:
+    global counting
+    counting = False
+    return launch_count
+
 
 def native_required() -> bool:
     """Native kernels are required whenever CUDA is usable (override: MVP_ALLOW_EAGER=1)."""
@@ -28,7 +69,7 @@ def ext():
     if _EXT is not None:
         return _EXT
     try:
-        _EXT = importlib.import_module("mvp_engine._C")
+        _EXT = _Counting(importlib.import_module("mvp_engine._C"))
     except Exception as exc:  # pragma: no cover - depends on the build
         _ERR = exc
         raise RuntimeError(

@@ -28,7 +28,7 @@ void adamw_step_(torch::Tensor& p, const torch::Tensor& g, torch::Tensor& m, tor
                  double wd, int64_t step, double grad_scale, const c10::optional<torch::Tensor>& norm_sq,
                  double max_norm);
 torch::Tensor sumsq(const torch::Tensor& x);
-torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids);
+torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids, int64_t status_ptr);
 void embedding_bwd_(torch::Tensor& dw, const torch::Tensor& dout, const torch::Tensor& ids);
 
 std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,

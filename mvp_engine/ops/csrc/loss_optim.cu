@@ -220,24 +220,32 @@ __global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restri
 }
 
 // ----------------------------------------------------------- embedding
+// Out-of-range ids read as zero rows and set the status word (kBadArgument).
 __global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ w, const int64_t* __restrict__ ids,
-                                     __nv_bfloat16* __restrict__ out, int64_t T, int H) {
+                                     __nv_bfloat16* __restrict__ out, int64_t T, int H, int64_t V, int* status) {
   const int H8 = H / 8;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < T * H8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = i / H8;
     const int c = static_cast<int>(i % H8);
-    reinterpret_cast<uint4*>(out + t * H)[c] = reinterpret_cast<const uint4*>(w + ids[t] * H)[c];
+    const int64_t id = ids[t];
+    if (id < 0 || id >= V) {
+      reinterpret_cast<uint4*>(out + t * H)[c] = make_uint4(0u, 0u, 0u, 0u);
+      if (c == 0) record_status(status, kBadArgument);
+      continue;
+    }
+    reinterpret_cast<uint4*>(out + t * H)[c] = reinterpret_cast<const uint4*>(w + id * H)[c];
   }
 }
 
 __global__ void embedding_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const int64_t* __restrict__ ids,
-                                     float* __restrict__ dw, int64_t T, int H) {
+                                     float* __restrict__ dw, int64_t T, int H, int64_t V) {
   const int H4 = H / 4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < T * H4;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t t = i / H4;
     const int c = static_cast<int>(i % H4);
+    if (ids[t] < 0 || ids[t] >= V) continue;
     const uint2 u = reinterpret_cast<const uint2*>(dout + t * H)[c];
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
@@ -338,7 +346,7 @@ torch::Tensor sumsq(const torch::Tensor& x) {
   return partial.sum();
 }
 
-torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids) {
+torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids, int64_t status_ptr) {
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous(), "embedding: bf16 weight");
   TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embedding: int64 ids");
   const int H = static_cast<int>(w.size(1));
@@ -349,7 +357,7 @@ torch::Tensor embedding_fwd(const torch::Tensor& w, const torch::Tensor& ids) {
   if (T > 0) {
     mvp::embedding_fwd_kernel<<<mvp::grid_for(T * H / 8, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), ids.data_ptr<int64_t>(),
-        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H);
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H, w.size(0), reinterpret_cast<int*>(status_ptr));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   return out;
@@ -363,6 +371,7 @@ void embedding_bwd_(torch::Tensor& dw, const torch::Tensor& dout, const torch::T
   const at::cuda::CUDAGuard guard(dw.device());
   if (T == 0) return;
   mvp::embedding_bwd_kernel<<<mvp::grid_for(T * H / 4, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), ids.data_ptr<int64_t>(), dw.data_ptr<float>(), T, H);
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), ids.data_ptr<int64_t>(), dw.data_ptr<float>(), T, H,
+      dw.size(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -133,6 +133,8 @@ class NativeFSDP(nn.Module):
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if (group is not None and dist.is_initialized()) else 0
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
+        if self.device.type == "meta":
+            raise ValueError("NativeFSDP needs a real device for its buffers (got meta)")
         self.param_dtype = _dtype(param_dtype)
         self.comm = comm
         self.shard_mesh = shard_mesh
@@ -144,6 +146,16 @@ class NativeFSDP(nn.Module):
         self.units: list[FlatUnit] = []
         self._comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self._build_units(cls_names)
+        # Shard masters are registered as parameters (their .grad is the fp32
+        # gradient shard) so generic code -- model.parameters(), torch optimizers,
+        # p.grad.mul_(...) -- works on the sharded state.
+        self.shard_params = nn.ParameterList()
+        for u in self.units:
+            if u.trainable:
+                p = nn.Parameter(u.master, requires_grad=True)
+                u.master = p
+                self.shard_params.append(p)
+        self._attach_grads()
         self._install_hooks()
         self._gather_all(initial=True)
 
@@ -213,10 +225,20 @@ class NativeFSDP(nn.Module):
         lo, hi = u.local_range(self.rank)
         if u.trainable:
             u.master = torch.zeros(u.shard, dtype=torch.float32, device=dev)
+        init = getattr(self.module, "init_param_", None)
+        seed = getattr(self.module, "_init_seed", None)
         with torch.no_grad():
             for e in u.entries:
                 p = src[id(e)]
-                flat = p.detach().reshape(-1)
+                if p.is_meta:
+                    # Materialise straight into the flat buffers, one parameter at a time.
+                    if init is None:
+                        raise RuntimeError(f"{e.fqns[0]} is on the meta device and the model has no init_param_")
+                    tmp = torch.empty(e.shape, dtype=torch.float32, device=dev)
+                    init(e.fqns[0], tmp, seed)
+                    flat = tmp.reshape(-1)
+                else:
+                    flat = p.detach().reshape(-1)
                 u.full[e.offset:e.offset + e.numel].copy_(flat)
                 if u.trainable:
                     a, b = max(lo, e.offset), min(hi, e.offset + e.numel)
@@ -408,6 +430,28 @@ class NativeFSDP(nn.Module):
         self._max_norm = float(max_norm)
         return nsq.sqrt()[0] * self._grad_scale
 
+    def _attach_grads(self) -> None:
+        for u in self.units:
+            if u.trainable:
+                u.master.grad = u.grad_shard[: u.shard] if u.grad_shard is u.grad else u.grad_shard
+
+    def attach_optimizer(self, optimizer: torch.optim.Optimizer) -> torch.optim.Optimizer:
+        """For a stock torch optimizer over ``shard_params``: after each ``step`` refresh the
+        compute weights from the updated masters and start the next all-gathers."""
+
+        def post(opt, args, kwargs):
+            with torch.no_grad():
+                for u in self.units:
+                    if u.trainable:
+                        lo, hi = u.local_range(self.rank)
+                        u.full[lo:hi].copy_(u.master.detach())
+            self.after_optimizer_step()
+
+        if not getattr(optimizer, "_mvp_native_step", False):
+            optimizer.register_step_pre_hook(lambda opt, a, k: self.finish_grad_sync())
+            optimizer.register_step_post_hook(post)
+        return optimizer
+
     def after_optimizer_step(self) -> None:
         """Zero gradient buffers, reset per-step state and start next step's all-gathers."""
         for u in self.units:
@@ -419,6 +463,7 @@ class NativeFSDP(nn.Module):
         self._grad_scale = 1.0
         self._norm_sq = None
         self._max_norm = None
+        self._attach_grads()
         for u in self.units:
             if u.trainable:
                 self._gather(u)

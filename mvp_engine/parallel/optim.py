@@ -32,6 +32,7 @@ class FlatAdamW(torch.optim.Optimizer):
             raise ValueError("No trainable parameters found.")
         super().__init__(params, dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay))
         self._step_count = 0
+        self._mvp_native_step = True
 
     @torch.no_grad()
     def step(self, closure: Optional[Any] = None):
@@ -44,7 +45,7 @@ class FlatAdamW(torch.optim.Optimizer):
         for u in self.units:
             lo, hi = u.local_range(f.rank)
             shadow = u.full[lo:hi] if u.full.dtype == torch.bfloat16 else None
-            ops.adamw_step_(u.master, u.grad_shard, u.exp_avg, u.exp_avg_sq, lr=float(g["lr"]), beta1=b1, beta2=b2,
+            ops.adamw_step_(u.master.data, u.grad_shard[: u.shard], u.exp_avg, u.exp_avg_sq, lr=float(g["lr"]), beta1=b1, beta2=b2,
                             eps=float(g["eps"]), weight_decay=float(g["weight_decay"]), step=self._step_count,
                             grad_scale=f._grad_scale, norm_sq=f._norm_sq,
                             max_norm=f._max_norm if f._max_norm is not None else 0.0, p_bf16=shadow)
