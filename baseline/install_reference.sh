@@ -7,6 +7,8 @@ HERE="$(cd "$(dirname "$0")" && pwd)"
 SRC="${1:-/root/reference}"
 python -m pip install --no-index --no-build-isolation --no-deps --find-links /opt/wheelhouse \
     --target "$HERE/_ref" "$SRC"
+# package data the wheel does not declare (the launcher and engine read it at run time)
+cp "$SRC/mvp_engine/config/default.yaml" "$HERE/_ref/mvp_engine/config/default.yaml"
 rm -rf "$HERE/_ref/recipes"
 cp -r "$SRC/recipes" "$HERE/_ref/recipes"
 echo "reference installed under $HERE/_ref"

@@ -210,6 +210,20 @@ def run_ours(args) -> None:
     for i in range(args.warmup):
         step_host(i)
     torch.cuda.synchronize()
+    if args.profile:
+        # One step inside an NVTX range for `ncu --nvtx --nvtx-include profile_step`.
+        # start/end (not push/pop) range: it spans threads, so autograd's backward
+        # kernels are inside it too
+        rid = torch.cuda.nvtx.range_start("profile_step")
+        step_host(args.warmup)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_end(rid)
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "ga": ga, "ckpt_layers": ckpt_layers}), flush=True)
+        if dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # ---- device-timed pass: inputs staged on the device beforehand
     staged = []
@@ -332,6 +346,7 @@ def main() -> None:
     ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
     ap.add_argument("--ckpt-layers", type=int, default=-1, help="-1: choose from free memory")
     ap.add_argument("--override", action="append", help="extra config override k=v (repeatable)")
+    ap.add_argument("--profile", action="store_true", help="warm up, then run one step in an NVTX range and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

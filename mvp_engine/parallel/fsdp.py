@@ -341,15 +341,18 @@ class NativeFSDP(nn.Module):
                 u.ag_event.record(self._comm_stream)
                 u.full.record_stream(self._comm_stream)
         else:
-            parts = list(u.full.chunk(self.world))
-            dist.all_gather(parts, u.full[lo:hi].clone(), group=self.group)
+            parts = [torch.empty(u.shard, dtype=u.full.dtype) for _ in range(self.world)]
+            dist.all_gather(parts, u.full[lo:hi].detach().clone(), group=self.group)
+            with torch.no_grad():
+                u.full.copy_(torch.cat(parts))
 
+    @torch.no_grad()
     def _gather_all(self, initial: bool = False) -> None:
         for u in self.units:
             if initial and self.world > 1 and u.trainable:
                 # masters were copied from the full init; refresh this rank's slice
                 lo, hi = u.local_range(self.rank)
-                u.full[lo:hi].copy_(u.master)
+                u.full[lo:hi].copy_(u.master.detach())
             self._gather(u)
 
     def _reduce_scatter(self, idx: int) -> None:
@@ -368,10 +371,11 @@ class NativeFSDP(nn.Module):
                 u.rs_event = torch.cuda.Event()
                 u.rs_event.record(self._comm_stream)
         else:
-            buf = u.grad.clone()
+            buf = u.grad.detach().clone()
             dist.all_reduce(buf, group=self.group)
             lo, hi = u.local_range(self.rank)
-            u.grad_shard.copy_(buf[lo:hi])
+            with torch.no_grad():
+                u.grad_shard.copy_(buf[lo:hi])
 
     def finish_grad_sync(self) -> None:
         """Reduce-scatter units whose hook did not fire (root, embeddings) and wait for all."""
@@ -485,12 +489,18 @@ class NativeFSDP(nn.Module):
         return DTensor.from_local(local, self.shard_mesh, [Shard(0)], run_check=False, shape=shape,
                                   stride=torch.empty(shape, device="meta").stride())
 
+    @torch.no_grad()
     def _full_fp32(self, u: FlatUnit, flat_shard: torch.Tensor) -> torch.Tensor:
+        flat_shard = flat_shard.detach()
         if self.world == 1:
             return flat_shard
-        out = torch.empty(u.padded, dtype=flat_shard.dtype, device=flat_shard.device)
-        dist.all_gather_into_tensor(out, flat_shard.contiguous(), group=self.group)
-        return out
+        if flat_shard.is_cuda:
+            out = torch.empty(u.padded, dtype=flat_shard.dtype, device=flat_shard.device)
+            dist.all_gather_into_tensor(out, flat_shard.contiguous(), group=self.group)
+            return out
+        parts = [torch.empty_like(flat_shard) for _ in range(self.world)]
+        dist.all_gather(parts, flat_shard.contiguous(), group=self.group)
+        return torch.cat(parts)
 
     def _iter_tensors(self, which: str, full: bool):
         for u in self.units:
@@ -507,6 +517,7 @@ class NativeFSDP(nn.Module):
                 else:
                     yield e, self._to_dtensor(self._shard_rows(t).detach().clone().cpu(), e.shape)
 
+    @torch.no_grad()
     def checkpoint_state_dict(self, full: bool = False) -> dict[str, Any]:
         out: dict[str, Any] = {}
         for e, t in self._iter_tensors("param", full):

@@ -1,0 +1,52 @@
+"""Native flat FSDP on gloo ranks (CPU): world 2 must reproduce the single-process run."""
+
+import torch
+
+from mvp_engine.testing import spawn_workers
+
+
+def _train(rank, world, port, steps, seed):
+    import os
+
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import build_qwen3
+    from mvp_engine.parallel.fsdp import NativeFSDP
+    from mvp_engine.parallel.optim import FlatAdamW
+
+    if world > 1:
+        initialize_process_group()
+    group = dist.group.WORLD if world > 1 else None
+    model = build_qwen3("mvp/qwen3-tiny", seed=seed, vocab_size=256, hidden_size=128, intermediate_size=256,
+                        num_attention_heads=2, num_key_value_heads=1)
+    fsdp = NativeFSDP(model, group=group, device=torch.device("cpu"), param_dtype=torch.float32)
+    opt = FlatAdamW(fsdp, lr=1e-3, weight_decay=0.1)
+    g = torch.Generator().manual_seed(123)
+    data = [torch.randint(0, 256, (2, 64), generator=g) for _ in range(steps)]
+    losses = []
+    for x in data:
+        # each rank takes its half of the global batch of 2 rows
+        rows = x if world == 1 else x[rank:rank + 1]
+        out = fsdp(input_ids=rows, labels=rows)
+        loss = out["loss"].sum() / (x.shape[0] * (x.shape[1] - 1))
+        loss.backward()
+        fsdp.clip_grad_norm_(1.0)
+        opt.step()
+        l = loss.detach().clone()
+        if world > 1:
+            dist.all_reduce(l)
+        losses.append(float(l))
+    sd = fsdp.checkpoint_state_dict(full=True)
+    return losses, {k: v.clone() for k, v in list(sd.items())[:4]}
+
+
+def test_fsdp_world2_matches_single_process():
+    single = spawn_workers(_train, 1, 5, 7)[0]
+    multi = spawn_workers(_train, 2, 5, 7)
+    for a, b in zip(single[0], multi[0][0]):
+        assert abs(a - b) < 2e-3 * max(1.0, abs(a)), (single[0], multi[0][0])
+    assert multi[0][0] == multi[1][0]
+    for k, v in single[1].items():
+        assert torch.allclose(v, multi[0][1][k], atol=1e-4), k
+        assert torch.allclose(multi[0][1][k], multi[1][1][k])
