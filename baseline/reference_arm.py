@@ -73,6 +73,14 @@ def run(args) -> None:
     if not os.path.isdir(os.path.join(REF, "recipes")):
         _unavailable("reference recipes/ missing under baseline/_ref (baseline/install_reference.sh copies them)")
         return
+    # transformers probes for `accelerate` when first imported; do that before the
+    # stand-ins are importable so the probe sees the real (absent) package.
+    import transformers  # noqa: F401
+    import transformers.modeling_utils  # noqa: F401
+
+    for k, v in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29531"), ("RANK", "0"), ("WORLD_SIZE", "1"),
+                 ("LOCAL_RANK", "0")):
+        os.environ.setdefault(k, v)
     # The reference package is also called mvp_engine: put it (and the stand-ins) first.
     root = os.path.dirname(HERE)
     sys.path[:] = [REF, SHIMS] + [p for p in sys.path if os.path.abspath(p or ".") != root]

@@ -396,12 +396,19 @@ class NativeFSDP(nn.Module):
         self._wait_gather(0)
         for sib in self._siblings(0):
             self._wait_gather(sib)
-        if self.module.training and torch.is_grad_enabled():
-            emb_anchor = getattr(self.module, "model", None)
-            if emb_anchor is not None and self.device.type == "cuda":
-                # gives the embedding backward a tensor that requires grad, so it runs
-                emb_anchor._embed_anchor = self._anchor
+        if self.module.training and torch.is_grad_enabled() and self.device.type == "cuda":
+            # Give the embedding backward a tensor that requires grad, so it runs even
+            # though the weight view itself does not require grad.
+            for mod in self._embed_owners():
+                mod._embed_anchor = self._anchor
         return self.module(*args, **kwargs)
+
+    def _embed_owners(self) -> list[nn.Module]:
+        owners = getattr(self, "_embed_owner_cache", None)
+        if owners is None:
+            owners = [m for m in self.module.modules() if hasattr(m, "embed_tokens")]
+            self._embed_owner_cache = owners
+        return owners
 
     @property
     def _anchor(self) -> torch.Tensor:

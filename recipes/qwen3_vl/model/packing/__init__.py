@@ -1,0 +1,4 @@
+from .prepare import build_packed_varlen_kwargs, prepare_packed_model_inputs
+from .qwen3_vl import build_qwen3_vl_packed_position_ids
+
+__all__ = ["build_packed_varlen_kwargs", "build_qwen3_vl_packed_position_ids", "prepare_packed_model_inputs"]

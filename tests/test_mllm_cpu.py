@@ -1,0 +1,54 @@
+"""Multimodal data kit on CPU: processor geometry, schema, packing, collation, guards."""
+
+import torch
+
+from mvp_engine.kit.mllm import (MLLMDataKit, MLLMDataSpec, MLLMLoaderSpec, MLLMPackingSpec, MLLMSampleSpec,
+                                 MLLMSourceSpec, MLLMTextOnlyBatchGuard, QwenImageHandler, QwenVLMediaHandler,
+                                 QwenVLTokenizationHandler)
+from mvp_engine.kit.mllm.data import SyntheticVLSchemaHandler, smart_resize
+
+
+def test_smart_resize_bounds():
+    h, w = smart_resize(1000, 700, factor=32, min_pixels=64 * 1024, max_pixels=1024 * 1024)
+    assert h % 32 == 0 and w % 32 == 0 and h * w <= 1024 * 1024
+    assert smart_resize(448, 448, factor=32, min_pixels=1, max_pixels=1 << 30) == (448, 448)
+
+
+def _spec(max_len=4096):
+    kit = MLLMDataKit()
+    proc = kit.build_processor("synthetic", image_max_pixels=1344 * 1344)
+    tok = proc.tokenizer
+    sample = MLLMSampleSpec(SyntheticVLSchemaHandler(), QwenVLMediaHandler(proc),
+                            QwenVLTokenizationHandler(tok, max_seq_len=max_len))
+    src = MLLMSourceSpec("synthetic://mm?min_px=64&max_px=256&num_rows=12&min_text=20&max_text=100",
+                         dataset_source="synthetic_mm", resample=False)
+    return kit, proc, MLLMDataSpec(src, sample, MLLMPackingSpec(max_len, buffer_size=4, open_pack_limit=2),
+                                   MLLMLoaderSpec(batch_size=1))
+
+
+def test_pipeline_image_tokens_match_features():
+    kit, proc, spec = _spec()
+    items = list(kit.build_dataset(spec))
+    assert items
+    image_id = proc.tokenizer.convert_tokens_to_ids("<|image_pad|>")
+    for it in items:
+        n_tok = int((it["input_ids"] == image_id).sum())
+        assert n_tok == int(it["image_grid_thw"].prod(-1).sum()) // 4
+        assert it["pixel_values"].shape == (int(it["image_grid_thw"].prod(-1).sum()), 3 * 2 * 16 * 16)
+        assert it["input_ids"].numel() <= 4096
+        seg = it["pack_segment_ids"]
+        assert int(seg.max()) == it["source_sample_num"]
+
+
+def test_collate_and_text_only_guard():
+    kit, proc, spec = _spec()
+    loader = kit.build_dataloader(kit.build_dataset(spec), spec)
+    b = next(iter(loader))
+    assert b["effective_tokens"] > 0 and "pixel_values" in b
+    dummy = QwenImageHandler().build_dummy_inputs(proc)
+    guard = MLLMTextOnlyBatchGuard(dummy_inputs=dummy, media_keys=("pixel_values", "image_grid_thw"),
+                                   pad_token_id=proc.tokenizer.pad_token_id)
+    text_only = {k: v for k, v in b.items() if k not in ("pixel_values", "image_grid_thw")}
+    out = guard(text_only)
+    assert out["pixel_values"].shape[0] == 4 and out["input_ids"].shape[1] >= b["input_ids"].shape[1]
+    assert int(out["pack_segment_ids"].max()) == int(b["pack_segment_ids"].max()) + 1
