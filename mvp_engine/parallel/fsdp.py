@@ -139,7 +139,9 @@ class NativeFSDP(nn.Module):
         self.comm = comm
         self.shard_mesh = shard_mesh
         self._sync_grads = True
-        self._grad_scale = 1.0
+        # Gradients are averaged over the data-parallel ranks (FSDP2 / DDP semantics): the
+        # reduce-scatter sums, and the 1/world factor rides in the optimizer's gradient scale.
+        self._grad_scale = 1.0 / self.world
         self._norm_sq: Optional[torch.Tensor] = None
         self._max_norm: Optional[float] = None
         cls_names = set(unit_classes) if unit_classes else set(getattr(model, "_no_split_modules", []) or [])
@@ -471,7 +473,7 @@ class NativeFSDP(nn.Module):
                 if u.grad_shard is not u.grad:
                     u.grad_shard.zero_()
             u.rs_pending = False
-        self._grad_scale = 1.0
+        self._grad_scale = 1.0 / self.world
         self._norm_sq = None
         self._max_norm = None
         self._attach_grads()

@@ -29,13 +29,14 @@ def _train(rank, world, port, steps, seed):
         # each rank takes its half of the global batch of 2 rows
         rows = x if world == 1 else x[rank:rank + 1]
         out = fsdp(input_ids=rows, labels=rows)
-        loss = out["loss"].sum() / (x.shape[0] * (x.shape[1] - 1))
+        loss = out["loss"].sum() / (rows.shape[0] * (rows.shape[1] - 1))  # rank-local mean; ranks are averaged
         loss.backward()
         fsdp.clip_grad_norm_(1.0)
         opt.step()
         l = loss.detach().clone()
         if world > 1:
             dist.all_reduce(l)
+            l /= world
         losses.append(float(l))
     sd = fsdp.checkpoint_state_dict(full=True)
     return losses, {k: v.clone() for k, v in list(sd.items())[:4]}

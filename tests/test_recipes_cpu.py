@@ -87,3 +87,48 @@ def test_qwen3_vl_engine_trains_on_cpu_two_ranks():
         assert 5.0 < lg["train/loss"] < 13.0
     assert logs[0]["train/loss"] == pytest.approx(logs[1]["train/loss"])
     assert logs[0]["tokens/total"] == logs[1]["tokens/total"]
+
+
+def _run_vit(rank, world, port, steps, global_batch, impl):
+    import tempfile
+
+    import torch.distributed as dist
+
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = ROOT / "recipes" / "vit_classification"
+    import_recipe_modules(root)
+    cfg = load_smoke_test_config(root, "tiny_cpu_fp32", output_dir=Path(tempfile.mkdtemp()),
+                                 config_overrides=(f"loop.total_steps={steps}", "checkpoint.interval=1000000",
+                                                   f"data.batch_size={global_batch // world}",
+                                                   f"parallel.backend_kwargs.impl={impl}"))
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    losses = []
+    post = eng.train_post_step
+
+    def record(ctx):
+        post(ctx)
+        l = torch.tensor([eng.last_logs["train/loss"]], dtype=torch.float64)
+        if dist.is_initialized() and world > 1:
+            dist.all_reduce(l)
+            l /= world
+        losses.append(float(l))
+
+    eng.train_post_step = record
+    eng.train()
+    return losses
+
+
+@pytest.mark.parametrize("impl", ["native", "torch"])
+def test_vit_tiny_fsdp_world2_matches_single_process(impl):
+    """ViT-Tiny/16 (192 hidden, 3 heads, MLP 768, 12 layers, 1000 classes), fp32, gloo FSDP over 2 ranks with
+    per-rank batch 8, AdamW lr 1e-3, 20 steps: the loss curve equals the single-process run with batch 16."""
+    from mvp_engine.testing.utils import spawn_workers
+
+    single = spawn_workers(_run_vit, 1, 20, 16, impl, timeout=900)[0]
+    multi = spawn_workers(_run_vit, 2, 20, 16, impl, timeout=900)
+    assert len(single) == 20 and multi[0] == multi[1]
+    for a, b in zip(single, multi[0]):
+        assert abs(a - b) <= 1e-4 * max(1.0, abs(a)), (single, multi[0])
