@@ -48,6 +48,9 @@ QWEN3_8B_SHAPES = {
 }
 
 
+_WITH_REF = True
+
+
 def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
     from mvp_engine import ops
 
@@ -66,7 +69,7 @@ def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
         }
         for kind, (ours, ref) in cases.items():
             t_ours = _time(ours, iters)
-            t_ref = _time(ref, iters)
+            t_ref = _time(ref, iters) if _WITH_REF else float("nan")
             print(
                 json.dumps(
                     {
@@ -119,6 +122,8 @@ def bench_attention(T: int, Hq: int, Hkv: int, iters: int, lo: int = 256, hi: in
            "fwd_ms": round(t_f, 4), "fwd_tflops": round(fwd_flops / t_f / 1e9, 1),
            "bwd_ms": round(t_b, 4), "bwd_tflops": round(2.5 * fwd_flops / t_b / 1e9, 1)}
     try:  # comparison column: the FlashAttention-2 library the reference trains with
+        if not _WITH_REF:
+            raise RuntimeError("skipped (--no-ref)")
         from flash_attn import flash_attn_varlen_func
 
         mx = max(lens)
@@ -140,7 +145,10 @@ def main() -> None:
     ap.add_argument("--heads", default="32,8")
     ap.add_argument("--shape", default=None, help="M,N,K")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--no-ref", action="store_true", help="skip the library comparison columns")
     args = ap.parse_args()
+    global _WITH_REF
+    _WITH_REF = not args.no_ref
     if args.what == "gemm":
         shapes = QWEN3_8B_SHAPES
         if args.shape:
