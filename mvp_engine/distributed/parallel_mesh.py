@@ -26,6 +26,7 @@ DEFAULT_ROLE_DIMS: dict[str, tuple[str, ...]] = {
     "tp": ("tensor",),
     "sp": ("tensor",),
     "cp": ("context",),
+    "dp_cp": ("replicate", "shard", "context"),
 }
 
 MESH_DIM_ORDER = ("replicate", "shard", "context", "tensor")
@@ -120,6 +121,12 @@ class ParallelMesh:
     def cp(self) -> MeshRole:
         return self.role("cp")
 
+    @property
+    def dp_cp(self) -> MeshRole:
+        """Ranks that share parameters and reduce gradients / token counts: data x context
+        parallel (the dp role itself when context parallelism is off)."""
+        return self.role("dp_cp") if self.has_dim("context") and self._shape.get("context", 1) > 1 else self.dp
+
     def role(self, name: str) -> MeshRole:
         cached = self._roles.get(name)
         if cached is not None:
@@ -170,7 +177,7 @@ class ParallelMesh:
         return dist.get_rank(self.device_mesh[name].get_group())
 
     def summary(self) -> dict[str, Any]:
-        roles = {n: self.role(n) for n in DEFAULT_ROLE_DIMS}
+        roles = {n: self.role(n) for n in DEFAULT_ROLE_DIMS if n != "dp_cp"}
         return {
             "dim_names": self.dim_names,
             "shape": tuple(self._shape[d] for d in self.dim_names),

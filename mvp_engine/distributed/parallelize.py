@@ -65,8 +65,8 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
         dev = device or next(model.parameters()).device
         if dev.type != "cuda" and param_dtype == "bfloat16":
             param_dtype = "float32" if next(model.parameters()).dtype == torch.float32 else param_dtype
-        dp = parallel_mesh.dp
-        shard_mesh = parallel_mesh.submesh("dp") if dp.active else None
+        dp = parallel_mesh.dp_cp  # context ranks share parameters too
+        shard_mesh = dp.mesh if dp.active else None
         if shard_mesh is not None and len(dp.dim_names) > 1:
             shard_mesh = parallel_mesh.device_mesh[dp.dim_names]._flatten("_".join(dp.dim_names))
         logger.info(f"Wrapping {type(model).__name__} with native flat FSDP over {dp.world_size} rank(s)...")
@@ -80,7 +80,10 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
         ddp_kw = dict(kw.get("ddp", {}) or {})
         if parallel_mesh.device_mesh is None:
             return model
-        _set_default(ddp_kw, "device_mesh", parallel_mesh.ddp.mesh)
+        if parallel_mesh.cp.active:
+            _set_default(ddp_kw, "process_group", parallel_mesh.dp_cp.group)
+        else:
+            _set_default(ddp_kw, "device_mesh", parallel_mesh.ddp.mesh)
         return DistributedDataParallel(model, **ddp_kw)
 
     if tp.active:
@@ -96,7 +99,8 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
         logger.info(f"Wrapping {type(model).__name__} with FSDP2...")
         fkw = dict(kw.get("fsdp2", {}) or {})
         _set_default(fkw, "target_classes", [])
-        _set_default(fkw, "mesh", parallel_mesh.fsdp.mesh)
+        _set_default(fkw, "mesh", parallel_mesh.fsdp.mesh if not parallel_mesh.cp.active
+                     else parallel_mesh.device_mesh[parallel_mesh.dp_cp.dim_names]._flatten("dp_cp"))
         _set_default(fkw, "reshard_after_forward", True)
         _set_default(fkw, "mp_policy", {"param_dtype": "bfloat16", "reduce_dtype": "float32",
                                         "buffer_dtype": "bfloat16"})

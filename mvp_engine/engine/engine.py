@@ -181,7 +181,7 @@ class Engine(ABC):
         rt.world_size = dist.get_world_size() if dist.is_initialized() else 1
         rt.hostname = socket.gethostname()
         rt.python_version = platform.python_version()
-        rt.torch_version = torch.__version__
+        rt.torch_version = str(torch.__version__)
         if not rt.run_id:
             local = f"{self.config.project.name}_{time.strftime('%Y%m%d%H%M%S', time.localtime())}_{secrets.token_hex(2)}"
             rt.run_id = broadcast_from_main(local)

@@ -249,6 +249,9 @@ def shift_labels(labels: torch.Tensor) -> torch.Tensor:
     return F.pad(labels, (0, 1), value=-100)[..., 1:]
 
 
+_shift_labels = shift_labels
+
+
 def cu_seqlens_from_segments(segment_ids: torch.Tensor) -> tuple[torch.Tensor, int]:
     """Flat-token ``cu_seqlens`` from per-row segment ids (0 = padding, its own segment).
 
@@ -341,17 +344,22 @@ class Qwen3ForCausalLM(nn.Module):
     def forward(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
                 position_ids: Optional[torch.Tensor] = None, cu_seq_lens_q: Optional[torch.Tensor] = None,
                 max_length_q: Optional[int] = None, pack_segment_ids: Optional[torch.Tensor] = None,
-                ctx: Optional[PackedContext] = None, **unused: Any) -> dict:
+                ctx: Optional[PackedContext] = None, shift_labels: Optional[torch.Tensor] = None,
+                **unused: Any) -> dict:
+        """``shift_labels`` (labels already shifted by one, e.g. by context-parallel sharding)
+        replaces ``labels``; with a context-parallel runtime attached (``_mvp_cp``) the inputs are
+        this rank's tokens while ``cu_seq_lens_q`` describes the whole row."""
         if ctx is None:
-            ctx = self.packed_context(input_ids, position_ids, cu_seq_lens_q, max_length_q, pack_segment_ids)
+            ctx = self.packed_context(input_ids, position_ids, cu_seq_lens_q, max_length_q, pack_segment_ids,
+                                      cp=getattr(self, "_mvp_cp", None))
         dtype = torch.bfloat16 if input_ids.is_cuda else self.lm_head.weight.dtype
         if torch.is_autocast_enabled() and not input_ids.is_cuda:
             dtype = torch.get_autocast_dtype("cpu")
         h = self.model(input_ids, ctx, dtype)
         w = _as_compute(self.lm_head.weight, h)
-        if labels is None:
+        if labels is None and shift_labels is None:
             return {"logits": ops.linear(h, w).view(*input_ids.shape, -1)}
-        flat_labels = shift_labels(labels).reshape(-1)
+        flat_labels = (shift_labels if shift_labels is not None else _shift_labels(labels)).reshape(-1)
         loss = ops.fused_linear_cross_entropy(h, w, flat_labels, self.loss_chunk_size)
         return {"loss": loss, "logits": None}
 

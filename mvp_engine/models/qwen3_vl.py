@@ -85,7 +85,7 @@ QWEN3_VL_PRESETS = {
                     deepstack_visual_indexes=[5, 11, 17])),
     "mvp/qwen3-vl-tiny": dict(
         text=dict(vocab_size=151936, hidden_size=256, intermediate_size=512, num_hidden_layers=3,
-                  num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=32768),
+                  num_attention_heads=4, num_key_value_heads=2, head_dim=128, max_position_embeddings=32768),
         vision=dict(depth=3, hidden_size=128, intermediate_size=256, num_heads=2, out_hidden_size=256,
                     deepstack_visual_indexes=[0, 1], num_position_embeddings=256)),
 }

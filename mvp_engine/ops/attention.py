@@ -116,3 +116,84 @@ def _sdpa_per_doc(q, k, v, cu_seqlens, causal, scale):
         o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=causal, scale=scale)
         outs.append(o.squeeze(0).transpose(0, 1))
     return torch.cat(outs, 0) if outs else q.new_zeros(q.shape)
+
+
+# ----------------------------------------------------------------- key-document pairs
+def _pair_mask(Lq: int, Lk: int, causal: bool, device) -> Optional[torch.Tensor]:
+    """Disallowed (query, key) cells of one document: causal aligned to the document end."""
+    if not causal:
+        return None
+    t = torch.arange(Lq, device=device).view(-1, 1)
+    u = torch.arange(Lk, device=device).view(1, -1)
+    return u > t + (Lk - Lq)
+
+
+def attention_pair_reference(q, k, v, cu_q, cu_k, causal, softmax_scale):
+    """Oracle for attention of query documents ``cu_q`` against key documents ``cu_k``
+    (document d: rows cu_q[d]..cu_q[d+1] see keys cu_k[d]..cu_k[d+1]).  Returns (o, lse [Hq, Tq])."""
+    T, Hq, D = q.shape
+    rep = Hq // k.shape[1]
+    out = torch.zeros(T, Hq, D, dtype=q.dtype, device=q.device)
+    lse = torch.full((Hq, T), float("-inf"), dtype=torch.float32, device=q.device)
+    for (qs, qe), (ks, ke) in zip(zip(cu_q.tolist()[:-1], cu_q.tolist()[1:]), zip(cu_k.tolist()[:-1], cu_k.tolist()[1:])):
+        if qe <= qs or ke <= ks:
+            continue
+        qq = q[qs:qe].float().transpose(0, 1)
+        kk = k[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        vv = v[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        att = (qq @ kk.transpose(1, 2)) * softmax_scale
+        m = _pair_mask(qe - qs, ke - ks, causal, q.device)
+        if m is not None:
+            att = att.masked_fill(m, float("-inf"))
+        l = torch.logsumexp(att, dim=-1)
+        p = torch.exp(att - l.unsqueeze(-1)).nan_to_num(0.0)
+        lse[:, qs:qe] = l
+        out[qs:qe] = (p @ vv).transpose(0, 1).to(q.dtype)
+    return out, lse
+
+
+def attention_pair_bwd_reference(do, q, k, v, o, lse, cu_q, cu_k, causal, softmax_scale):
+    """Gradients of one (query docs, key docs) pair given the softmax normaliser ``lse`` of the
+    complete attention (so per-pair results add up to the full gradient)."""
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    rep = Hq // Hkv
+    dq = torch.zeros(T, Hq, D, dtype=torch.float32, device=q.device)
+    dk = torch.zeros(k.shape[0], Hkv, D, dtype=torch.float32, device=q.device)
+    dv = torch.zeros_like(dk)
+    delta = (do.float() * o.float()).sum(-1).transpose(0, 1)  # [Hq, T]
+    for (qs, qe), (ks, ke) in zip(zip(cu_q.tolist()[:-1], cu_q.tolist()[1:]), zip(cu_k.tolist()[:-1], cu_k.tolist()[1:])):
+        if qe <= qs or ke <= ks:
+            continue
+        qq = q[qs:qe].float().transpose(0, 1)
+        kk = k[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        vv = v[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        dd = do[qs:qe].float().transpose(0, 1)
+        s = (qq @ kk.transpose(1, 2)) * softmax_scale
+        m = _pair_mask(qe - qs, ke - ks, causal, q.device)
+        p = torch.exp(s - lse[:, qs:qe].unsqueeze(-1))
+        if m is not None:
+            p = p.masked_fill(m, 0.0)
+        dp = dd @ vv.transpose(1, 2)
+        ds = p * (dp - delta[:, qs:qe].unsqueeze(-1)) * softmax_scale
+        dq[qs:qe] += (ds @ kk).transpose(0, 1)
+        gk = (ds.transpose(1, 2) @ qq).view(Hkv, rep, ke - ks, D).sum(1)
+        gv = (p.transpose(1, 2) @ dd).view(Hkv, rep, ke - ks, D).sum(1)
+        dk[ks:ke] += gk.transpose(0, 1)
+        dv[ks:ke] += gv.transpose(0, 1)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+def attention_pair_fwd(q, k, v, cu_q, cu_k, causal, softmax_scale):
+    """(o, lse) of ``q`` against a separate key stream (tcgen05 kernel on CUDA)."""
+    if _native(q):
+        return _ext.ext().flash_attn_fwd(q, k, v, cu_q, softmax_scale, causal, _ext.status_buffer(q.device).data_ptr(),
+                                         cu_seqlens_k=cu_k)
+    return attention_pair_reference(q, k, v, cu_q, cu_k, causal, softmax_scale)
+
+
+def attention_pair_bwd(do, q, k, v, o, lse, cu_q, cu_k, causal, softmax_scale):
+    if _native(q):
+        return _ext.ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, cu_q, softmax_scale, causal,
+                                         _ext.status_buffer(q.device).data_ptr(), cu_seqlens_k=cu_k)
+    return attention_pair_bwd_reference(do, q, k, v, o, lse, cu_q, cu_k, causal, softmax_scale)

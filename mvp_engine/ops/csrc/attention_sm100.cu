@@ -5,6 +5,13 @@
 // j with start(i) <= j <= i (causal) or start(i) <= j < end(i) (bidirectional,
 // used by the vision tower).  No mask tensor is ever built.
 //
+// Separate key documents: with cu_seqlens_k, query rows cu_q[d] .. cu_q[d+1]
+// attend keys cu_k[d] .. cu_k[d+1] of a key stream of Tk rows (document d may
+// be empty on either side).  Causal masking is then aligned to the end of the
+// document (query row t of Lq sees key u of Lk iff u <= t + Lk - Lq), which is
+// plain causal masking when cu_k == cu_q.  Ring context parallelism uses this
+// to attend a local query chunk to another rank's key chunk.
+//
 // q: [T, Hq, 128], k: [T, Hkv, 128], v: [T, Hkv, 128] (any row strides that
 // are multiples of 8 elements), o: [T, Hq, 128] bf16, lse: [Hq, T] fp32
 // (natural-log LSE of the scaled logits, for the backward pass).
@@ -42,24 +49,50 @@ struct FwdParams {
   __nv_bfloat16* o;
   int64_t o_row_stride;
   float* lse;
-  const int* cu_seqlens;
+  const int* cu_seqlens;    // query-side documents
+  const int* cu_seqlens_k;  // key-side documents (== cu_seqlens for self-attention)
   int n_docs;
-  int T, Hq, Hkv;
+  int T, Tk, Hq, Hkv;
   float scale_log2;
   int causal;
   int* status;
 };
 
-__device__ __forceinline__ void doc_bounds(const int* cu, int n_docs, int i, int& start, int& end) {
-  // largest d with cu[d] <= i
-  int lo = 0, hi = n_docs;  // cu has n_docs + 1 entries
+// Largest d with cu[d] <= i (cu has n_docs + 1 entries): the non-empty document holding row i.
+__device__ __forceinline__ int doc_index(const int* cu, int n_docs, int i) {
+  int lo = 0, hi = n_docs;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (__ldg(cu + mid) <= i) lo = mid;
     else hi = mid;
   }
-  start = __ldg(cu + lo);
-  end = __ldg(cu + lo + 1);
+  return lo;
+}
+
+// Key range [lo, hi] (inclusive) visible to query row i.
+__device__ __forceinline__ void key_range(const int* cu_q, const int* cu_k, int n_docs, int causal, int i, int& lo,
+                                          int& hi) {
+  const int d = doc_index(cu_q, n_docs, i);
+  const int ks = __ldg(cu_k + d), ke = __ldg(cu_k + d + 1);
+  lo = ks;
+  hi = ke - 1;
+  if (causal) {
+    const int qs = __ldg(cu_q + d), qe = __ldg(cu_q + d + 1);
+    hi = min(hi, ks + (i - qs) + (ke - ks) - (qe - qs));
+  }
+}
+
+// Query range [lo, hi) that sees key row k.
+__device__ __forceinline__ void query_range(const int* cu_q, const int* cu_k, int n_docs, int causal, int k, int& lo,
+                                            int& hi) {
+  const int d = doc_index(cu_k, n_docs, k);
+  const int qs = __ldg(cu_q + d), qe = __ldg(cu_q + d + 1);
+  lo = qs;
+  hi = qe;
+  if (causal) {
+    const int ks = __ldg(cu_k + d), ke = __ldg(cu_k + d + 1);
+    lo = qs + max(0, (k - ks) - ((ke - ks) - (qe - qs)));
+  }
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -105,14 +138,12 @@ __global__ void __launch_bounds__(192, 1)
   const int q0 = qb * BLK;
 
   // KV range of this query block.
-  int first_start, first_end;
-  doc_bounds(p.cu_seqlens, p.n_docs, q0, first_start, first_end);
   const int q_last = min(q0 + BLK, p.T) - 1;
-  int last_start, last_end;
-  doc_bounds(p.cu_seqlens, p.n_docs, q_last, last_start, last_end);
-  const int kv_lo = first_start;
-  const int kv_hi = p.causal ? (q_last + 1) : last_end;
-  const int n_blocks = (kv_hi - kv_lo + BLK - 1) / BLK;
+  int kv_lo, first_hi, last_lo, last_hi;
+  key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, q0, kv_lo, first_hi);
+  key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, q_last, last_lo, last_hi);
+  const int kv_hi = last_hi + 1;
+  const int n_blocks = kv_hi > kv_lo ? (kv_hi - kv_lo + BLK - 1) / BLK : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -238,9 +269,8 @@ __global__ void __launch_bounds__(192, 1)
     const int r = warp * 32 + lane;
     const int i = q0 + r;
     const bool valid = i < p.T;
-    int start_i = 0, end_i = 0;
-    if (valid) doc_bounds(p.cu_seqlens, p.n_docs, i, start_i, end_i);
-    const int hi_i = p.causal ? i : end_i - 1;  // last allowed key (inclusive)
+    int start_i = 0, hi_i = -1;  // allowed keys start_i .. hi_i
+    if (valid) key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, i, start_i, hi_i);
     const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -372,11 +402,12 @@ constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 256;
 }  // namespace attn
 }  // namespace mvp
 
-// q [T, Hq, 128], k/v [T, Hkv, 128] (row strides multiple of 8, unit head/dim
-// strides), cu_seqlens int32 [n+1] on device.  Returns (o [T, Hq, 128], lse [Hq, T]).
+// q [T, Hq, 128], k/v [Tk, Hkv, 128] (row strides multiple of 8, unit head/dim
+// strides), cu_seqlens int32 [n+1] on device (and cu_seqlens_k [n+1] when the key
+// stream has its own documents; Tk == T otherwise).  Returns (o [T, Hq, 128], lse [Hq, T]).
 std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
-                                          int64_t status_ptr) {
+                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k) {
   using namespace mvp::attn;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
               "flash_attn_fwd: bf16 inputs");
@@ -387,24 +418,37 @@ std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::T
               "flash_attn_fwd: heads must be contiguous within a token");
   TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_cuda(), "flash_attn_fwd: int32 cu_seqlens");
   const int T = static_cast<int>(q.size(0));
+  const int Tk = static_cast<int>(k.size(0));
   const int Hq = static_cast<int>(q.size(1));
   const int Hkv = static_cast<int>(k.size(1));
   TORCH_CHECK(Hq % Hkv == 0, "flash_attn_fwd: Hq must be a multiple of Hkv");
+  TORCH_CHECK(v.size(0) == Tk && v.size(1) == Hkv, "flash_attn_fwd: k/v shapes differ");
+  const torch::Tensor& cu_k = cu_seqlens_k.has_value() ? *cu_seqlens_k : cu_seqlens;
+  TORCH_CHECK(cu_k.scalar_type() == at::kInt && cu_k.is_cuda() && cu_k.numel() == cu_seqlens.numel(),
+              "flash_attn_fwd: cu_seqlens_k must be int32 with as many documents as cu_seqlens");
+  TORCH_CHECK(cu_seqlens_k.has_value() || Tk == T, "flash_attn_fwd: Tk != T needs cu_seqlens_k");
   const at::cuda::CUDAGuard guard(q.device());
   auto o = torch::empty({T, Hq, D}, q.options());
   auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
   if (T == 0) return {o, lse};
   CUtensorMap tq, tk, tv;
+  if (Tk == 0) {  // nothing to attend: zero output, -inf LSE
+    o.zero_();
+    lse.fill_(-INFINITY);
+    return {o, lse};
+  }
   mvp::make_tmap_2d_bf16(&tq, q.data_ptr(), static_cast<int64_t>(Hq) * D, T, q.stride(0), 64, BLK);
-  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, T, k.stride(0), 64, BLK);
-  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, T, v.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, k.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, v.stride(0), 64, BLK);
   FwdParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   p.o_row_stride = o.stride(0);
   p.lse = lse.data_ptr<float>();
   p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.cu_seqlens_k = cu_k.data_ptr<int>();
   p.n_docs = static_cast<int>(cu_seqlens.numel() - 1);
   p.T = T;
+  p.Tk = Tk;
   p.Hq = Hq;
   p.Hkv = Hkv;
   p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
@@ -446,8 +490,9 @@ struct BwdParams {
   const float* lse;    // [Hq, T]
   const float* delta;  // [Hq, T]
   const int* cu_seqlens;
+  const int* cu_seqlens_k;
   int n_docs;
-  int T, Hq, Hkv;
+  int T, Tk, Hq, Hkv;
   float scale, scale_log2;
   int causal;
   int* status;
@@ -483,13 +528,11 @@ __global__ void __launch_bounds__(192, 1)
   const int hk = blockIdx.y;
   const int rep = p.Hq / p.Hkv;
   const int k0 = blockIdx.x * BLK;
-  const int k_last = min(k0 + BLK, p.T) - 1;
-  int ks0, ke0, ksl, kel;
-  doc_bounds(p.cu_seqlens, p.n_docs, k0, ks0, ke0);
-  doc_bounds(p.cu_seqlens, p.n_docs, k_last, ksl, kel);
-  const int q_lo = p.causal ? k0 : ks0;
-  const int q_hi = kel;
-  const int nq = (q_hi - q_lo + BLK - 1) / BLK;
+  const int k_last = min(k0 + BLK, p.Tk) - 1;
+  int q_lo, q_hi0, ql_lo, q_hi;
+  query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, k0, q_lo, q_hi0);
+  query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, k_last, ql_lo, q_hi);
+  const int nq = q_hi > q_lo ? (q_hi - q_lo + BLK - 1) / BLK : 0;
   const int n_iter = nq * rep;
 
   if (threadIdx.x == 0) {
@@ -587,10 +630,9 @@ __global__ void __launch_bounds__(192, 1)
     // warps 0-3: one key row (S^T/dP^T/dK/dV lane) and one query row (dQ lane) per thread
     const int c = warp * 32 + lane;
     const int kc = k0 + c;
-    const bool kvalid = kc < p.T;
-    int ks = 0, ke = 0;
-    if (kvalid) doc_bounds(p.cu_seqlens, p.n_docs, kc, ks, ke);
-    const int lo_c = p.causal ? kc : ks;
+    const bool kvalid = kc < p.Tk;
+    int lo_c = 0, ke = 0;  // query rows lo_c .. ke-1 see key kc
+    if (kvalid) query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, kc, lo_c, ke);
     const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
     bool ok = true;
     for (int n = 0; n < n_iter; ++n) {
@@ -671,7 +713,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(dq_read);
     }
-    if (ok && n_iter > 0) {
+    if (ok) {  // keys no query sees (n_iter == 0) get zero gradients
       tc_fence_after();
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
@@ -681,8 +723,13 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t rr[32];
-          tmem_ld_32x32b_x32(tacc + lane_addr + ch * 32, rr);
-          tmem_wait_ld();
+          if (n_iter > 0) {
+            tmem_ld_32x32b_x32(tacc + lane_addr + ch * 32, rr);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) rr[t] = 0u;
+          }
           if (kvalid) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -750,24 +797,35 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
                                           const torch::Tensor& v, const torch::Tensor& out, const torch::Tensor& lse,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
                                           int64_t status_ptr, const c10::optional<torch::Tensor>& dk_out,
-                                          const c10::optional<torch::Tensor>& dv_out) {
+                                          const c10::optional<torch::Tensor>& dv_out,
+                                          const c10::optional<torch::Tensor>& cu_seqlens_k) {
   using namespace mvp::attn;
   TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && q.is_contiguous(), "flash_attn_bwd: contiguous q/o/do");
   TORCH_CHECK(k.stride(2) == 1 && v.stride(2) == 1 && k.stride(1) == D && v.stride(1) == D,
               "flash_attn_bwd: k/v head layout");
   const int T = static_cast<int>(q.size(0));
+  const int Tk = static_cast<int>(k.size(0));
   const int Hq = static_cast<int>(q.size(1));
   const int Hkv = static_cast<int>(k.size(1));
+  const torch::Tensor& cu_k = cu_seqlens_k.has_value() ? *cu_seqlens_k : cu_seqlens;
+  TORCH_CHECK(cu_k.scalar_type() == at::kInt && cu_k.is_cuda() && cu_k.numel() == cu_seqlens.numel(),
+              "flash_attn_bwd: cu_seqlens_k must be int32 with as many documents as cu_seqlens");
+  TORCH_CHECK(cu_seqlens_k.has_value() || Tk == T, "flash_attn_bwd: Tk != T needs cu_seqlens_k");
   const at::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   auto dq_acc = torch::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
   auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
-  torch::Tensor dk = dk_out.has_value() ? *dk_out : torch::empty({T, Hkv, D}, q.options());
-  torch::Tensor dv = dv_out.has_value() ? *dv_out : torch::empty({T, Hkv, D}, q.options());
+  torch::Tensor dk = dk_out.has_value() ? *dk_out : torch::empty({Tk, Hkv, D}, q.options());
+  torch::Tensor dv = dv_out.has_value() ? *dv_out : torch::empty({Tk, Hkv, D}, q.options());
   TORCH_CHECK(dk.stride(2) == 1 && dv.stride(2) == 1 && dk.stride(1) == D && dv.stride(1) == D,
               "flash_attn_bwd: dk/dv head layout");
   auto dq = torch::empty({T, Hq, D}, q.options());
-  if (T == 0) return {dq, dk, dv};
+  if (T == 0 || Tk == 0) {
+    dq.zero_();
+    dk.zero_();
+    dv.zero_();
+    return {dq, dk, dv};
+  }
   {
     const int64_t items = static_cast<int64_t>(T) * Hq;
     bwd_delta_kernel<<<static_cast<int>((items + 7) / 8), 256, 0, stream>>>(
@@ -777,8 +835,8 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
   }
   CUtensorMap tq, tk, tv, tdo;
   mvp::make_tmap_2d_bf16(&tq, q.data_ptr(), static_cast<int64_t>(Hq) * D, T, q.stride(0), 64, BLK);
-  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, T, k.stride(0), 64, BLK);
-  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, T, v.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, k.stride(0), 64, BLK);
+  mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, v.stride(0), 64, BLK);
   mvp::make_tmap_2d_bf16(&tdo, dout.data_ptr(), static_cast<int64_t>(Hq) * D, T, dout.stride(0), 64, BLK);
   BwdParams p;
   p.dq_acc = dq_acc.data_ptr<float>();
@@ -789,8 +847,10 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
   p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.cu_seqlens_k = cu_k.data_ptr<int>();
   p.n_docs = static_cast<int>(cu_seqlens.numel() - 1);
   p.T = T;
+  p.Tk = Tk;
   p.Hq = Hq;
   p.Hkv = Hkv;
   p.scale = static_cast<float>(softmax_scale);
@@ -802,7 +862,7 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
     C10_CUDA_CHECK(cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
     configured = true;
   }
-  dim3 grid((T + BLK - 1) / BLK, Hkv);
+  dim3 grid((Tk + BLK - 1) / BLK, Hkv);
   bwd_kernel<<<grid, 192, kBwdSmem, stream>>>(tq, tk, tv, tdo, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int64_t n = static_cast<int64_t>(T) * Hq * D;

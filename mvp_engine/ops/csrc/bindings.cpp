@@ -33,13 +33,14 @@ void embedding_bwd_(torch::Tensor& dw, const torch::Tensor& dout, const torch::T
 
 std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
-                                          int64_t status_ptr);
+                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k);
 
 std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch::Tensor& q, const torch::Tensor& k,
                                           const torch::Tensor& v, const torch::Tensor& out, const torch::Tensor& lse,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
                                           int64_t status_ptr, const c10::optional<torch::Tensor>& dk_out,
-                                          const c10::optional<torch::Tensor>& dv_out);
+                                          const c10::optional<torch::Tensor>& dv_out,
+                                          const c10::optional<torch::Tensor>& cu_seqlens_k);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mvp_engine sm_100a kernels";
@@ -56,9 +57,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sumsq", &sumsq);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd_", &embedding_bwd_);
-  m.def("flash_attn_fwd", &flash_attn_fwd, "varlen flash attention forward (tcgen05)");
+  m.def("flash_attn_fwd", &flash_attn_fwd, "varlen flash attention forward (tcgen05)", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("cu_seqlens"), py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"),
+        py::arg("cu_seqlens_k") = py::none());
   m.def("flash_attn_bwd", &flash_attn_bwd, "varlen flash attention backward (tcgen05)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("cu_seqlens"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"), py::arg("dk_out") = py::none(),
-        py::arg("dv_out") = py::none());
+        py::arg("dv_out") = py::none(), py::arg("cu_seqlens_k") = py::none());
 }

@@ -25,6 +25,7 @@ from mvp_engine.kit import (LLMDataKit, LLMDataSpec, LLMLoaderSpec, LLMModelKit,
                             LLMSourceSpec, LLMStepEstimationKit, LLMTokenIdsSchemaHandler, MFUKit, OptimKit,
                             TokenNormedLossKit)
 from mvp_engine.kit.llm import ModelInputs
+from mvp_engine.parallel.context import maybe_shard_batch
 from mvp_engine.utils.log import logger
 from mvp_engine.utils.training import accumulate_gradients, clip_grad_norm_
 
@@ -45,8 +46,10 @@ class Qwen3Engine(Engine):
         self.step_estimation_kit = LLMStepEstimationKit()
         self.mfu_kit = MFUKit()
         self.optim_kit = OptimKit()
-        self.token_loss_kit = TokenNormedLossKit(device=self.device, dp_world_size=self.parallel_mesh.dp.world_size,
-                                                 dp_group=self.parallel_mesh.dp.group)
+        # token counts / loss sums reduce over every rank that holds part of a step's tokens
+        # (data x context parallel ranks)
+        red = self.parallel_mesh.dp_cp
+        self.token_loss_kit = TokenNormedLossKit(device=self.device, dp_world_size=red.world_size, dp_group=red.group)
         o = self.config.optim
         self.token_loss_kit.build_loss_guard(spike_multiplier=o.loss_spike_skip_multiplier,
                                              window_size=int(o.loss_spike_skip_window_size),
@@ -129,21 +132,26 @@ class Qwen3Engine(Engine):
 
     # -------------------------------------------------------------- steps
     def train_pre_step(self, ctx: TrainStepContext) -> TrainStepContext:
-        batch: ModelInputs = self.data_kit.to_device(ctx.data, self.device)
+        batch = maybe_shard_batch(self.unwrapped_model, ctx.data)  # context parallel: this rank's chunks (host)
+        batch: ModelInputs = self.data_kit.to_device(batch, self.device)
         ctx.data = prepare_packed_model_inputs(batch)
         return ctx
 
-    _MODEL_KEYS = ("input_ids", "labels", "position_ids", "cu_seq_lens_q", "max_length_q")
+    _MODEL_KEYS = ("input_ids", "labels", "shift_labels", "position_ids", "cu_seq_lens_q", "max_length_q")
 
     def forward_step(self, ctx: TrainStepContext) -> None:
         data = ctx.data
         with torch.autocast(device_type=self.device_type, dtype=self.dtype,
                             enabled=self.dtype != torch.float32 and self.device_type == "cuda"):
             outputs = self.model(**{k: data[k] for k in self._MODEL_KEYS if k in data})
-        self.mfu_kit.accumulate_microbatch(model=self.unwrapped_model, batch_size=int(data["input_ids"].shape[0]),
-                                           seq_len=int(data["input_ids"].shape[1]),
-                                           attention_token_pairs=data.get("attention_token_pairs"),
-                                           is_training=True, freeze_llm=bool(self.config.model.freeze_llm))
+        cp_len = data.get("cp_total_tokens")
+        flops = self.unwrapped_model.calculate_model_flops(
+            batch_size=int(data["input_ids"].shape[0]), seq_len=int(cp_len or data["input_ids"].shape[1]),
+            attention_token_pairs=data.get("attention_token_pairs"), is_training=True,
+            freeze_llm=bool(self.config.model.freeze_llm))
+        if cp_len:  # each context rank does 1/cp of the row's work
+            flops /= self.parallel_mesh.cp.world_size
+        self.mfu_kit.accumulate_microbatch(model_flops=flops)
         ctx.outputs = {"loss": outputs["loss"], "logs": {"train/loss": 0}}
 
     def backward_step(self, ctx: TrainStepContext) -> None:
