@@ -272,6 +272,27 @@ class _IterWrapper(torch.utils.data.IterableDataset):
         return iter(ds)
 
 
+class MappedLoader:
+    """Iterable of ``fn(batch)`` over another loader's batches (host-side, in the training process)."""
+
+    def __init__(self, loader: Any, fn: Callable) -> None:
+        self.loader, self.fn = loader, fn
+
+    def __iter__(self):
+        for b in self.loader:
+            yield self.fn(b)
+
+    def map(self, fn: Callable) -> "MappedLoader":
+        return MappedLoader(self, fn)
+
+
+class BatchLoader(torch.utils.data.DataLoader):
+    """torch ``DataLoader`` with ``map(fn)`` for per-batch host transforms."""
+
+    def map(self, fn: Callable) -> MappedLoader:
+        return MappedLoader(self, fn)
+
+
 class TorchLoader:
     """torch DataLoader front-end over a :class:`Dataset` (workers shard the stream)."""
 
@@ -284,7 +305,7 @@ class TorchLoader:
         self.multiprocessing_context = multiprocessing_context if self.num_workers > 0 else None
 
     def batch(self, batch_size: int, drop_last: bool = True, collate_fn: Optional[Callable] = None):
-        return torch.utils.data.DataLoader(
+        return BatchLoader(
             _IterWrapper(self.dataset), batch_size=batch_size, drop_last=drop_last, collate_fn=collate_fn,
             num_workers=self.num_workers, pin_memory=self.pin_memory, persistent_workers=self.persistent_workers,
             multiprocessing_context=self.multiprocessing_context)

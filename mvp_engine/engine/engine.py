@@ -390,7 +390,8 @@ class Engine(ABC):
                 "perf/step_time_device_ms": self.step_time_ms}
         for i, lr in enumerate(self.scheduler.get_last_lr()):
             logs[f"lr/group_{i}"] = lr
-        logger.log_metrics({**ctx.outputs["logs"], **logs}, step=self.step, total_steps=self.total_steps)
+        self.last_logs = {**ctx.outputs["logs"], **logs}
+        logger.log_metrics(self.last_logs, step=self.step, total_steps=self.total_steps)
 
     def after_train(self) -> None:
         self.save(force=True and not self.config.dev_mode)

@@ -341,7 +341,15 @@ class Qwen3ForCausalLM(nn.Module):
         pos = position_ids.reshape(-1, T) if position_ids.dim() <= 2 else position_ids.reshape(position_ids.shape[0], -1)
         return PackedContext(pos, cu, int(max_length_q), self.model.rope, cp=cp)
 
-    def forward(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
+    def forward(self, input_ids: torch.Tensor, *args: Any, **kwargs: Any) -> dict:
+        """The model manages its own precision (bf16 operands, fp32 accumulation and statistics);
+        an enclosing CUDA autocast region would only re-cast what the kernels already decide."""
+        if input_ids.is_cuda and torch.is_autocast_enabled("cuda"):
+            with torch.autocast("cuda", enabled=False):
+                return self._forward(input_ids, *args, **kwargs)
+        return self._forward(input_ids, *args, **kwargs)
+
+    def _forward(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
                 position_ids: Optional[torch.Tensor] = None, cu_seq_lens_q: Optional[torch.Tensor] = None,
                 max_length_q: Optional[int] = None, pack_segment_ids: Optional[torch.Tensor] = None,
                 ctx: Optional[PackedContext] = None, shift_labels: Optional[torch.Tensor] = None,

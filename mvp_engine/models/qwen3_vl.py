@@ -38,7 +38,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
-from ..ops.attention import flash_attn_varlen
+from ..ops.attention import attention_any_head_dim, flash_attn_varlen
 from .qwen3 import PackedContext, Qwen3Config, Qwen3DecoderLayer, Qwen3RMSNorm, _as_compute, shift_labels
 
 
@@ -227,16 +227,7 @@ def _rotate_half(x):
 
 def vision_attention(q, k, v, cu, max_len):
     """Bidirectional attention within each image; head_dim padded to 128 on CUDA (exact)."""
-    D = q.shape[-1]
-    scale = D**-0.5
-    if q.is_cuda and D <= 128 and q.dtype == torch.bfloat16:
-        pad = 128 - D
-        if pad:
-            q, k, v = (F.pad(t, (0, pad)) for t in (q, k, v))
-        o = flash_attn_varlen(q.contiguous(), k.contiguous(), v.contiguous(), cu, max_len, causal=False,
-                              softmax_scale=scale)
-        return o[..., :D]
-    return flash_attn_varlen(q, k, v, cu, max_len, causal=False, softmax_scale=scale)
+    return attention_any_head_dim(q, k, v, cu, max_len, causal=False)
 
 
 class Qwen3VLVisionBlock(nn.Module):
@@ -424,7 +415,15 @@ class Qwen3VLForConditionalGeneration(nn.Module):
             self.init_param_(name, buf, seed)
             p.copy_(buf)
 
-    def forward(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
+    def forward(self, input_ids: torch.Tensor, *args: Any, **kwargs: Any) -> dict:
+        """The model manages its own precision (bf16 operands, fp32 accumulation and statistics);
+        an enclosing CUDA autocast region would only re-cast what the kernels already decide."""
+        if input_ids.is_cuda and torch.is_autocast_enabled("cuda"):
+            with torch.autocast("cuda", enabled=False):
+                return self._forward(input_ids, *args, **kwargs)
+        return self._forward(input_ids, *args, **kwargs)
+
+    def _forward(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
                 position_ids: Optional[torch.Tensor] = None, cu_seq_lens_q: Optional[torch.Tensor] = None,
                 max_length_q: Optional[int] = None, pixel_values: Optional[torch.Tensor] = None,
                 image_grid_thw: Optional[torch.Tensor] = None, vision_meta: Optional[dict] = None,

@@ -6,6 +6,12 @@ over unfolded patches), a learned CLS token and position embeddings, L blocks
 of ``x + Attn(LN(x))`` and ``x + MLP(LN(x))`` with exact GELU, a final
 LayerNorm and a linear classifier on the CLS token.  Dropout probabilities are
 honoured in training mode.
+
+Precision: activations run in the parameters' dtype (bf16 under the native
+data-parallel runtime, fp32 otherwise) with LayerNorm statistics and the
+logits in fp32; an enclosing autocast region is switched off.  On CUDA the
+projections run on the tcgen05 GEMM and attention on the varlen flash kernel
+(one document per image, bidirectional, head_dim zero-padded to 128).
 """
 
 from __future__ import annotations
@@ -18,6 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
+from ..ops.attention import attention_any_head_dim
 
 
 @dataclass
@@ -48,6 +55,11 @@ def _linear(x: torch.Tensor, lin: nn.Linear) -> torch.Tensor:
     return F.linear(x, lin.weight.to(x.dtype), None if lin.bias is None else lin.bias.to(x.dtype))
 
 
+def _layer_norm(x: torch.Tensor, ln: nn.LayerNorm) -> torch.Tensor:
+    """LayerNorm with fp32 statistics, result in the activation dtype."""
+    return F.layer_norm(x.float(), ln.normalized_shape, ln.weight.float(), ln.bias.float(), ln.eps).to(x.dtype)
+
+
 class ViTPatchEmbeddings(nn.Module):
     def __init__(self, c: ViTConfig):
         super().__init__()
@@ -62,6 +74,8 @@ class ViTPatchEmbeddings(nn.Module):
         patches = pixel_values.reshape(B, C, Hh // P, P, Ww // P, P).permute(0, 2, 4, 1, 3, 5)
         patches = patches.reshape(B, (Hh // P) * (Ww // P), C * P * P)
         w = self.projection.weight.reshape(self.projection.weight.shape[0], -1)
+        if patches.is_cuda and patches.dtype == torch.bfloat16 and w.dtype == torch.bfloat16:
+            return ops.linear(patches.contiguous(), w) + self.projection.bias
         return F.linear(patches, w.to(patches.dtype), self.projection.bias.to(patches.dtype))
 
 
@@ -107,11 +121,16 @@ class ViTAttention(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         a = self.attention
         B, N, H = x.shape
-        q = _linear(x, a.query).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
-        k = _linear(x, a.key).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
-        v = _linear(x, a.value).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
-        o = F.scaled_dot_product_attention(q, k, v, dropout_p=a.dropout_p if self.training else 0.0)
-        o = o.transpose(1, 2).reshape(B, N, H)
+        if x.is_cuda and x.dtype == torch.bfloat16 and not (self.training and a.dropout_p > 0):
+            q, k, v = (_linear(x, lin).view(B * N, a.num_heads, a.head_dim) for lin in (a.query, a.key, a.value))
+            cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device=x.device)
+            o = attention_any_head_dim(q, k, v, cu, N, causal=False).reshape(B, N, H)
+        else:
+            q = _linear(x, a.query).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
+            k = _linear(x, a.key).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
+            v = _linear(x, a.value).view(B, N, a.num_heads, a.head_dim).transpose(1, 2)
+            o = F.scaled_dot_product_attention(q, k, v, dropout_p=a.dropout_p if self.training else 0.0)
+            o = o.transpose(1, 2).reshape(B, N, H)
         return self.output.dropout(_linear(o, self.output.dense))
 
 
@@ -139,7 +158,7 @@ class ViTLayer(nn.Module):
 
     @staticmethod
     def _ln(x: torch.Tensor, ln: nn.LayerNorm) -> torch.Tensor:
-        return F.layer_norm(x, ln.normalized_shape, ln.weight.to(x.dtype), ln.bias.to(x.dtype), ln.eps)
+        return _layer_norm(x, ln)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = x + self.attention(self._ln(x, self.layernorm_before))
@@ -201,8 +220,11 @@ class ViTForImageClassification(nn.Module):
             p.copy_(buf)
 
     def forward(self, pixel_values: torch.Tensor, labels: Optional[torch.Tensor] = None, **_: Any) -> dict:
-        h = self.vit(pixel_values)
-        logits = F.linear(h[:, 0], self.classifier.weight.to(h.dtype), self.classifier.bias.to(h.dtype))
+        if pixel_values.is_cuda and torch.is_autocast_enabled("cuda"):
+            with torch.autocast("cuda", enabled=False):
+                return self.forward(pixel_values, labels)
+        h = self.vit(pixel_values.to(self.classifier.weight.dtype))
+        logits = F.linear(h[:, 0].float(), self.classifier.weight.float(), self.classifier.bias.float())
         loss = None
         if labels is not None:
             loss = F.cross_entropy(logits.float(), labels)

@@ -197,3 +197,15 @@ def attention_pair_bwd(do, q, k, v, o, lse, cu_q, cu_k, causal, softmax_scale):
         return _ext.ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, cu_q, softmax_scale, causal,
                                          _ext.status_buffer(q.device).data_ptr(), cu_seqlens_k=cu_k)
     return attention_pair_bwd_reference(do, q, k, v, o, lse, cu_q, cu_k, causal, softmax_scale)
+
+
+def attention_any_head_dim(q, k, v, cu_seqlens, max_seqlen, causal, softmax_scale=None):
+    """Varlen attention for head_dim <= 128 on CUDA bf16: zero-padding q/k/v to 128 leaves QK^T and the
+    softmax unchanged and the padded output columns zero, so the head_dim-128 kernel computes it exactly."""
+    D = q.shape[-1]
+    scale = softmax_scale if softmax_scale is not None else D**-0.5
+    if q.is_cuda and D < 128 and q.dtype == torch.bfloat16:
+        pad = 128 - D
+        q, k, v = (F.pad(t, (0, pad)) for t in (q, k, v))
+        return flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=causal, softmax_scale=scale)[..., :D]
+    return flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=causal, softmax_scale=scale)

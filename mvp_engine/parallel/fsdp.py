@@ -251,16 +251,16 @@ class NativeFSDP(nn.Module):
             u.grad_shard = u.grad if self.world == 1 else torch.zeros(u.shard, dtype=torch.float32, device=dev)
             u.exp_avg = torch.zeros_like(u.master)
             u.exp_avg_sq = torch.zeros_like(u.master)
-        native_grads = dev.type == "cuda"
         for e in u.entries:
             view = u.full[e.offset:e.offset + e.numel].view(e.shape)
             if u.trainable:
                 gview = u.grad[e.offset:e.offset + e.numel].view(e.shape)
+                # Native kernels accumulate weight gradients straight into the flat fp32 buffer
+                # (and give autograd none); any other op (eager PyTorch: biases, LayerNorm, ...) lets
+                # autograd produce .grad, which the hook folds into the same buffer.
                 view._mvp_grad_acc = gview
-                if not native_grads:
-                    # CPU / eager ops: autograd accumulates into .grad; fold it into the flat buffer.
-                    view.requires_grad_(True)
-                    view.register_post_accumulate_grad_hook(_make_fold_hook(gview))
+                view.requires_grad_(True)
+                view.register_post_accumulate_grad_hook(_make_fold_hook(gview))
             for mod, pname in e.owners:
                 del mod._parameters[pname]
                 setattr(mod, pname, view)

@@ -132,3 +132,60 @@ def test_vit_tiny_fsdp_world2_matches_single_process(impl):
     assert len(single) == 20 and multi[0] == multi[1]
     for a, b in zip(single, multi[0]):
         assert abs(a - b) <= 1e-4 * max(1.0, abs(a)), (single, multi[0])
+
+
+def _run_recipe(rank, world, port, recipe, config, overrides):
+    import tempfile
+
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = ROOT / "recipes" / recipe
+    import_recipe_modules(root)
+    cfg = load_smoke_test_config(root, config, output_dir=Path(tempfile.mkdtemp()),
+                                 config_overrides=("checkpoint.interval=1000000",) + tuple(overrides))
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    eng.before_train()
+    m = eng.unwrapped_model
+
+    def snapshot():
+        if hasattr(eng.model, "checkpoint_state_dict"):  # native runtime: parameters live in flat buffers
+            return {n: t.detach().float().clone() for n, t in eng.model.checkpoint_state_dict(full=True).items()}
+        return {n: p.detach().float().clone() for n, p in m.named_parameters()}
+
+    before = snapshot()
+    eng.do_train()
+    after = snapshot()
+    changed = sorted(n for n in before if not torch.equal(before[n], after[n]))
+    out = {"logs": eng.last_logs, "changed": changed, "names": sorted(before)}
+    if recipe == "magic_transformer":
+        out["generated"] = m.generate(torch.zeros(1, 4, dtype=torch.long), max_new_tokens=3).shape
+    return out
+
+
+def test_openbee_stage1_trains_only_the_merger():
+    from mvp_engine.testing.utils import spawn_workers
+
+    r = spawn_workers(_run_recipe, 1, "openbee", "synthetic_tiny", ("loop.total_steps=2",), timeout=600)[0]
+    assert r["changed"], "nothing trained"
+    for n in r["changed"]:
+        assert n.startswith(("model.visual.merger.", "model.visual.deepstack_merger_list.")), n
+    assert any(n.startswith("model.language_model.") for n in r["names"])
+
+
+def test_minimal_vlm_trains_language_model_only():
+    from mvp_engine.testing.utils import spawn_workers
+
+    r = spawn_workers(_run_recipe, 1, "minimal_vlm", "synthetic_tiny", ("loop.total_steps=2",), timeout=600)[0]
+    assert 5.0 < r["logs"]["train/loss"] < 13.0
+    assert r["changed"] and not any(n.startswith("model.visual.") for n in r["changed"])
+
+
+def test_magic_transformer_trains_and_generates():
+    from mvp_engine.testing.utils import spawn_workers
+
+    r = spawn_workers(_run_recipe, 1, "magic_transformer", "train", ("loop.total_steps=3", "log.interval=1"),
+                      timeout=600)[0]
+    assert 5.0 < r["logs"]["train/loss"] < 8.0
+    assert "embed.weight" in r["changed"] and tuple(r["generated"]) == (1, 7)
