@@ -42,7 +42,7 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
     if sequence_parallel and not tp.active:
         raise ValueError("Sequence parallel requires an active tensor mesh with parallel.mesh.tensor > 1.")
     shard_active = parallel_mesh.has_dim("shard") and parallel_mesh.role("shard").active
-    if not shard_active and tp.active:
+    if not shard_active and tp.active and impl != "native":
         raise ValueError(f"Invalid device mesh shape {parallel_mesh.summary()['shape']}. "
                          "Tensor/sequence parallel should be used with FSDP rather than the pure DDP")
 
@@ -71,7 +71,8 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
             shard_mesh = parallel_mesh.device_mesh[dp.dim_names]._flatten("_".join(dp.dim_names))
         logger.info(f"Wrapping {type(model).__name__} with native flat FSDP over {dp.world_size} rank(s)...")
         return NativeFSDP(model, group=dp.group, device=dev, param_dtype=param_dtype,
-                          comm="fused" if comm_cfg.get("fused", True) else "nccl", shard_mesh=shard_mesh)
+                          comm="fused" if comm_cfg.get("fused", True) else "nccl", shard_mesh=shard_mesh,
+                          tp_group=tp.group if tp.active else None)
 
     if not shard_active and not tp.active:
         from torch.nn.parallel import DistributedDataParallel

@@ -58,10 +58,14 @@ class PerTokenLossGuard(LossGuard):
 
 class TokenNormedLossKit:
     def __init__(self, *, device: torch.device, dp_world_size: int, dp_group=None,
-                 loss_guard: Optional[PerTokenLossGuard] = None) -> None:
+                 loss_guard: Optional[PerTokenLossGuard] = None, loss_sum_group=None) -> None:
+        """``loss_sum_group``: ranks that each hold part of every sample's per-token losses while
+        counting the sample's tokens in full (sequence-parallel tensor ranks); loss sums are
+        additionally summed over it."""
         self.device = device
         self.dp_world_size = int(dp_world_size)
         self.dp_group = dp_group
+        self.loss_sum_group = loss_sum_group
         self.loss_guard = loss_guard
         self.reset()
 
@@ -107,6 +111,8 @@ class TokenNormedLossKit:
         if dist.is_available() and dist.is_initialized() and self.dp_world_size > 1:
             dist.all_reduce(counts, group=self.dp_group)
             dist.all_reduce(loss_sum, group=self.dp_group)
+        if self.loss_sum_group is not None:
+            dist.all_reduce(loss_sum, group=self.loss_sum_group)
         c = counts.tolist()
         if c[1] <= 0:
             raise ValueError("Accumulation window must contain at least one supervised token.")

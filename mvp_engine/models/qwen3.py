@@ -174,11 +174,14 @@ class Qwen3DecoderLayer(nn.Module):
         input RMSNorm: ``h = x + residual``.
         """
         attn = self.self_attn
+        tp = getattr(self, "_tp", None)  # tensor-parallel runtime (column / row-parallel shards)
         if residual is None:
             hn = self.input_layernorm(x)
             h = x
         else:
             hn, h = self.input_layernorm(x, residual)
+        if tp is not None:
+            hn = tp.enter(hn)
         qkv = ops.linear(hn, self.fused_weight("qkv", hn))
         Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
         q, k = ops.qk_norm_rope(
@@ -188,10 +191,16 @@ class Qwen3DecoderLayer(nn.Module):
         v = qkv[:, (Hq + Hkv) * D:].view(-1, Hkv, D)
         o = ctx.attention(q, k, v, attn.scaling)
         o = ops.linear(o.reshape(o.shape[0], Hq * D), _as_compute(attn.o_proj.weight, hn))
+        if tp is not None:
+            o = tp.exit(o)
         hn2, h2 = self.post_attention_layernorm(o, h)
+        if tp is not None:
+            hn2 = tp.enter(hn2)
         gu = ops.linear(hn2, self.fused_weight("gate_up", hn2))
         act = ops.swiglu(gu)
         out = ops.linear(act, _as_compute(self.mlp.down_proj.weight, act))
+        if tp is not None:
+            out = tp.exit(out)
         return out, h2
 
 
@@ -363,11 +372,15 @@ class Qwen3ForCausalLM(nn.Module):
         dtype = torch.bfloat16 if input_ids.is_cuda else self.lm_head.weight.dtype
         if torch.is_autocast_enabled() and not input_ids.is_cuda:
             dtype = torch.get_autocast_dtype("cpu")
-        h = self.model(input_ids, ctx, dtype)
+        tp = getattr(self, "_mvp_tp", None)
+        local = tp.seq_slice(input_ids.numel()) if tp is not None else slice(None)
+        h = self.model(input_ids.reshape(-1)[local], ctx, dtype)  # sequence parallel: this rank's tokens
         w = _as_compute(self.lm_head.weight, h)
         if labels is None and shift_labels is None:
+            if tp is not None and tp.sequence_parallel:
+                raise NotImplementedError("logits under sequence parallelism: pass labels for the loss")
             return {"logits": ops.linear(h, w).view(*input_ids.shape, -1)}
-        flat_labels = (shift_labels if shift_labels is not None else _shift_labels(labels)).reshape(-1)
+        flat_labels = (shift_labels if shift_labels is not None else _shift_labels(labels)).reshape(-1)[local]
         loss = ops.fused_linear_cross_entropy(h, w, flat_labels, self.loss_chunk_size)
         return {"loss": loss, "logits": None}
 

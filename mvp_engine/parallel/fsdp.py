@@ -60,6 +60,8 @@ class _Entry:
     numel: int
     offset: int  # in the unit's full layout
     requires_grad: bool
+    tp_partial: bool = False  # replicated over tensor parallelism, gradient summed over the tensor group
+    tp_replicated: bool = False  # same value on every tensor rank (partial or not)
 
 
 @dataclass
@@ -82,6 +84,8 @@ class FlatUnit:
     rs_event: Optional[torch.cuda.Event] = None
     rs_pending: bool = False
     views: dict[str, torch.Tensor] = field(default_factory=dict)
+    rep_end: int = 0  # entries [0, rep_end) are tensor-parallel partial (summed over the tensor group)
+    repl_end: int = 0  # entries [0, repl_end) are replicated over the tensor group (partial or complete)
 
     def local_range(self, rank: int) -> tuple[int, int]:
         return rank * self.shard, (rank + 1) * self.shard
@@ -126,10 +130,12 @@ class NativeFSDP(nn.Module):
     def __init__(self, model: nn.Module, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, param_dtype: Any = torch.bfloat16,
                  unit_classes: Optional[Iterable[str]] = None, comm: str = "nccl",
-                 shard_mesh: Any = None) -> None:
+                 shard_mesh: Any = None, tp_group: Optional[dist.ProcessGroup] = None) -> None:
         super().__init__()
         self.module = model
         self.group = group
+        self.tp_group = tp_group
+        self.tp_world = dist.get_world_size(tp_group) if (tp_group is not None and dist.is_initialized()) else 1
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if (group is not None and dist.is_initialized()) else 0
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
@@ -193,7 +199,9 @@ class NativeFSDP(nn.Module):
                     seen[id(p)].owners.append((mod, pname))
                     continue
                 unit = self.units[owning_unit(fqn)]
-                e = _Entry([fqn], [(mod, pname)], p.shape, p.numel(), 0, p.requires_grad)
+                e = _Entry([fqn], [(mod, pname)], p.shape, p.numel(), 0, p.requires_grad,
+                           tp_partial=self.tp_world > 1 and bool(getattr(p, "_mvp_tp_partial", False)),
+                           tp_replicated=self.tp_world > 1 and not getattr(p, "_mvp_tp_sharded", False))
                 seen[id(p)] = e
                 unit.entries.append(e)
         # Frozen parameters of a unit move to a sibling unit without optimizer state.
@@ -212,9 +220,15 @@ class NativeFSDP(nn.Module):
         by_entry = {id(e): params_id for params_id, e in seen.items()}
         for u in self.units:
             off = 0
+            # tensor-partial entries first, then other tensor-replicated ones, then tensor shards
+            u.entries.sort(key=lambda e: (not e.tp_partial, not e.tp_replicated))
             for e in u.entries:
                 e.offset = off
                 off += int(math.ceil(e.numel / _ALIGN) * _ALIGN)
+                if e.tp_partial:
+                    u.rep_end = off
+                if e.tp_replicated:
+                    u.repl_end = off
             u.total = off
             quantum = _ALIGN * self.world
             u.padded = max(quantum, int(math.ceil(off / quantum) * quantum))
@@ -362,17 +376,28 @@ class NativeFSDP(nn.Module):
         if not u.trainable or u.rs_pending:
             return
         u.rs_pending = True
-        if self.world == 1:
+        tp_sum = self.tp_world > 1 and u.rep_end > 0
+        if self.world == 1 and not tp_sum:
             return
         if self._comm_stream is not None:
             ev = torch.cuda.Event()
             ev.record(torch.cuda.current_stream(self.device))
             self._comm_stream.wait_event(ev)
             with torch.cuda.stream(self._comm_stream):
-                dist.reduce_scatter_tensor(u.grad_shard, u.grad, op=dist.ReduceOp.SUM, group=self.group)
+                if tp_sum:
+                    dist.all_reduce(u.grad[:u.rep_end], group=self.tp_group)
+                if self.world > 1:
+                    dist.reduce_scatter_tensor(u.grad_shard, u.grad, op=dist.ReduceOp.SUM, group=self.group)
                 u.rs_event = torch.cuda.Event()
                 u.rs_event.record(self._comm_stream)
         else:
+            if tp_sum:
+                part = u.grad[:u.rep_end].detach().clone()
+                dist.all_reduce(part, group=self.tp_group)
+                with torch.no_grad():
+                    u.grad[:u.rep_end].copy_(part)
+            if self.world == 1:
+                return
             buf = u.grad.detach().clone()
             dist.all_reduce(buf, group=self.group)
             lo, hi = u.local_range(self.rank)
@@ -437,6 +462,14 @@ class NativeFSDP(nn.Module):
 
         parts = [ops.sumsq(g) for g in self.grad_shards()]
         nsq = torch.stack(parts).sum().reshape(1) if parts else torch.zeros(1, device=self.device)
+        if self.tp_world > 1:
+            # Replicated ranges are identical on every tensor rank (partial ones after their
+            # all-reduce): count them once in the sum over the tensor group.
+            rep = [ops.sumsq(u.grad_shard[:max(0, min(u.repl_end, hi) - lo)]) for u in self.units
+                   if u.trainable and u.repl_end > 0 for lo, hi in [u.local_range(self.rank)] if u.repl_end > lo]
+            if rep:
+                nsq = nsq - torch.stack(rep).sum().reshape(1) * (1.0 - 1.0 / self.tp_world)
+            dist.all_reduce(nsq, group=self.tp_group)
         if self.world > 1:
             dist.all_reduce(nsq, group=self.group)
         self._norm_sq = nsq

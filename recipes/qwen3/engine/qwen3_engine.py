@@ -49,7 +49,10 @@ class Qwen3Engine(Engine):
         # token counts / loss sums reduce over every rank that holds part of a step's tokens
         # (data x context parallel ranks)
         red = self.parallel_mesh.dp_cp
-        self.token_loss_kit = TokenNormedLossKit(device=self.device, dp_world_size=red.world_size, dp_group=red.group)
+        tp = self.parallel_mesh.tp
+        sp = tp.active and bool(self.config.parallel.backend_kwargs.sequence_parallel)
+        self.token_loss_kit = TokenNormedLossKit(device=self.device, dp_world_size=red.world_size, dp_group=red.group,
+                                                 loss_sum_group=tp.group if sp else None)
         o = self.config.optim
         self.token_loss_kit.build_loss_guard(spike_multiplier=o.loss_spike_skip_multiplier,
                                              window_size=int(o.loss_spike_skip_window_size),
@@ -151,6 +154,7 @@ class Qwen3Engine(Engine):
             freeze_llm=bool(self.config.model.freeze_llm))
         if cp_len:  # each context rank does 1/cp of the row's work
             flops /= self.parallel_mesh.cp.world_size
+        flops /= self.parallel_mesh.tp.world_size  # and each tensor rank 1/tp
         self.mfu_kit.accumulate_microbatch(model_flops=flops)
         ctx.outputs = {"loss": outputs["loss"], "logs": {"train/loss": 0}}
 
