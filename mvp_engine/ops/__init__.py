@@ -457,3 +457,19 @@ def sumsq(x: torch.Tensor) -> torch.Tensor:
     if not _native(x):
         return x.float().pow(2).sum()
     return _ext.ext().sumsq(x.contiguous())
+
+
+# ------------------------------------------------------------- peer collectives
+def peer_reduce_scatter(peer_bufs: list[int], peer_slots: list[int], my_slots: int, rank: int, offset: int,
+                        shard: int, seq: int, out: torch.Tensor, scale: float = 1.0,
+                        sumsq: Optional[torch.Tensor] = None, timeout_s: float = 10.0) -> None:
+    """``out = scale * sum over ranks of buf_r[offset + rank*shard : +shard]`` pulled over NVLink from the
+    peers' symmetric buffers, after every rank has published sequence number ``seq`` (bounded wait)."""
+    _ext.ext().peer_reduce_scatter(peer_bufs, peer_slots, my_slots, rank, offset, shard, seq, scale, out, sumsq,
+                                   _ext.status_buffer(out.device).data_ptr(), int(timeout_s * 1e9))
+
+
+def peer_barrier(peer_slots: list[int], my_slots: int, rank: int, seq: int, timeout_s: float = 10.0) -> None:
+    """Stream-ordered device barrier over the peers' signal slots (bounded wait)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _ext.ext().peer_barrier(peer_slots, my_slots, rank, seq, _ext.status_buffer(dev).data_ptr(), int(timeout_s * 1e9))

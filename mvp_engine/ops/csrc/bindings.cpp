@@ -42,6 +42,13 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
                                           const c10::optional<torch::Tensor>& dv_out,
                                           const c10::optional<torch::Tensor>& cu_seqlens_k);
 
+void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vector<int64_t>& peer_slots,
+                         int64_t my_slots, int64_t rank, int64_t offset, int64_t shard, int64_t seq, double scale,
+                         torch::Tensor& out, const c10::optional<torch::Tensor>& sumsq, int64_t status_ptr,
+                         int64_t timeout_ns);
+void peer_barrier(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                  int64_t status_ptr, int64_t timeout_ns);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mvp_engine sm_100a kernels";
   m.def("gemm", &gemm_sm100, "tcgen05 bf16 GEMM C (+)= A * B^T with K- or MN-major operands");
@@ -60,6 +67,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &flash_attn_fwd, "varlen flash attention forward (tcgen05)", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"),
         py::arg("cu_seqlens_k") = py::none());
+  m.def("peer_reduce_scatter", &peer_reduce_scatter,
+        "pull reduce-scatter of a symmetric fp32 buffer over NVLink peers (bounded waits)");
+  m.def("peer_barrier", &peer_barrier, "device-side barrier over peer signal slots (bounded)");
   m.def("flash_attn_bwd", &flash_attn_bwd, "varlen flash attention backward (tcgen05)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("cu_seqlens"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"), py::arg("dk_out") = py::none(),

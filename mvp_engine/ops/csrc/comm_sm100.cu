@@ -1,0 +1,198 @@
+// Collectives over NVLink peer memory for the native data-parallel runtime.
+//
+// Gradient reduce-scatter by pulling (replaces NCCL's reduce-scatter of the
+// flat fp32 gradient buffer of one unit):
+//   * every rank keeps the full fp32 gradient of every unit in one symmetric
+//     allocation (same offsets on every rank, peers mapped into this process);
+//   * when a unit's backward is done, the kernel on each rank first publishes
+//     "unit ready, sequence s" into every peer's signal slots (system-scope
+//     release after a system fence), then waits until every peer has
+//     published s into its own slots (system-scope acquire, bounded by
+//     %globaltimer), then sums its shard slice over all ranks with 16-byte
+//     loads straight from peer memory and writes the fp32 gradient shard,
+//     optionally scaled, and its sum of squares (for the global-norm clip).
+// The wire traffic equals a ring reduce-scatter's ((W-1)/W of the unit per
+// rank) but there is no intermediate buffer, no extra pass over HBM and the
+// squared norm comes for free.
+//
+// A wait that runs out (a peer that never arrives) sets the status word to
+// kTimeoutPeer and returns without reading peer memory; the host raises.
+// The bound (timeout_ns) is a launch argument: 10 s in training, far above
+// the millisecond skew between ranks that run the same unit order.
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace mvp {
+namespace comm {
+
+constexpr int kMaxRanks = 8;
+
+struct RsParams {
+  const float* peers[kMaxRanks];        // base of the symmetric gradient buffer on each rank
+  unsigned long long* peer_slots[kMaxRanks];  // base of each rank's signal slots [kMaxRanks]
+  unsigned long long* my_slots;         // this rank's slots, written by the peers
+  int64_t offset;                        // element offset of the unit in the buffer
+  int64_t shard;                         // elements per rank (multiple of 4)
+  int rank, world;
+  unsigned long long seq;
+  float scale;
+  float* out;                            // [shard] fp32
+  float* sumsq;                          // optional [1] fp32 accumulator
+  int* status;
+  unsigned long long timeout_ns;         // bound of every wait for a peer
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) rs_pull_kernel(RsParams p) {
+  __shared__ int s_ok;
+  __shared__ float s_red[8];
+  // 1. publish: this rank's unit is complete (its producing kernels finished before this one started)
+  if (blockIdx.x == 0 && threadIdx.x < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_slots[threadIdx.x] + p.rank, p.seq);
+  }
+  // 2. wait for every peer's publication, bounded
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < p.world && ok; ++r) {
+      while (ld_acquire_sys(p.my_slots + r) < p.seq) {
+        if (globaltimer() - t0 > p.timeout_ns) {
+          atomicCAS(p.status, 0, kTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  // 3. pull and sum this rank's slice
+  const int64_t base = p.offset + static_cast<int64_t>(p.rank) * p.shard;
+  const int64_t n4 = p.shard / 4;
+  float local_sq = 0.f;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < p.world) {
+        const float4 v = reinterpret_cast<const float4*>(p.peers[r] + base)[i];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    acc.x *= p.scale;
+    acc.y *= p.scale;
+    acc.z *= p.scale;
+    acc.w *= p.scale;
+    reinterpret_cast<float4*>(p.out)[i] = acc;
+    local_sq += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+  }
+  if (p.sumsq != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) local_sq += __shfl_xor_sync(0xffffffffu, local_sq, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = local_sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < blockDim.x / 32; ++w) t += s_red[w];
+      atomicAdd(p.sumsq, t);
+    }
+  }
+}
+
+// Device-side barrier over the same slots (used before gradient buffers are reused): publish
+// seq to every peer, wait for every peer's seq.  One block.
+__global__ void slots_barrier_kernel(RsParams p) {
+  if (threadIdx.x < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_slots[threadIdx.x] + p.rank, p.seq);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < p.world; ++r) {
+      while (ld_acquire_sys(p.my_slots + r) < p.seq) {
+        if (globaltimer() - t0 > p.timeout_ns) {
+          atomicCAS(p.status, 0, kTimeoutPeer);
+          return;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+}
+
+RsParams make_params(const std::vector<int64_t>& peer_bufs, const std::vector<int64_t>& peer_slots,
+                     int64_t my_slots, int rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns) {
+  TORCH_CHECK(timeout_ns > 0, "peer collectives need a positive wait bound");
+  const int world = static_cast<int>(peer_bufs.size());
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "peer collectives support 1..8 ranks");
+  TORCH_CHECK(static_cast<int>(peer_slots.size()) == world, "one signal base per rank");
+  TORCH_CHECK(rank >= 0 && rank < world, "rank out of range");
+  RsParams p{};
+  for (int r = 0; r < world; ++r) {
+    p.peers[r] = reinterpret_cast<const float*>(peer_bufs[r]);
+    p.peer_slots[r] = reinterpret_cast<unsigned long long*>(peer_slots[r]);
+  }
+  p.my_slots = reinterpret_cast<unsigned long long*>(my_slots);
+  p.rank = rank;
+  p.world = world;
+  p.seq = static_cast<unsigned long long>(seq);
+  p.status = reinterpret_cast<int*>(status_ptr);
+  p.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+  return p;
+}
+
+}  // namespace comm
+}  // namespace mvp
+
+// out[i] = scale * sum_r peer_r[offset + rank*shard + i]; optional sumsq += ||out||^2.
+void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vector<int64_t>& peer_slots,
+                         int64_t my_slots, int64_t rank, int64_t offset, int64_t shard, int64_t seq, double scale,
+                         torch::Tensor& out, const c10::optional<torch::Tensor>& sumsq, int64_t status_ptr,
+                         int64_t timeout_ns) {
+  using namespace mvp::comm;
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= shard,
+              "peer_reduce_scatter: fp32 contiguous output of at least `shard` elements");
+  TORCH_CHECK(shard % 4 == 0 && offset % 4 == 0, "peer_reduce_scatter: 16-byte aligned slices");
+  const at::cuda::CUDAGuard guard(out.device());
+  RsParams p = make_params(peer_bufs, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  p.offset = offset;
+  p.shard = shard;
+  p.scale = static_cast<float>(scale);
+  p.out = out.data_ptr<float>();
+  p.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
+  // Enough CTAs to keep NVLink busy, few enough to leave the SMs to the overlapped backward.
+  const int64_t n4 = shard / 4;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, (n4 + 255) / 256)));
+  rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void peer_barrier(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                  int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  std::vector<int64_t> dummy(peer_slots.size(), 0);
+  RsParams p = make_params(dummy, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  slots_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -138,9 +138,79 @@ def bench_attention(T: int, Hq: int, Hkv: int, iters: int, lo: int = 256, hi: in
     print(json.dumps(row), flush=True)
 
 
+def bench_peer_rs(mbytes: int, iters: int) -> None:
+    """Pull reduce-scatter of one fp32 gradient unit over NVLink vs NCCL's reduce-scatter (launch with
+    torchrun, one rank per GPU).  Device time per call, max over ranks; roofline = bytes this rank pulls
+    from its peers ((W-1)/W of the unit) at the measured 770 GB/s per-direction peer copy rate."""
+    import os
+
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+
+    from mvp_engine import ops
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.ops import _ext
+
+    initialize_process_group()
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n = (mbytes << 20) // 4 // (64 * world) * (64 * world)
+    shard = n // world
+    buf = symm.empty(n, dtype=torch.float32, device=dev)
+    buf.normal_()
+    slots = symm.empty(8, dtype=torch.int64, device=dev)
+    slots.zero_()
+    torch.cuda.synchronize()
+    hb, hs = symm.rendezvous(buf, dist.group.WORLD), symm.rendezvous(slots, dist.group.WORLD)
+    hs.barrier()
+    peers, pslots = [int(x) for x in hb.buffer_ptrs], [int(x) for x in hs.buffer_ptrs]
+    out = torch.empty(shard, device=dev)
+    seq = [0]
+
+    def ours():
+        seq[0] += 1
+        ops.peer_reduce_scatter(peers, pslots, slots.data_ptr(), rank, 0, shard, seq[0], out)
+
+    plain = torch.empty(n, device=dev).normal_()
+
+    def nccl():
+        dist.reduce_scatter_tensor(out, plain)
+
+    res = {}
+    for name, fn in (("peer_pull", ours), ("nccl", nccl)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ts = []
+        for _ in range(iters):
+            dist.barrier()
+            torch.cuda.synchronize()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            fn()
+            e_.record()
+            torch.cuda.synchronize()
+            ts.append(s_.elapsed_time(e_))
+        t = torch.tensor([sorted(ts)[len(ts) // 2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = float(t)
+    _ext.check_status(dev)
+    wire = (world - 1) / world * n * 4
+    if rank == 0:
+        print(json.dumps({"kernel": "rs_pull_kernel", "world": world, "unit_mb": round(n * 4 / 2**20, 1),
+                          "peer_pull_ms": round(res["peer_pull"], 4), "nccl_ms": round(res["nccl"], 4),
+                          "peer_pull_gbs": round(wire / res["peer_pull"] / 1e6, 1),
+                          "nccl_gbs": round(wire / res["nccl"] / 1e6, 1),
+                          "roofline_frac_of_770": round(wire / res["peer_pull"] / 1e6 / 770.0, 3)}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention"])
+    ap.add_argument("what", choices=["gemm", "attention", "peer_rs"])
+    ap.add_argument("--mbytes", type=int, default=768, help="peer_rs: unit size in MiB")
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--heads", default="32,8")
     ap.add_argument("--shape", default=None, help="M,N,K")
@@ -155,6 +225,8 @@ def main() -> None:
             M, N, K = (int(v) for v in args.shape.split(","))
             shapes = {"custom": (M, N, K)}
         bench_gemm(shapes, args.iters)
+    elif args.what == "peer_rs":
+        bench_peer_rs(args.mbytes, args.iters)
     elif args.what == "attention":
         hq, hkv = (int(v) for v in args.heads.split(","))
         bench_attention(args.tokens, hq, hkv, args.iters)

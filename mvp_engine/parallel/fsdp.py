@@ -40,6 +40,7 @@ flat shards (one unit at a time, offloaded to CPU).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Any, Callable, Iterable, Optional
 
@@ -62,6 +63,17 @@ class _Entry:
     requires_grad: bool
     tp_partial: bool = False  # replicated over tensor parallelism, gradient summed over the tensor group
     tp_replicated: bool = False  # same value on every tensor rank (partial or not)
+
+
+@dataclass
+class _PeerState:
+    buf: torch.Tensor  # symmetric fp32 gradient buffer of all trainable units
+    slots: torch.Tensor  # symmetric int64 signal slots [8]
+    handles: tuple
+    peer_bufs: list[int]
+    peer_slots: list[int]
+    my_slots: int
+    offsets: dict[int, int]
 
 
 @dataclass
@@ -233,7 +245,61 @@ class NativeFSDP(nn.Module):
             quantum = _ALIGN * self.world
             u.padded = max(quantum, int(math.ceil(off / quantum) * quantum))
             u.shard = u.padded // self.world
+        self._peer = self._setup_peer_collectives()
+        for u in self.units:
             self._materialise(u, {id(e): params[by_entry[id(e)]] for e in u.entries})
+
+    def _setup_peer_collectives(self) -> Optional["_PeerState"]:
+        """Gradient buffers in one symmetric (peer-mapped) allocation for the pull reduce-scatter kernel.
+
+        Used for ``comm="fused"`` on CUDA with 2..8 data-parallel ranks; anything else (or a setup
+        failure, reported once) keeps NCCL's reduce-scatter.
+        """
+        if self.comm != "fused" or self.world <= 1 or self.device.type != "cuda" or self.world > 8:
+            return None
+        if os.environ.get("MVP_FUSED_COMM", "1") == "0":
+            return None
+        try:
+            import torch.distributed._symmetric_memory as symm
+
+            try:
+                if symm.get_backend(self.device) != "CUDA":
+                    symm.set_backend("CUDA")
+            except Exception:  # noqa: BLE001 - older / newer APIs: keep the default backend
+                pass
+            group = self.group if self.group is not None else dist.group.WORLD
+            try:
+                symm.enable_symm_mem_for_group(group.group_name)
+            except Exception:  # noqa: BLE001 - not needed (or not present) on newer torch
+                pass
+            total = sum(u.padded for u in self.units if u.trainable)
+            buf = symm.empty(max(total, 4), dtype=torch.float32, device=self.device)
+            buf.zero_()
+            slots = symm.empty(8, dtype=torch.int64, device=self.device)
+            slots.zero_()
+            torch.cuda.synchronize(self.device)
+            h_buf = symm.rendezvous(buf, group)
+            h_slots = symm.rendezvous(slots, group)
+            h_slots.barrier()
+            off, offsets = 0, {}
+            for u in self.units:
+                if u.trainable:
+                    offsets[u.index] = off
+                    off += u.padded
+            return _PeerState(buf=buf, slots=slots, handles=(h_buf, h_slots),
+                              peer_bufs=[int(x) for x in h_buf.buffer_ptrs],
+                              peer_slots=[int(x) for x in h_slots.buffer_ptrs],
+                              my_slots=int(slots.data_ptr()), offsets=offsets)
+        except Exception as exc:  # noqa: BLE001 - fall back to NCCL, loudly
+            from ..utils.log import simple_info
+
+            simple_info(f"native FSDP: peer-memory reduce-scatter unavailable ({type(exc).__name__}: {exc}); "
+                        "using NCCL reduce-scatter", level="warning")
+            return None
+
+    def _next_seq(self) -> int:
+        self._seq = getattr(self, "_seq", 0) + 1
+        return self._seq
 
     def _materialise(self, u: FlatUnit, src: dict[int, torch.Tensor]) -> None:
         dev = self.device
@@ -261,7 +327,11 @@ class NativeFSDP(nn.Module):
                     if a < b:
                         u.master[a - lo:b - lo].copy_(flat[a - e.offset:b - e.offset].float())
         if u.trainable:
-            u.grad = torch.zeros(u.padded, dtype=torch.float32, device=dev)
+            if self._peer is not None:
+                o = self._peer.offsets[u.index]
+                u.grad = self._peer.buf[o:o + u.padded]
+            else:
+                u.grad = torch.zeros(u.padded, dtype=torch.float32, device=dev)
             u.grad_shard = u.grad if self.world == 1 else torch.zeros(u.shard, dtype=torch.float32, device=dev)
             u.exp_avg = torch.zeros_like(u.master)
             u.exp_avg_sq = torch.zeros_like(u.master)
@@ -386,7 +456,13 @@ class NativeFSDP(nn.Module):
             with torch.cuda.stream(self._comm_stream):
                 if tp_sum:
                     dist.all_reduce(u.grad[:u.rep_end], group=self.tp_group)
-                if self.world > 1:
+                if self.world > 1 and self._peer is not None:
+                    from .. import ops as _ops
+
+                    pe = self._peer
+                    _ops.peer_reduce_scatter(pe.peer_bufs, pe.peer_slots, pe.my_slots, self.rank,
+                                             pe.offsets[u.index], u.shard, self._next_seq(), u.grad_shard)
+                elif self.world > 1:
                     dist.reduce_scatter_tensor(u.grad_shard, u.grad, op=dist.ReduceOp.SUM, group=self.group)
                 u.rs_event = torch.cuda.Event()
                 u.rs_event.record(self._comm_stream)
@@ -500,6 +576,12 @@ class NativeFSDP(nn.Module):
 
     def after_optimizer_step(self) -> None:
         """Zero gradient buffers, reset per-step state and start next step's all-gathers."""
+        if self._peer is not None:
+            # peers may still be pulling from this rank's gradient buffers: meet them first
+            from .. import ops as _ops
+
+            pe = self._peer
+            _ops.peer_barrier(pe.peer_slots, pe.my_slots, self.rank, self._next_seq())
         for u in self.units:
             if u.trainable:
                 u.grad.zero_()
