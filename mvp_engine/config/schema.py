@@ -156,3 +156,6 @@ class BaseEngineConfig(BaseModel):
     optim: BaseOptimConfig = Field(default_factory=BaseOptimConfig)
     loop: BaseLoopConfig = Field(default_factory=BaseLoopConfig)
     checkpoint: BaseCheckpointConfig = Field(default_factory=BaseCheckpointConfig)
+    # A checkpoint directory to resume from, or "latest": the newest complete checkpoint of this
+    # project (none -> fresh start), for automatic restarts after a failure.
+    resume: Optional[str] = None

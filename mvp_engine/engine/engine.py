@@ -57,6 +57,25 @@ logging.captureWarnings(True)
 logging.basicConfig(level=os.environ.get("LOGLEVEL", "ERROR").upper())
 
 
+COMPLETE_MARKER = "COMPLETE"
+
+
+def latest_complete_checkpoint(root: Union[str, PathLike]) -> Optional[str]:
+    """Newest ``<policy>_<n>`` directory under ``root`` holding the completion marker (None if none).
+
+    A checkpoint interrupted mid-save (or damaged afterwards and stripped of its marker) is skipped,
+    so an automatic restart resumes from the last checkpoint that was fully written.
+    """
+    root = Path(root)
+    if not root.is_dir():
+        return None
+    cands = [p for p in root.iterdir() if p.is_dir() and p.name.split("_")[-1].isdigit()]
+    for p in sorted(cands, key=lambda p: int(p.name.split("_")[-1]), reverse=True):
+        if (p / COMPLETE_MARKER).is_file():
+            return str(p)
+    return None
+
+
 @dataclass
 class TrainStepContext:
     """Mutable state for one training micro-batch."""
@@ -242,6 +261,8 @@ class Engine(ABC):
                         hf_enable=self.config.checkpoint.hf_enable)
         if dist.is_initialized():
             dist.barrier()
+        if is_main_process():  # written last: a checkpoint without it is incomplete and never resumed from
+            (cur / COMPLETE_MARKER).write_text(str(self.step))
 
     def load(self, ckpt_path: Union[str, PathLike], restore_training_state: bool = True,
              restore_rng_state: bool = True) -> None:
@@ -284,8 +305,13 @@ class Engine(ABC):
         logger.info("Building GradientScaler...")
         self.scaler = GradientScaler(enabled=self.dtype != torch.float32, dtype=self.dtype, device=self.device_type)
         resume = getattr(self.config, "resume", None)
+        if resume == "latest":  # newest complete checkpoint of this project, if any
+            resume = latest_complete_checkpoint(self.project_dir / "checkpoints")
         if resume is not None:
             self.load(resume, restore_training_state=True, restore_rng_state=True)
+        from ..distributed.watchdog import start_default_watchdog
+
+        self._watchdog = start_default_watchdog()
         logger.info("Initializing Timer...")
         self.timer = Timer(total_progress=self.total_steps, window_size=self.config.log.timer_window_size)
 
@@ -306,6 +332,8 @@ class Engine(ABC):
                         prepared = self.train_pre_step(ctx)
                         if prepared is not None and prepared is not ctx:
                             ctx.data = prepared
+                    if getattr(self, "_watchdog", None) is not None:
+                        self._watchdog.check()  # a silent peer ends the run before the next collectives
                     with self.timer.scope("exec_time"):
                         self.train_exec_step(ctx)
                     if not ctx.optimizer_step_completed:
@@ -394,6 +422,8 @@ class Engine(ABC):
         logger.log_metrics(self.last_logs, step=self.step, total_steps=self.total_steps)
 
     def after_train(self) -> None:
+        if getattr(self, "_watchdog", None) is not None:
+            self._watchdog.stop()
         self.save(force=True and not self.config.dev_mode)
         logger.info("Training finished!")
         logger.destroy()

@@ -1,0 +1,169 @@
+"""Failure detection on host ranks (gloo / store / files): nothing here touches a GPU.
+
+* a rank that exits without warning is reported by the heartbeat watchdog of the survivors;
+* a collective whose peer never joins ends with an error at the process-group timeout;
+* a store key that is dropped makes its waiter time out instead of blocking;
+* a checkpoint whose save was interrupted (or damaged) is skipped by ``resume: latest``.
+"""
+
+import multiprocessing as mp
+import os
+import time
+from pathlib import Path
+
+import pytest
+import torch
+
+from mvp_engine.testing.utils import find_free_port
+
+
+def _watch_worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), MVP_PG_TIMEOUT_S="20")
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.distributed.watchdog import HeartbeatWatchdog, PeerFailureError
+    from mvp_engine.testing.faults import exit_abruptly
+    from torch.distributed.distributed_c10d import _get_default_store
+
+    initialize_process_group()
+    wd = HeartbeatWatchdog(_get_default_store(), rank, world, interval_s=0.2, timeout_s=1.5).start()
+    dist.barrier()
+    if rank == world - 1:
+        time.sleep(0.5)
+        exit_abruptly()
+    t0 = time.monotonic()
+    while time.monotonic() - t0 < 15:
+        try:
+            wd.check()
+        except PeerFailureError as e:
+            q.put((rank, e.ranks, round(time.monotonic() - t0, 2)))
+            wd.stop()
+            return
+        time.sleep(0.1)
+    q.put((rank, [], None))
+
+
+def test_heartbeat_reports_a_rank_that_exits():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = find_free_port()
+    world = 3
+    procs = [ctx.Process(target=_watch_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=60) for _ in range(world - 1)]
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert procs[-1].exitcode == 17
+    for rank, failed, dt in got:
+        assert failed == [world - 1], (rank, failed)
+        assert dt is not None and dt < 10
+
+
+def _timeout_worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), MVP_PG_TIMEOUT_S="3")
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+
+    initialize_process_group()
+    dist.barrier()
+    if rank == 1:
+        time.sleep(12)  # never joins the collective below in time
+        q.put((rank, "slept", None))
+        return
+    t0 = time.monotonic()
+    try:
+        x = torch.ones(4)
+        dist.all_reduce(x)
+        q.put((rank, "completed", None))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, type(e).__name__, round(time.monotonic() - t0, 2)))
+
+
+def test_collective_with_a_missing_peer_ends_at_the_pg_timeout():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = find_free_port()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (what, dt) for r, what, dt in (q.get(timeout=60) for _ in range(2))}
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    what, dt = res[0]
+    assert what != "completed" and dt is not None and dt < 11
+
+
+def test_dropped_store_key_times_out():
+    from datetime import timedelta
+
+    from torch.distributed import TCPStore
+
+    from mvp_engine.testing.faults import drop_store_key
+
+    store = TCPStore("127.0.0.1", find_free_port(), 1, True, timeout=timedelta(seconds=2))
+    store.set("ready/0", "1")
+    assert drop_store_key(store, "ready/0")
+    t0 = time.monotonic()
+    with pytest.raises(Exception):
+        store.wait(["ready/0"], timedelta(seconds=1))
+    assert time.monotonic() - t0 < 5
+
+
+def test_resume_latest_skips_incomplete_checkpoints(tmp_path):
+    from mvp_engine.engine.engine import COMPLETE_MARKER, latest_complete_checkpoint
+    from mvp_engine.testing.faults import corrupt_file, remove_completion_marker
+
+    root = tmp_path / "checkpoints"
+    for step in (10, 20, 30):
+        d = root / f"iter_{step}"
+        (d / "model").mkdir(parents=True)
+        (d / "model" / "shard.bin").write_bytes(os.urandom(64))
+        (d / COMPLETE_MARKER).write_text(str(step))
+    assert latest_complete_checkpoint(root) == str(root / "iter_30")
+    corrupt_file(root / "iter_30" / "model" / "shard.bin")
+    remove_completion_marker(root / "iter_30")  # a torn save never gets its marker
+    assert latest_complete_checkpoint(root) == str(root / "iter_20")
+    (root / "iter_40").mkdir()  # interrupted before anything was written
+    assert latest_complete_checkpoint(root) == str(root / "iter_20")
+    assert latest_complete_checkpoint(tmp_path / "none") is None
+
+
+def _resume_run(rank, world, port, out_dir, steps, resume):
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = Path(__file__).resolve().parent.parent / "recipes" / "magic_transformer"
+    import_recipe_modules(root)
+    over = [f"loop.total_steps={steps}", "checkpoint.interval=2", "checkpoint.keep_n=5", "log.interval=1",
+            "log.backends=[terminal]"]
+    if resume:
+        over.append("resume=latest")
+    cfg = load_smoke_test_config(root, "train", output_dir=Path(out_dir), run_id="fixed-run",
+                                 config_overrides=tuple(over))
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    eng.before_train()
+    start = eng.step
+    eng.do_train()
+    eng.after_train()
+    return start, eng.step
+
+
+def test_engine_resumes_from_latest_complete_checkpoint(tmp_path):
+    from mvp_engine.testing import spawn_workers
+
+    first = spawn_workers(_resume_run, 1, str(tmp_path), 4, False, timeout=300)[0]
+    assert first == (0, 4)
+    ckpts = sorted(p.name for p in (tmp_path / "fixed-run" / "checkpoints").iterdir())
+    assert "iter_4" in ckpts
+    second = spawn_workers(_resume_run, 1, str(tmp_path), 6, True, timeout=300)[0]
+    assert second == (4, 6)
