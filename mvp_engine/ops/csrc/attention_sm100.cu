@@ -17,13 +17,19 @@
 // (natural-log LSE of the scaled logits, for the backward pass).
 //
 // Forward CTA = one 128-row query block of one head (grid = q blocks x Hq):
-//   warps 0-3  softmax: each thread owns one query row = one TMEM lane; it
-//              reads S from TMEM, applies the document mask, keeps a running
-//              max / sum, rescales O in TMEM only when the max grows by more
-//              than 2^8 (lazy rescale), and writes P (bf16) into a 128-byte
-//              swizzled shared-memory tile that feeds the next MMA.
-//   warp 4     TMA producer: Q once, then K/V blocks into a 2-deep ring.
-//   warp 5     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before waiting for
+//   warps 0-7  softmax, two warpgroups: thread (warp % 4, lane) owns query row
+//              r = TMEM lane, warpgroup h its keys 64h .. 64h+63 of each
+//              block.  Each reads its half of S from TMEM, applies the
+//              document mask (skipped for blocks entirely inside the row's
+//              window), exchanges its partial row max with the other half
+//              through shared memory, keeps the running max and its partial
+//              sum, rescales its half of O in TMEM only when the max grows by
+//              more than 2^8 (lazy rescale), and writes its half of P (bf16)
+//              into the 128-byte swizzled shared-memory tile of the next MMA.
+//              Two warps per SM sub-partition hide the exp2 / TMEM latency
+//              that a single warpgroup cannot.
+//   warp 8     TMA producer: Q once, then K/V blocks into a 2-deep ring.
+//   warp 9     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before waiting for
 //              P_j so the tensor core overlaps the softmax; then O += P_j V_j.
 // TMEM: S double buffer (2 x 128 columns) + O (128 columns).
 #include <cuda.h>
@@ -108,7 +114,11 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t base, int s) {
   return make_smem_desc_sw128(base + s * 2048, CHUNK_BYTES, 1024);
 }
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int kFwdThreads = 320;  // 8 softmax warps + TMA warp + MMA warp
+constexpr int kTmaWarp = 8;
+constexpr int kMmaWarp = 9;
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -129,6 +139,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* done_bar = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* xchg = bars + 16;     // [2] the two softmax halves exchanged their row maxima (256 arrivals)
+  uint64_t* lsum_bar = bars + 18; // the two halves exchanged their row sums (256 arrivals)
+  float* xmax = reinterpret_cast<float*>(bars + 20);  // [2 parity][2 halves][128 rows] maxima, then [2][128] sums
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -152,15 +165,18 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[b], 1);
       mbar_init(&kv_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
+      mbar_init(&s_empty[b], 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
+    mbar_init(&xchg[0], 256);
+    mbar_init(&xchg[1], 256);
+    mbar_init(lsum_bar, 256);
     mbar_init(o_ready, 1);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -171,7 +187,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tS = tmem;         // [2] x 128 columns
   const uint32_t tO = tmem + 256;   // 128 columns
 
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     // --------------------------------------------------------------- TMA
     if (elect_one_sync()) {
       tma_prefetch_desc(&tmQ);
@@ -215,7 +231,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // --------------------------------------------------------------- MMA
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BLK, BLK, false, false);
@@ -266,12 +282,13 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ----------------------------------------------------------- softmax
-    const int r = warp * 32 + lane;
+    const int r = (warp & 3) * 32 + lane;  // query row = TMEM lane
+    const int half = warp >> 2;             // keys / O columns 64*half .. 64*half+63
     const int i = q0 + r;
     const bool valid = i < p.T;
     int start_i = 0, hi_i = -1;  // allowed keys start_i .. hi_i
     if (valid) key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, i, start_i, hi_i);
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_blocks; ++j) {
@@ -280,26 +297,41 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[b], ph, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      float s[BLK];
+      float s[64];
 #pragma unroll
-      for (int c = 0; c < BLK / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t rr[32];
-        tmem_ld_32x32b_x32(tS + b * BLK + lane_addr + c * 32, rr);
+        tmem_ld_32x32b_x32(tS + b * BLK + lane_addr + half * 64 + c * 32, rr);
         tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(rr[t]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[b]);
-      const int k0 = kv_lo + j * BLK;
+      const int k0 = kv_lo + j * BLK + half * 64;
       float mb = -INFINITY;
+      if (valid && k0 >= start_i && k0 + 63 <= hi_i) {  // whole half-block visible: no mask
 #pragma unroll
-      for (int c = 0; c < BLK; ++c) {
-        const int key = k0 + c;
-        const bool allowed = valid && key >= start_i && key <= hi_i;
-        s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
-        mb = fmaxf(mb, s[c]);
+        for (int c = 0; c < 64; ++c) {
+          s[c] *= p.scale_log2;
+          mb = fmaxf(mb, s[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const int key = k0 + c;
+          const bool allowed = valid && key >= start_i && key <= hi_i;
+          s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
+          mb = fmaxf(mb, s[c]);
+        }
       }
+      // row max over both halves (bounded mbarrier exchange: a half that gave up cannot hang the other)
+      float* xm = xmax + (j & 1) * 256;
+      xm[half * 128 + r] = mb;
+      mbar_arrive(&xchg[j & 1]);
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&xchg[j & 1], ph, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
+      mb = fmaxf(mb, xm[(half ^ 1) * 128 + r]);
       const float m_new = fmaxf(m, mb);
       float m_use = m, alpha = 1.f;
       if (m_new > m + kRescaleThreshold || (m == -INFINITY && m_new != -INFINITY)) {
@@ -314,39 +346,36 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
+          for (int c = 0; c < 4; ++c) {
             uint32_t rr[16];
-            tmem_ld_32x32b_x16(tO + lane_addr + c * 16, rr);
+            tmem_ld_32x32b_x16(tO + lane_addr + half * 64 + c * 16, rr);
             tmem_wait_ld();
 #pragma unroll
             for (int t = 0; t < 16; ++t) rr[t] = __float_as_uint(__uint_as_float(rr[t]) * alpha);
-            tmem_st_32x32b_x16(tO + lane_addr + c * 16, rr);
+            tmem_st_32x32b_x16(tO + lane_addr + half * 64 + c * 16, rr);
           }
           tmem_wait_st();
         }
       }
       m = m_use;
       float rowsum = 0.f;
-      // P = exp2(s - m) as bf16 into the swizzled K-major tile: row r, key chunk c.
+      // P = exp2(s - m) as bf16 into this half's 64-key chunk of the swizzled K-major tile.
+      uint8_t* row_base = sP + half * CHUNK_BYTES + r * 128;
+      const bool live = m != -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint8_t* row_base = sP + c * CHUNK_BYTES + r * 128;
+      for (int u = 0; u < 8; ++u) {
+        float e[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          float e[8];
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const float x = s[c * 64 + u * 8 + t];
-            e[t] = (m == -INFINITY || x == -INFINITY) ? 0.f : exp2f(x - m);
-            rowsum += e[t];
-          }
-          uint4 pk;
-          pk.x = pack_bf16x2(e[0], e[1]);
-          pk.y = pack_bf16x2(e[2], e[3]);
-          pk.z = pack_bf16x2(e[4], e[5]);
-          pk.w = pack_bf16x2(e[6], e[7]);
-          *reinterpret_cast<uint4*>(row_base + ((u ^ (r & 7)) << 4)) = pk;
+        for (int t = 0; t < 8; ++t) {
+          e[t] = live ? exp2f(s[u * 8 + t] - m) : 0.f;  // exp2f(-inf) = 0 for masked keys
+          rowsum += e[t];
         }
+        uint4 pk;
+        pk.x = pack_bf16x2(e[0], e[1]);
+        pk.y = pack_bf16x2(e[2], e[3]);
+        pk.z = pack_bf16x2(e[4], e[5]);
+        pk.w = pack_bf16x2(e[6], e[7]);
+        *reinterpret_cast<uint4*>(row_base + ((u ^ (r & 7)) << 4)) = pk;
       }
       l = l * alpha + rowsum;
       fence_proxy_async();
@@ -358,15 +387,21 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu,
                       mbar_wait_bounded(o_ready, (n_blocks - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
     }
+    // row sum over both halves
+    float* xl = xmax + 512;
+    xl[half * 128 + r] = l;
+    mbar_arrive(lsum_bar);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(lsum_bar, 0, abort_flag, p.status, kTimeoutEpilogue));
+    if (ok) l += xl[(half ^ 1) * 128 + r];
     if (ok) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + static_cast<int64_t>(i) * p.o_row_stride + h * D;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(i) * p.o_row_stride + h * D + half * 64;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t rr[32];
         if (n_blocks > 0) {
-          tmem_ld_32x32b_x32(tO + lane_addr + c * 32, rr);
+          tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, rr);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -384,20 +419,20 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (valid) p.lse[static_cast<int64_t>(h) * p.T + i] = (l > 0.f) ? (m + log2f(l)) / kLog2e : -INFINITY;
+      if (valid && half == 0) p.lse[static_cast<int64_t>(h) * p.T + i] = (l > 0.f) ? (m + log2f(l)) / kLog2e : -INFINITY;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
 
-constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 256;
+constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 160 + 3 * 256 * 4;  // tiles, align, barriers, exchange
 
 }  // namespace attn
 }  // namespace mvp
@@ -460,7 +495,7 @@ std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::T
     configured = true;
   }
   dim3 grid((T + BLK - 1) / BLK, Hq);
-  fwd_kernel<<<grid, 192, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  fwd_kernel<<<grid, kFwdThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }
@@ -498,7 +533,9 @@ struct BwdParams {
   int* status;
 };
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int kBwdThreads = 320;  // 8 gradient warps + TMA warp + MMA warp
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -520,7 +557,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* mma2_done = bars + 5;
   uint64_t* dq_read = bars + 6;
   uint64_t* done_bar = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* stage = bars + 8;  // [2] lse / delta of the next query block staged (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -540,14 +578,16 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(qd_full, 1);
     mbar_init(qd_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(mma2_done, 1);
-    mbar_init(dq_read, 128);
+    mbar_init(dq_read, 256);
+    mbar_init(&stage[0], 256);
+    mbar_init(&stage[1], 256);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -557,7 +597,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (elect_one_sync()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -591,7 +631,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (elect_one_sync()) {
       constexpr uint32_t id_kk = make_idesc_bf16(BLK, BLK, false, false);
       constexpr uint32_t id_km = make_idesc_bf16(BLK, D, false, true);
@@ -627,13 +667,16 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
     }
   } else {
-    // warps 0-3: one key row (S^T/dP^T/dK/dV lane) and one query row (dQ lane) per thread
-    const int c = warp * 32 + lane;
+    // warps 0-7, two warpgroups: thread (warp % 4, lane) owns key row c (S^T / dP^T / dK / dV lane) and
+    // query row c of the dQ tile; warpgroup `half` takes query columns 64*half .. +63 of S^T / dP^T
+    // and d columns 64*half .. +63 of dQ / dK / dV.
+    const int c = (warp & 3) * 32 + lane;
+    const int half = warp >> 2;
     const int kc = k0 + c;
     const bool kvalid = kc < p.Tk;
     int lo_c = 0, ke = 0;  // query rows lo_c .. ke-1 see key kc
     if (kvalid) query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, kc, lo_c, ke);
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
     for (int n = 0; n < n_iter; ++n) {
       const int h = hk * rep + n / nq;
@@ -643,23 +686,27 @@ __global__ void __launch_bounds__(192, 1)
       {
         const int qi = q0 + c;
         const bool qv = qi < p.T;
-        lse_b[c] = qv ? p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e : INFINITY;
-        del_b[c] = qv ? p.delta[static_cast<int64_t>(h) * p.T + qi] : 0.f;
+        if (half == 0) lse_b[c] = qv ? p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e : INFINITY;
+        else del_b[c] = qv ? p.delta[static_cast<int64_t>(h) * p.T + qi] : 0.f;
       }
-      named_barrier_sync(1, 128);
+      mbar_arrive(&stage[n & 1]);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait_bounded(&stage[n & 1], (n >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+      if (!ok) break;
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
-      for (int ch = 0; ch < BLK / 32; ++ch) {
+      for (int ch = 0; ch < 2; ++ch) {
+        const int col0 = half * 64 + ch * 32;
         uint32_t sr[32], dr[32];
-        tmem_ld_32x32b_x32(tS + lane_addr + ch * 32, sr);
-        tmem_ld_32x32b_x32(tdP + lane_addr + ch * 32, dr);
+        tmem_ld_32x32b_x32(tS + lane_addr + col0, sr);
+        tmem_ld_32x32b_x32(tdP + lane_addr + col0, dr);
         tmem_wait_ld();
         float pv[32], ds[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const int r = ch * 32 + t;
+          const int r = col0 + t;
           const int qr = q0 + r;
           const bool allowed = kvalid && qr >= lo_c && qr < ke && qr < p.T;
           const float pe = allowed ? exp2f(__uint_as_float(sr[t]) * p.scale_log2 - lse_b[r]) : 0.f;
@@ -667,10 +714,9 @@ __global__ void __launch_bounds__(192, 1)
           ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
         }
         // 32 q columns = half of one 64-wide chunk = four 16-byte units.
-        const int chunk = ch >> 1;
-        const int u0 = (ch & 1) * 4;
-        uint8_t* prow = sPt + chunk * CHUNK_BYTES + c * 128;
-        uint8_t* drow = sdSt + chunk * CHUNK_BYTES + c * 128;
+        uint8_t* prow = sPt + half * CHUNK_BYTES + c * 128;
+        uint8_t* drow = sdSt + half * CHUNK_BYTES + c * 128;
+        const int u0 = ch * 4;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint4 a, b;
@@ -693,13 +739,13 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(mma2_done, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      // dQ rows: thread c now owns query row q0 + c.
+      // dQ rows: thread c now owns query row q0 + c, d columns 64*half .. +63.
       const int qi = q0 + c;
-      float* dst = p.dq_acc + (static_cast<int64_t>(qi) * p.Hq + h) * D;
+      float* dst = p.dq_acc + (static_cast<int64_t>(qi) * p.Hq + h) * D + half * 64;
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
+      for (int ch = 0; ch < 2; ++ch) {
         uint32_t rr[32];
-        tmem_ld_32x32b_x32(tS + lane_addr + ch * 32, rr);
+        tmem_ld_32x32b_x32(tS + lane_addr + half * 64 + ch * 32, rr);
         tmem_wait_ld();
         if (qi < p.T) {
 #pragma unroll
@@ -718,13 +764,13 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t tacc = which == 0 ? tdK : tdV;
-        __nv_bfloat16* out = which == 0 ? p.dk + static_cast<int64_t>(kc) * p.dk_row_stride + hk * D
-                                        : p.dv + static_cast<int64_t>(kc) * p.dv_row_stride + hk * D;
+        __nv_bfloat16* out = which == 0 ? p.dk + static_cast<int64_t>(kc) * p.dk_row_stride + hk * D + half * 64
+                                        : p.dv + static_cast<int64_t>(kc) * p.dv_row_stride + hk * D + half * 64;
 #pragma unroll
-        for (int ch = 0; ch < D / 32; ++ch) {
+        for (int ch = 0; ch < 2; ++ch) {
           uint32_t rr[32];
           if (n_iter > 0) {
-            tmem_ld_32x32b_x32(tacc + lane_addr + ch * 32, rr);
+            tmem_ld_32x32b_x32(tacc + lane_addr + half * 64 + ch * 32, rr);
             tmem_wait_ld();
           } else {
 #pragma unroll
@@ -748,7 +794,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -786,7 +832,7 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
   }
 }
 
-constexpr int kBwdSmem = 6 * TILE_BYTES + 4 * BLK * 4 + 1024 + 256;
+constexpr int kBwdSmem = 6 * TILE_BYTES + 4 * BLK * 4 + 1024 + 256;  // tiles, lse/delta, align, barriers
 
 }  // namespace attn
 }  // namespace mvp
@@ -863,7 +909,7 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
     configured = true;
   }
   dim3 grid((Tk + BLK - 1) / BLK, Hkv);
-  bwd_kernel<<<grid, 192, kBwdSmem, stream>>>(tq, tk, tv, tdo, p);
+  bwd_kernel<<<grid, kBwdThreads, kBwdSmem, stream>>>(tq, tk, tv, tdo, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int64_t n = static_cast<int64_t>(T) * Hq * D;
   f32_to_bf16_kernel<<<static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 16)), 256, 0, stream>>>(

@@ -82,29 +82,49 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(RsParams p) {
   }
   __syncthreads();
   if (!s_ok) return;
-  // 3. pull and sum this rank's slice
+  // 3. pull and sum this rank's slice: kUnroll float4 per rank in flight per thread so that enough
+  //    bytes are outstanding to cover the NVLink round trip
+  constexpr int kUnroll = 4;
   const int64_t base = p.offset + static_cast<int64_t>(p.rank) * p.shard;
   const int64_t n4 = p.shard / 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float local_sq = 0.f;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < n4; i0 += stride * kUnroll) {
+    float4 acc[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
       if (r < p.world) {
-        const float4 v = reinterpret_cast<const float4*>(p.peers[r] + base)[i];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+        const float4* src = reinterpret_cast<const float4*>(p.peers[r] + base);
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t i = i0 + u * stride;
+          v[u] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
+        }
       }
     }
-    acc.x *= p.scale;
-    acc.y *= p.scale;
-    acc.z *= p.scale;
-    acc.w *= p.scale;
-    reinterpret_cast<float4*>(p.out)[i] = acc;
-    local_sq += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n4) {
+        float4 a = acc[u];
+        a.x *= p.scale;
+        a.y *= p.scale;
+        a.z *= p.scale;
+        a.w *= p.scale;
+        reinterpret_cast<float4*>(p.out)[i] = a;
+        local_sq += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+      }
+    }
   }
   if (p.sumsq != nullptr) {
 #pragma unroll
@@ -181,9 +201,10 @@ void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vecto
   p.scale = static_cast<float>(scale);
   p.out = out.data_ptr<float>();
   p.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
-  // Enough CTAs to keep NVLink busy, few enough to leave the SMs to the overlapped backward.
+  // Two CTAs per SM keep ~10 MB of loads in flight (enough for NVLink); they need no shared memory
+  // and few registers, so they co-reside with the persistent GEMM / attention CTAs of the backward.
   const int64_t n4 = shard / 4;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, (n4 + 255) / 256)));
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(2 * 148, (n4 + 1023) / 1024)));
   rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
