@@ -10,15 +10,23 @@
 //   weight grad dW = dY^T X: A = dY (M-major), B = X (N-major)
 //
 // Pipeline (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: streams 128 x 64 A and BN x 64 B tiles into a
+//   warp 0      TMA producer: streams BM x 64 A and BN x 64 B tiles into a
 //               STAGES-deep ring of 128-byte-swizzled shared-memory buffers.
 //   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from
 //               one elected thread; tcgen05.commit releases ring slots and
 //               publishes finished accumulators.
-//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (one TMEM lane per
+//   warps 2..   epilogue: tcgen05.ld the fp32 accumulator (one TMEM lane per
 //               output row), convert and store to global memory.
-// Two accumulator buffers in TMEM let the epilogue of tile i overlap the
-// MMAs of tile i+1.  All waits are bounded (see common.cuh).
+// Two tile shapes:
+//   BM=128: two accumulator buffers in TMEM (2 x BN columns) let the epilogue
+//           of tile i overlap the MMAs of tile i+1; 4 epilogue warps.
+//   BM=256 (BN=256): each k-step issues two M=128 MMAs that share the B tile,
+//           so a CTA moves 1.5x fewer operand bytes per FLOP through L2 and
+//           shared memory (3-stage ring of 64 KB); the two M-halves fill all
+//           512 TMEM columns, so the epilogue (8 warps, one per half and lane
+//           quarter) does not overlap the next tile.  The host picks the shape
+//           from the reduction length.
+// All waits are bounded (see common.cuh).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -46,9 +54,7 @@ static bool gemm_trace() {
 namespace mvp {
 namespace gemm {
 
-constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
 
 enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
 
@@ -60,13 +66,17 @@ struct Params {
   int group_m;
 };
 
-template <int BN>
+template <int BN, int BM>
 struct Config {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static_assert(BM == 128 || (BM == 256 && BN == 256), "tile shapes: 128 x {128, 256} or 256 x 256");
+  static constexpr int STAGES = BM == 256 ? 3 : (BN == 256 ? 4 : 6);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered fp32 accumulator
+  static constexpr int NACC = BM == 256 ? 1 : 2;      // accumulator buffers (M-halves fill TMEM at BM=256)
+  static constexpr int TMEM_COLS = 2 * BN;            // 512 or 256 columns
+  static constexpr int EPI_WARPS = BM == 256 ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -82,10 +92,10 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
   tn = r / gm;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int BM, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(Config<BN, BM>::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
-  using Cfg = Config<BN>;
+  using Cfg = Config<BN, BM>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 32 * Cfg::EPI_WARPS);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -192,14 +202,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (elect_one_sync()) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = make_idesc_bf16(128, BN, A_MN, B_MN);  // every MMA is M=128 (cta_group::1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = Cfg::NACC == 2 ? (local & 1) : 0;
+        const uint32_t acc_phase = Cfg::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.status, kTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -213,12 +223,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            uint64_t adesc, bdesc;
-            if constexpr (!A_MN) adesc = make_smem_desc_sw128(a_base + k * 32, 16, 1024);
-            else adesc = make_smem_desc_sw128(a_base + k * 2048, 64 * BK * 2, 1024);
+            uint64_t bdesc;
             if constexpr (!B_MN) bdesc = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
             else bdesc = make_smem_desc_sw128(b_base + k * 2048, 64 * BK * 2, 1024);
-            mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int half = 0; half < BM / 128; ++half) {
+              // rows 128*half.. of the A tile: 16 KB further in both layouts (K-major: 128 rows of
+              // 128 B; MN-major: two 64-row chunks of 8 KB)
+              const uint32_t a_half = a_base + half * 16384;
+              uint64_t adesc;
+              if constexpr (!A_MN) adesc = make_smem_desc_sw128(a_half + k * 32, 16, 1024);
+              else adesc = make_smem_desc_sw128(a_half + k * 2048, 64 * BK * 2, 1024);
+              mma_bf16_ss(d_tmem + half * BN, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -236,13 +253,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = sub * 32 + lane;
+    const int mhalf = (warp - 2) >> 2;  // BM=256: which M-half (accumulator) this warpgroup drains
+    const int row_in_tile = mhalf * 128 + sub * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int tm, tn;
       tile_coords(t, num_m, num_n, p.group_m, tm, tn);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = Cfg::NACC == 2 ? (local & 1) : 0;
+      const uint32_t acc_phase = Cfg::NACC == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.status, kTimeoutEpilogue))) break;
       tc_fence_after();
       const int m = tm * BM + row_in_tile;
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + (acc + mhalf) * BN + c * 32, r);
         tmem_wait_ld();
         const int n = tn * BN + c * 32;
         if (!row_ok || n >= p.N) continue;
@@ -311,10 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, int BM, bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int num_sms, cudaStream_t stream) {
-  using Cfg = Config<BN>;
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
+  using Cfg = Config<BN, BM>;
+  auto kern = gemm_bf16_kernel<BN, BM, A_MN, B_MN, EPI>;
   static bool configured = false;  // per instantiation
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
@@ -322,17 +340,28 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int n
   }
   const int num_tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = std::max(1, std::min(num_tiles, num_sms));
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, int EPI>
+template <int BN, int BM, int EPI>
 void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int sms,
                     cudaStream_t s) {
-  if (!a_mn && !b_mn) launch<BN, false, false, EPI>(ta, tb, p, sms, s);
-  else if (!a_mn && b_mn) launch<BN, false, true, EPI>(ta, tb, p, sms, s);
-  else if (a_mn && !b_mn) launch<BN, true, false, EPI>(ta, tb, p, sms, s);
-  else launch<BN, true, true, EPI>(ta, tb, p, sms, s);
+  if (!a_mn && !b_mn) launch<BN, BM, false, false, EPI>(ta, tb, p, sms, s);
+  else if (!a_mn && b_mn) launch<BN, BM, false, true, EPI>(ta, tb, p, sms, s);
+  else if (a_mn && !b_mn) launch<BN, BM, true, false, EPI>(ta, tb, p, sms, s);
+  else launch<BN, BM, true, true, EPI>(ta, tb, p, sms, s);
+}
+
+// BM=256 only when the reduction is long (K >= 8192): its epilogue does not overlap the next tile's
+// MMAs, which costs more than the operand-traffic saving buys on short reductions (measured on
+// the Qwen3-8B linear shapes: forward / input-grad GEMMs with K = 4096 run faster at BM=128,
+// weight-grad GEMMs with K = 8192 tokens and K >= 12288 ones at BM=256).
+// MVP_GEMM_BM=128/256 forces one shape.
+inline int choose_bm(int64_t M, int64_t N, int64_t K, int BN) {
+  static const char* force = std::getenv("MVP_GEMM_BM");
+  if (force != nullptr) return std::atoi(force) == 256 && BN == 256 ? 256 : 128;
+  return (BN == 256 && M >= 256 && K >= 8192) ? 256 : 128;
 }
 
 }  // namespace gemm
@@ -376,6 +405,8 @@ void gemm_sm100(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool 
   GEMM_TRACE("enter M=%lld N=%lld K=%lld a_mn=%d b_mn=%d acc=%d f32=%d\n", (long long)M, (long long)N,
              (long long)K, (int)a_mn, (int)b_mn, (int)accumulate, (int)out_f32);
   const int BN = N >= 256 ? 256 : 128;
+  const int sms = mvp::num_sms(a.get_device());
+  const int BM = choose_bm(M, N, K, BN);
   // Tensor maps: dim0 is the contiguous dimension.
   CUtensorMap ta, tb;
   if (!a_mn) mvp::make_tmap_2d_bf16(&ta, a.data_ptr(), K, M, a.stride(0), 64, BM);
@@ -391,17 +422,20 @@ void gemm_sm100(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool 
   p.C = c.data_ptr();
   p.ldc = c.stride(0);
   p.status = reinterpret_cast<int*>(status_ptr);
-  p.group_m = 16;
-  const int sms = mvp::num_sms(a.get_device());
-  GEMM_TRACE("launch sms=%d BN=%d\n", sms, BN);
+  p.group_m = BM == 256 ? 8 : 16;
+  GEMM_TRACE("launch sms=%d BM=%d BN=%d\n", sms, BM, BN);
   const int epi = out_f32 ? (accumulate ? kAccumF32 : kStoreF32) : kStoreBf16;
-  if (BN == 256) {
-    if (epi == kStoreBf16) dispatch_major<256, kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
-    else if (epi == kStoreF32) dispatch_major<256, kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
-    else dispatch_major<256, kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+  if (BN == 256 && BM == 256) {
+    if (epi == kStoreBf16) dispatch_major<256, 256, kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else if (epi == kStoreF32) dispatch_major<256, 256, kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else dispatch_major<256, 256, kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+  } else if (BN == 256) {
+    if (epi == kStoreBf16) dispatch_major<256, 128, kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else if (epi == kStoreF32) dispatch_major<256, 128, kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else dispatch_major<256, 128, kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
   } else {
-    if (epi == kStoreBf16) dispatch_major<128, kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
-    else if (epi == kStoreF32) dispatch_major<128, kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
-    else dispatch_major<128, kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+    if (epi == kStoreBf16) dispatch_major<128, 128, kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else if (epi == kStoreF32) dispatch_major<128, 128, kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+    else dispatch_major<128, 128, kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
   }
 }
