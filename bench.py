@@ -45,6 +45,23 @@ PER_GPU_SEQS = 8
 MODEL = "Qwen/Qwen3-8B-Base"
 METRIC = "tokens/s (Qwen3-8B FSDP pretraining, 8192-token packed sequences; whole job)"
 
+# Named workloads.  The default is the headline benchmark; the others are the long-context
+# context-parallel and the tensor-parallel configurations (all ranks form one context / tensor
+# group up to its size, data parallelism over the rest).
+WORKLOADS = {
+    "qwen3-8b-fsdp": dict(model=MODEL, seq=SEQ_LEN, seqs_per_dp=PER_GPU_SEQS, docs=(256, 4096), metric=METRIC,
+                          model_name="Qwen3-8B"),
+    "qwen3-8b-cp-ring": dict(model=MODEL, seq=131072, seqs_per_dp=1, docs=(4096, 65536), cp="ring",
+                             metric="tokens/s (Qwen3-8B, 131072-token packed sequences, ring context parallel; "
+                                    "whole job)", model_name="Qwen3-8B"),
+    "qwen3-8b-cp-ulysses": dict(model=MODEL, seq=131072, seqs_per_dp=1, docs=(4096, 65536), cp="ulysses",
+                                metric="tokens/s (Qwen3-8B, 131072-token packed sequences, Ulysses context "
+                                       "parallel; whole job)", model_name="Qwen3-8B"),
+    "qwen3-32b-tp": dict(model="Qwen/Qwen3-32B", seq=4096, global_batch=32, docs=(256, 4096), tp=8,
+                         metric="tokens/s (Qwen3-32B, TP + sequence parallel + FSDP, 4096-token packed sequences; "
+                                "whole job)", model_name="Qwen3-32B"),
+}
+
 
 def _env_int(name: str, default: int) -> int:
     try:
@@ -151,11 +168,28 @@ def run_ours(args) -> None:
     from recipes.qwen3.engine.qwen3_engine import Qwen3Engine
 
     steps_total = args.warmup + 2 * args.steps + 2
-    overrides = [
+    wl = WORKLOADS[args.workload]
+    if args.model == MODEL:
+        args.model = wl["model"]
+    if args.seq_len == SEQ_LEN:
+        args.seq_len = wl["seq"]
+    cp = world if wl.get("cp") else 1
+    tp = min(world, wl.get("tp", 1))
+    dp = world // (cp * tp)
+    global_batch = wl.get("global_batch", wl.get("seqs_per_dp", PER_GPU_SEQS) * dp)
+    lo, hi = wl["docs"]
+    mesh = []
+    if cp > 1:
+        mesh = [f"parallel.mesh.context={cp}", "parallel.mesh.shard=1", "parallel.mesh.replicate=1",
+                f"parallel.backend_kwargs.context_parallel.impl={wl['cp']}"]
+    elif tp > 1:
+        mesh = [f"parallel.mesh.tensor={tp}", "parallel.mesh.shard=-1", "parallel.mesh.replicate=1",
+                "parallel.backend_kwargs.sequence_parallel=true"]
+    overrides = mesh + [
         f"model.pretrained_model_name_or_path={args.model}",
-        f"data.train_path=synthetic://text?vocab={_vocab_of(args.model)}&min_len=256&max_len=4096",
+        f"data.train_path=synthetic://text?vocab={_vocab_of(args.model)}&min_len={lo}&max_len={hi}",
         f"data.max_seq_len={args.seq_len}",
-        f"optim.global_batch_size={PER_GPU_SEQS * world}",
+        f"optim.global_batch_size={global_batch}",
         "data.batch_size=1",
         "optim.gradient_accumulation_steps=-1",
         f"loop.total_steps={steps_total}",
@@ -188,7 +222,8 @@ def run_ours(args) -> None:
     free, _total = torch.cuda.mem_get_info()
     H, F, L = cfgm.hidden_size, cfgm.intermediate_size, cfgm.num_hidden_layers
     qkv = (cfgm.num_attention_heads + 2 * cfgm.num_key_value_heads) * cfgm.head_dim
-    per_layer = args.seq_len * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
+    local_tokens = args.seq_len // cp  # context ranks hold 1/cp of the row
+    per_layer = local_tokens * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
                                     cfgm.head_dim + 3 * F) * 1.1
     head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
     budget = free - head_ws - (10 << 30)
@@ -202,7 +237,8 @@ def run_ours(args) -> None:
     n_host = (args.warmup + 2 * args.steps) * ga  # the end-to-end pass gets fresh batches
     host_batches = [next(it) for _ in range(n_host)]
     h2d_bytes = sum(_bytes_of(b) for b in host_batches[:ga])
-    tokens_per_step = sum(int(b["total_tokens"]) for b in host_batches[:ga]) * world
+    # context / tensor ranks of a group share their samples: count each sample once
+    tokens_per_step = sum(int(b["total_tokens"]) for b in host_batches[:ga]) * dp
 
     def step_host(i: int) -> dict:
         return engine.train_step(host_batches[i * ga:(i + 1) * ga])
@@ -291,7 +327,7 @@ def run_ours(args) -> None:
     peaks = _measured_peak()
     value = tokens_per_step / (ms / 1e3)
     line = {
-        "metric": METRIC,
+        "metric": wl["metric"],
         "value": round(value, 1),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -299,13 +335,15 @@ def run_ours(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if cp == 1 and "global_batch" not in wl else "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: uniform token ids over 151936, document lengths U[256,4096] packed to 8192 tokens "
-                "(causal mask per document); random-init Qwen3-8B weights",
-        "config": {"model": "Qwen3-8B", "global_batch": PER_GPU_SEQS * world, "seq_len": args.seq_len,
-                   "parallelism": f"fsdp{world}", "micro_batch": 1, "grad_accum": ga,
+        "data": f"synthetic: uniform token ids over 151936, document lengths U[{lo},{hi}] packed to "
+                f"{args.seq_len} tokens (causal mask per document); random-init {wl['model_name']} weights",
+        "config": {"model": wl["model_name"], "global_batch": global_batch, "seq_len": args.seq_len,
+                   "parallelism": (f"fsdp{world}" if cp == 1 and tp == 1 else
+                                   f"cp{cp}-{wl['cp']}" if cp > 1 else f"tp{tp}-sp x fsdp{dp}"),
+                   "micro_batch": 1, "grad_accum": ga, "workload": args.workload,
                    "activation_checkpoint_layers": ckpt_layers,
                    "l2": "no flush: weights, optimizer state and activations >> 126 MB L2",
                    "optimizer": "AdamW (fp32 master, fused flat-shard kernel), clip 1.0, cosine"},
@@ -342,6 +380,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-8b-fsdp",
+                    help="default: the headline Qwen3-8B FSDP benchmark")
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
     ap.add_argument("--ckpt-layers", type=int, default=-1, help="-1: choose from free memory")
