@@ -1,0 +1,421 @@
+// Pair-of-SMs bf16 GEMM for sm_100a: one 256 x 256 output tile per cluster of two CTAs.
+//
+//   C[M, N] (+)= A[M, K] * B[N, K]^T   (same operand conventions as gemm_sm100.cu)
+//
+// tcgen05.mma with cta_group::2 computes a 256 x 256 x 16 product across the two
+// SMs of a cluster: CTA r of the pair holds rows 128r..128r+127 of the A tile and
+// rows 128r..128r+127 of the B tile (half of N) in its own shared memory, and its
+// own tensor memory receives rows 128r..128r+127 of the accumulator (all 256
+// columns).  Per SM and k-block that is 32 KB of operands for 2 x 128 x 256 x 64
+// FLOPs -- half the B traffic of a single-SM 128 x 256 tile -- while each SM still
+// holds two 256-column accumulators, so the epilogue of one tile overlaps the MMAs
+// of the next.
+//
+// Roles (both CTAs run the same warp layout):
+//   warp 0      TMA: each CTA loads its own A and B halves; the copies report
+//               their bytes to the leader CTA's full barrier (cta_group::2 copy,
+//               plain -- never multicast).
+//   warp 1      allocates TMEM in both CTAs (cta_group::2); in the leader CTA one
+//               thread issues the MMAs and commits with a two-CTA multicast
+//               arrive, releasing ring slots and publishing accumulators in both.
+//   warps 2..5  epilogue of this CTA's 128 rows; releases the accumulator by
+//               arriving on the leader's barrier.
+// Every wait is bounded; every thread of both CTAs reaches the final cluster
+// barrier, after which both MMA warps free the tensor memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace mvp {
+namespace gemm2 {
+
+constexpr int BK = 64;
+constexpr int TILE = 256;      // output tile per cluster: 256 x 256
+constexpr int HALF = 128;      // rows of A and of B held by each CTA
+constexpr int STAGES = 6;
+constexpr int A_BYTES = HALF * BK * 2;   // 16 KB
+constexpr int B_BYTES = HALF * BK * 2;   // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;           // two 256-column accumulators
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+
+struct Params {
+  int M, N, K;
+  void* C;
+  int64_t ldc;
+  int* status;
+  int group_m;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared-memory address of the same variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar_addr) : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose completion is reported to the
+// barrier at cluster address `bar` (the leader CTA's).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the barrier at this offset in both CTAs of the pair when the MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Arrive on this CTA's barrier when the pair MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& tm, int& tn) {
+  const int per_group = group_m * num_n;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gm = min(group_m, num_m - first_m);
+  const int r = t - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);  // used in the leader
+  uint64_t* empty_bar = full_bar + STAGES;                                         // both CTAs
+  uint64_t* tfull_bar = empty_bar + STAGES;                                        // [2] both CTAs
+  uint64_t* tempty_bar = tfull_bar + 2;                                            // [2] used in the leader
+  uint64_t* done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t crank = cluster_ctarank();  // 0 = leader
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_m = (p.M + TILE - 1) / TILE;
+  const int num_n = (p.N + TILE - 1) / TILE;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * 128);  // epilogue threads of both CTAs
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive / copy
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (elect_one_sync()) {
+      const uint32_t leader_full0 = mapa_shared(smem_u32(&full_bar[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, p.group_m, tm, tn);
+        const int m0 = tm * TILE + crank * HALF, n0 = tn * TILE + crank * HALF;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, abort_flag, p.status, kTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (crank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          const uint32_t bar = leader_full0 + stage * 8;
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+            tma_load_2d_pair(a_dst + 64 * BK * 2, &tmA, bar, m0 + 64, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
+            tma_load_2d_pair(b_dst + 64 * BK * 2, &tmB, bar, n0 + 64, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // After an abort, let copies already issued into this CTA's ring land (bounded) before exit.
+      if ((!ok || *abort_flag) && issued_mask) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 200000000ull) {
+        }
+        (void)issued_phase;
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA (leader only)
+    if (crank == 0 && elect_one_sync()) {
+      constexpr uint32_t idesc = make_idesc_bf16(TILE, TILE, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * TILE;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag, p.status, kTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t adesc, bdesc;
+            if constexpr (!A_MN) adesc = make_smem_desc_sw128(a_base + k * 32, 16, 1024);
+            else adesc = make_smem_desc_sw128(a_base + k * 2048, 64 * BK * 2, 1024);
+            if constexpr (!B_MN) bdesc = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
+            else bdesc = make_smem_desc_sw128(b_base + k * 2048, 64 * BK * 2, 1024);
+            mma_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull_bar[acc]);
+      }
+      mma_commit_pair_local(done_bar);
+      mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int sub = warp & 3;
+    const int row_in_tile = crank * HALF + sub * 32 + lane;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+    int local = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, p.group_m, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.status, kTimeoutEpilogue)))
+        break;
+      tc_fence_after();
+      const int m = tm * TILE + row_in_tile;
+      const bool row_ok = m < p.M;
+#pragma unroll 1
+      for (int c = 0; c < TILE / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * TILE + c * 32, r);
+        tmem_wait_ld();
+        const int n = tn * TILE + c * 32;
+        if (!row_ok || n >= p.N) continue;
+        const bool full_chunk = (n + 32 <= p.N);
+        if constexpr (EPI == kStoreBf16) {
+          __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
+          if (full_chunk && ((reinterpret_cast<uintptr_t>(C) & 15) == 0)) {
+            uint4* dst = reinterpret_cast<uint4*>(C);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 q;
+              q.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+              q.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+              q.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+              q.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              dst[v] = q;
+            }
+          } else {
+            for (int j = 0; j < 32 && n + j < p.N; ++j) C[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        } else {
+          float* C = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
+          if (full_chunk && ((reinterpret_cast<uintptr_t>(C) & 15) == 0)) {
+            float4* dst = reinterpret_cast<float4*>(C);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float4 q = make_float4(__uint_as_float(r[4 * v + 0]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              if constexpr (EPI == kAccumF32) {
+                const float4 o = dst[v];
+                q.x += o.x;
+                q.y += o.y;
+                q.z += o.z;
+                q.w += o.w;
+              }
+              dst[v] = q;
+            }
+          } else {
+            for (int j = 0; j < 32 && n + j < p.N; ++j) {
+              float val = __uint_as_float(r[j]);
+              if constexpr (EPI == kAccumF32) val += C[j];
+              C[j] = val;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      remote_arrive(leader_tempty0 + acc * 8);
+    }
+  }
+
+  // Both CTAs: every role is done (the leader's MMAs have retired); then free the pair's TMEM.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int num_sms, cudaStream_t stream) {
+  auto kern = gemm2sm_kernel<A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured = true;
+  }
+  const int num_tiles = ((p.M + TILE - 1) / TILE) * ((p.N + TILE - 1) / TILE);
+  const int clusters = std::max(1, std::min(num_tiles, num_sms / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+}
+
+template <int EPI>
+void dispatch(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int sms,
+              cudaStream_t s) {
+  if (!a_mn && !b_mn) launch<false, false, EPI>(ta, tb, p, sms, s);
+  else if (!a_mn && b_mn) launch<false, true, EPI>(ta, tb, p, sms, s);
+  else if (a_mn && !b_mn) launch<true, false, EPI>(ta, tb, p, sms, s);
+  else launch<true, true, EPI>(ta, tb, p, sms, s);
+}
+
+}  // namespace gemm2
+}  // namespace mvp
+
+// Same contract as gemm_sm100 (operands already validated by the caller).
+void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                     bool accumulate, int64_t status_ptr) {
+  using namespace mvp::gemm2;
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const bool out_f32 = c.scalar_type() == at::kFloat;
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta, tb;
+  // Each CTA loads 128 rows of A and 128 rows of B (K-major: one 64 x 128 box; MN-major: two 64 x 64 boxes).
+  if (!a_mn) mvp::make_tmap_2d_bf16(&ta, a.data_ptr(), K, M, a.stride(0), 64, HALF);
+  else mvp::make_tmap_2d_bf16(&ta, a.data_ptr(), M, K, a.stride(0), 64, 64);
+  if (!b_mn) mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), K, N, b.stride(0), 64, HALF);
+  else mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), N, K, b.stride(0), 64, 64);
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.status = reinterpret_cast<int*>(status_ptr);
+  p.group_m = 8;
+  const int sms = mvp::num_sms(a.get_device());
+  const int epi = out_f32 ? (accumulate ? kAccumF32 : kStoreF32) : kStoreBf16;
+  if (epi == kStoreBf16) dispatch<kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
+  else if (epi == kStoreF32) dispatch<kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+  else dispatch<kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+}

@@ -367,6 +367,17 @@ inline int choose_bm(int64_t M, int64_t N, int64_t K, int BN) {
 }  // namespace gemm
 }  // namespace mvp
 
+void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                     bool accumulate, int64_t status_ptr);
+
+// The two-SM 256 x 256 kernel (gemm2sm_sm100.cu) takes every GEMM with M, N >= 256;
+// MVP_GEMM_PAIR=0 keeps the single-SM kernels.
+static bool use_pair_kernel(int64_t M, int64_t N) {
+  static const char* env = std::getenv("MVP_GEMM_PAIR");
+  static const bool on = env == nullptr || std::atoi(env) != 0;
+  return on && M >= 256 && N >= 256;
+}
+
 // Host entry point.
 //   a: if a_mn == false, an [M, K] view with unit stride along K;
 //      if a_mn == true,  a [K, M] view with unit stride along M.
@@ -404,6 +415,10 @@ void gemm_sm100(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool 
 
   GEMM_TRACE("enter M=%lld N=%lld K=%lld a_mn=%d b_mn=%d acc=%d f32=%d\n", (long long)M, (long long)N,
              (long long)K, (int)a_mn, (int)b_mn, (int)accumulate, (int)out_f32);
+  if (use_pair_kernel(M, N)) {
+    gemm_sm100_pair(a, a_mn, b, b_mn, c, accumulate, status_ptr);
+    return;
+  }
   const int BN = N >= 256 ? 256 : 128;
   const int sms = mvp::num_sms(a.get_device());
   const int BM = choose_bm(M, N, K, BN);

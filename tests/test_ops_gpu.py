@@ -30,6 +30,8 @@ GEMM_SHAPES = [
     (1000, 1000, 1000),
     (129, 257, 520),
     (1024, 3072, 4096),
+    (520, 776, 136),      # two-SM 256 x 256 tiles with ragged M / N tails
+    (2048, 4096, 8192),
 ]
 
 
