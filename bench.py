@@ -51,13 +51,14 @@ METRIC = "tokens/s (Qwen3-8B FSDP pretraining, 8192-token packed sequences; whol
 WORKLOADS = {
     "qwen3-8b-fsdp": dict(model=MODEL, seq=SEQ_LEN, seqs_per_dp=PER_GPU_SEQS, docs=(256, 4096), metric=METRIC,
                           model_name="Qwen3-8B"),
-    "qwen3-8b-cp-ring": dict(model=MODEL, seq=131072, seqs_per_dp=1, docs=(4096, 65536), cp="ring",
+    "qwen3-8b-cp-ring": dict(model=MODEL, seq=131072, seqs_per_dp=1, docs=(4096, 65536), cp="ring", ckpt_all=True,
                              metric="tokens/s (Qwen3-8B, 131072-token packed sequences, ring context parallel; "
                                     "whole job)", model_name="Qwen3-8B"),
     "qwen3-8b-cp-ulysses": dict(model=MODEL, seq=131072, seqs_per_dp=1, docs=(4096, 65536), cp="ulysses",
+                                ckpt_all=True,
                                 metric="tokens/s (Qwen3-8B, 131072-token packed sequences, Ulysses context "
                                        "parallel; whole job)", model_name="Qwen3-8B"),
-    "qwen3-32b-tp": dict(model="Qwen/Qwen3-32B", seq=4096, global_batch=32, docs=(256, 4096), tp=8,
+    "qwen3-32b-tp": dict(model="Qwen/Qwen3-32B", seq=4096, global_batch=32, docs=(256, 4096), tp=8, ckpt_all=True,
                          metric="tokens/s (Qwen3-32B, TP + sequence parallel + FSDP, 4096-token packed sequences; "
                                 "whole job)", model_name="Qwen3-32B"),
 }
@@ -229,6 +230,8 @@ def run_ours(args) -> None:
     budget = free - head_ws - (10 << 30)
     keep = max(0, min(L, int(budget // per_layer)))
     ckpt_layers = L - keep if args.ckpt_layers < 0 else args.ckpt_layers
+    if wl.get("ckpt_all") and args.ckpt_layers < 0:  # long sequences / activation checkpointing on by config
+        ckpt_layers = L
     if ckpt_layers > 0:
         inner.gradient_checkpointing_enable({"num_layers": ckpt_layers})
     engine.model.train()
