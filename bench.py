@@ -58,6 +58,10 @@ WORKLOADS = {
                                 ckpt_all=True,
                                 metric="tokens/s (Qwen3-8B, 131072-token packed sequences, Ulysses context "
                                        "parallel; whole job)", model_name="Qwen3-8B"),
+    "qwen3-vl-8b": dict(model="Qwen/Qwen3-VL-8B-Instruct", seq=16384, seqs_per_dp=4, docs=(448, 1344),
+                        recipe="qwen3_vl", config="recipes/qwen3_vl/configs/train.yaml",
+                        metric="tokens/s (Qwen3-VL-8B SFT, 16384-token packs of 1-4 images + text; whole job)",
+                        model_name="Qwen3-VL-8B"),
     "qwen3-32b-tp": dict(model="Qwen/Qwen3-32B", seq=4096, global_batch=32, docs=(256, 4096), tp=8, ckpt_all=True,
                          metric="tokens/s (Qwen3-32B, TP + sequence parallel + FSDP, 4096-token packed sequences; "
                                 "whole job)", model_name="Qwen3-32B"),
@@ -165,11 +169,15 @@ def run_ours(args) -> None:
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
     rank = _env_int("RANK", 0)
-    import_recipe_modules(__import__("pathlib").Path(ROOT) / "recipes" / "qwen3")
-    from recipes.qwen3.engine.qwen3_engine import Qwen3Engine
+    wl = WORKLOADS[args.workload]
+    recipe = wl.get("recipe", "qwen3")
+    import_recipe_modules(__import__("pathlib").Path(ROOT) / "recipes" / recipe)
+    if recipe == "qwen3_vl":
+        from recipes.qwen3_vl.engine.qwen3_vl_engine import Qwen3VLEngine as EngineClass
+    else:
+        from recipes.qwen3.engine.qwen3_engine import Qwen3Engine as EngineClass
 
     steps_total = args.warmup + 2 * args.steps + 2
-    wl = WORKLOADS[args.workload]
     if args.model == MODEL:
         args.model = wl["model"]
     if args.seq_len == SEQ_LEN:
@@ -186,9 +194,15 @@ def run_ours(args) -> None:
     elif tp > 1:
         mesh = [f"parallel.mesh.tensor={tp}", "parallel.mesh.shard=-1", "parallel.mesh.replicate=1",
                 "parallel.backend_kwargs.sequence_parallel=true"]
-    overrides = mesh + [
+    if recipe == "qwen3_vl":  # 1-4 images, sides multiples of 32 in [lo, hi] px; text (~1/3 of tokens) supervised
+        data = [f"data.train_path=synthetic://mm?min_px={lo}&max_px={hi}&min_images=1&max_images=4"
+                f"&min_text=256&max_text=2048&loss_fraction=1.0", "data.dataset_source=synthetic_mm",
+                f"model.image_max_pixels={hi * hi}", "parallel.mesh.replicate=1", "parallel.mesh.shard=-1",
+                "log.backends=[terminal]"]
+    else:
+        data = [f"data.train_path=synthetic://text?vocab={_vocab_of(args.model)}&min_len={lo}&max_len={hi}"]
+    overrides = mesh + data + [
         f"model.pretrained_model_name_or_path={args.model}",
-        f"data.train_path=synthetic://text?vocab={_vocab_of(args.model)}&min_len={lo}&max_len={hi}",
         f"data.max_seq_len={args.seq_len}",
         f"optim.global_batch_size={global_batch}",
         "data.batch_size=1",
@@ -201,8 +215,8 @@ def run_ours(args) -> None:
         "data.num_workers=0",
         "model.gradient_checkpointing.enabled=false",
     ] + list(args.override or [])
-    cfg = compose_config(os.path.join(ROOT, "recipes/qwen3/configs/synthetic_8b.yaml"), overrides)
-    engine = Qwen3Engine(cfg)
+    cfg = compose_config(os.path.join(ROOT, wl.get("config", "recipes/qwen3/configs/synthetic_8b.yaml")), overrides)
+    engine = EngineClass(cfg)
     ga = int(engine.config.optim.gradient_accumulation_steps)
 
     # Decide how many layers recompute activations from the memory left after
@@ -218,7 +232,7 @@ def run_ours(args) -> None:
     engine.scaler = GradientScaler(enabled=True, dtype=engine.dtype, device=engine.device_type)
     engine.timer = Timer(total_progress=engine.total_steps)
     inner = engine.unwrapped_model
-    cfgm = inner.config
+    cfgm = getattr(inner.config, "text_config", inner.config)
     torch.cuda.synchronize()
     free, _total = torch.cuda.mem_get_info()
     H, F, L = cfgm.hidden_size, cfgm.intermediate_size, cfgm.num_hidden_layers

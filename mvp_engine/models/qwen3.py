@@ -180,9 +180,8 @@ class Qwen3DecoderLayer(nn.Module):
             h = x
         else:
             hn, h = self.input_layernorm(x, residual)
-        if tp is not None:
-            hn = tp.enter(hn)
-        qkv = ops.linear(hn, self.fused_weight("qkv", hn))
+        qkv = (tp.column_linear(hn, self.fused_weight("qkv", hn)) if tp is not None
+               else ops.linear(hn, self.fused_weight("qkv", hn)))
         Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
         q, k = ops.qk_norm_rope(
             qkv, Hq, Hkv, _as_compute(attn.q_norm.weight, hn), _as_compute(attn.k_norm.weight, hn),
@@ -190,17 +189,15 @@ class Qwen3DecoderLayer(nn.Module):
         )
         v = qkv[:, (Hq + Hkv) * D:].view(-1, Hkv, D)
         o = ctx.attention(q, k, v, attn.scaling)
-        o = ops.linear(o.reshape(o.shape[0], Hq * D), _as_compute(attn.o_proj.weight, hn))
-        if tp is not None:
-            o = tp.exit(o)
+        o = o.reshape(o.shape[0], Hq * D)
+        wo = _as_compute(attn.o_proj.weight, hn)
+        o = tp.row_linear(o, wo) if tp is not None else ops.linear(o, wo)
         hn2, h2 = self.post_attention_layernorm(o, h)
-        if tp is not None:
-            hn2 = tp.enter(hn2)
-        gu = ops.linear(hn2, self.fused_weight("gate_up", hn2))
+        wgu = self.fused_weight("gate_up", hn2)
+        gu = tp.column_linear(hn2, wgu) if tp is not None else ops.linear(hn2, wgu)
         act = ops.swiglu(gu)
-        out = ops.linear(act, _as_compute(self.mlp.down_proj.weight, act))
-        if tp is not None:
-            out = tp.exit(out)
+        wd = _as_compute(self.mlp.down_proj.weight, act)
+        out = tp.row_linear(act, wd) if tp is not None else ops.linear(act, wd)
         return out, h2
 
 

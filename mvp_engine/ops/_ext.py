@@ -21,6 +21,7 @@ KERNELS_PER_CALL = {
     "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 1, "swiglu_fwd": 1,
     "swiglu_bwd": 1, "ce_fwd": 1, "ce_bwd_": 1, "adamw_step_": 1, "sumsq": 1, "embedding_fwd": 1,
     "embedding_bwd_": 1, "flash_attn_fwd": 1, "flash_attn_bwd": 3, "peer_reduce_scatter": 1, "peer_barrier": 1,
+    "peer_push_rows": 2, "peer_wait_all": 1, "peer_slot_reduce": 1, "gemm_pair_tp": 1,
 }
 launch_count = 0
 counting = False

@@ -49,6 +49,18 @@ void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vecto
 void peer_barrier(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
                   int64_t status_ptr, int64_t timeout_ns);
 
+void peer_push_rows(const torch::Tensor& src, const std::vector<int64_t>& dsts, int64_t dst_row0,
+                    const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                    int64_t status_ptr, int64_t timeout_ns);
+void peer_wait_all(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                   int64_t status_ptr, int64_t timeout_ns);
+void peer_slot_reduce(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
+                      int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns);
+void gemm_pair_tp(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const c10::optional<torch::Tensor>& c,
+                  int64_t ldc, int64_t a_slots, int64_t a_seq, int64_t a_rows, int64_t a_first_row,
+                  const std::vector<int64_t>& dst, int64_t dst_rows, int64_t dst_row0, int64_t status_ptr,
+                  int64_t wait_ns);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mvp_engine sm_100a kernels";
   m.def("gemm", &gemm_sm100, "tcgen05 bf16 GEMM C (+)= A * B^T with K- or MN-major operands");
@@ -70,6 +82,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_reduce_scatter", &peer_reduce_scatter,
         "pull reduce-scatter of a symmetric fp32 buffer over NVLink peers (bounded waits)");
   m.def("peer_barrier", &peer_barrier, "device-side barrier over peer signal slots (bounded)");
+  m.def("peer_push_rows", &peer_push_rows, "copy a row slice into every rank's gather buffer, then publish");
+  m.def("peer_wait_all", &peer_wait_all, "wait (bounded) until every rank published a sequence number");
+  m.def("peer_slot_reduce", &peer_slot_reduce, "sum routed partial slots after the publish / wait handshake");
+  m.def("gemm_pair_tp", &gemm_pair_tp, "two-SM GEMM with per-slice A readiness and routed output rows");
   m.def("flash_attn_bwd", &flash_attn_bwd, "varlen flash attention backward (tcgen05)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("cu_seqlens"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"), py::arg("dk_out") = py::none(),

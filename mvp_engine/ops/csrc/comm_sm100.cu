@@ -217,3 +217,154 @@ void peer_barrier(const std::vector<int64_t>& peer_slots, int64_t my_slots, int6
   slots_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ----------------------------------------------------------------------------
+// Tensor-parallel all-gather / reduce-scatter halves around the two-SM GEMM.
+//
+// All-gather by pushing: every rank copies its row slice into the gather buffer of every rank
+// (same offsets; peers' buffers are mapped), then publishes a sequence number; the consuming
+// GEMM waits per row slice (gemm_pair_tp), so it starts on the rows it already holds.
+// Reduce-scatter by routing: the producing GEMM writes row block d of its partial result into
+// rank d's slot buffer (slot = source rank); rank d then publishes, waits for every source and
+// sums its slots.
+namespace mvp {
+namespace comm {
+
+// Destination bases travel in p.peers (the ranks' gather buffers).
+__global__ void __launch_bounds__(256) push_rows_kernel(RsParams p, const uint4* __restrict__ src, int64_t n16,
+                                                        int64_t dst_off16) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = src[i];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < p.world) reinterpret_cast<uint4*>(const_cast<float*>(p.peers[r]))[dst_off16 + i] = v;
+  }
+  __threadfence_system();
+}
+
+__global__ void publish_kernel(RsParams p) {
+  if (threadIdx.x < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_slots[threadIdx.x] + p.rank, p.seq);
+  }
+}
+
+__global__ void wait_all_kernel(RsParams p) {
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < p.world; ++r) {
+      while (ld_acquire_sys(p.my_slots + r) < p.seq) {
+        if (globaltimer() - t0 > p.timeout_ns) {
+          atomicCAS(p.status, 0, kTimeoutPeer);
+          return;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+}
+
+// out[i] = sum over sources s of slots[s * n + i] (bf16 in, fp32 sum, bf16 out), after publishing this
+// rank's routed writes and seeing every source's.
+__global__ void __launch_bounds__(256) slot_reduce_kernel(RsParams p, const __nv_bfloat16* __restrict__ slots,
+                                                          __nv_bfloat16* __restrict__ out, int64_t n) {
+  __shared__ int s_ok;
+  if (blockIdx.x == 0 && threadIdx.x < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_slots[threadIdx.x] + p.rank, p.seq);
+  }
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < p.world && ok; ++r) {
+      while (ld_acquire_sys(p.my_slots + r) < p.seq) {
+        if (globaltimer() - t0 > p.timeout_ns) {
+          atomicCAS(p.status, 0, kTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int64_t n8 = n / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < p.world; ++s) {
+      const uint4 v = reinterpret_cast<const uint4*>(slots + static_cast<int64_t>(s) * n)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(h[t]);
+        acc[2 * t] += f.x;
+        acc[2 * t + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+}  // namespace comm
+}  // namespace mvp
+
+// Copy src (contiguous bf16, `rows` x `cols`) to rows [dst_row0, dst_row0 + rows) of every rank's
+// buffer (bases in `dsts`, row stride `cols`), then publish `seq` to every rank.
+void peer_push_rows(const torch::Tensor& src, const std::vector<int64_t>& dsts, int64_t dst_row0,
+                    const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                    int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.is_contiguous() && src.dim() == 2,
+              "peer_push_rows: contiguous 2-D bf16 source");
+  TORCH_CHECK((src.size(1) * 2) % 16 == 0, "peer_push_rows: rows must be multiples of 16 bytes");
+  const at::cuda::CUDAGuard guard(src.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  RsParams p = make_params(dsts, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  const int64_t n16 = src.numel() * 2 / 16;
+  const int64_t off16 = dst_row0 * src.size(1) * 2 / 16;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(2 * 148, (n16 + 255) / 256)));
+  push_rows_kernel<<<blocks, 256, 0, stream>>>(p, reinterpret_cast<const uint4*>(src.data_ptr()), n16, off16);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  publish_kernel<<<1, 32, 0, stream>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void peer_wait_all(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                   int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  std::vector<int64_t> dummy(peer_slots.size(), 0);
+  RsParams p = make_params(dummy, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  wait_all_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out = sum over the `world` slot blocks of `slots` (contiguous [world, rows, cols] bf16) after the
+// publish / wait handshake on `seq`.
+void peer_slot_reduce(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
+                      int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kBFloat16 && slots.is_contiguous(),
+              "peer_slot_reduce: contiguous bf16 slots");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() % 8 == 0,
+              "peer_slot_reduce: contiguous bf16 output, 8-element multiple");
+  std::vector<int64_t> dummy(peer_slots.size(), 0);
+  RsParams p = make_params(dummy, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  TORCH_CHECK(slots.numel() == out.numel() * p.world, "peer_slot_reduce: slots = world x output");
+  const at::cuda::CUDAGuard guard(out.device());
+  const int64_t n = out.numel();
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(2 * 148, (n / 8 + 255) / 256)));
+  slot_reduce_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p, reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

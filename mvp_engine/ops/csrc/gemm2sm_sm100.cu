@@ -53,6 +53,20 @@ struct Params {
   int64_t ldc;
   int* status;
   int group_m;
+  // Tensor-parallel fusion (both optional):
+  //  * rows of a K-major A arrive from other ranks: rows [j*a_rows, (j+1)*a_rows) are usable once
+  //    a_slots[j] >= a_seq (published by rank j after pushing them here); tiles start at row
+  //    a_first_row so a rank begins with the rows it already holds.
+  const unsigned long long* a_slots;
+  unsigned long long a_seq;
+  int a_rows;
+  int a_first_row;
+  unsigned long long wait_ns;
+  //  * bf16 output rows are routed to other ranks: row m goes to row (dst_row0 + m % dst_rows) of
+  //    the buffer at dst[m / dst_rows] (a peer's memory), row stride ldc.
+  void* dst[8];
+  int dst_rows;
+  int dst_row0;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -114,6 +128,12 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
 __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& tm, int& tn) {
@@ -184,11 +204,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_phase = 0;
+      uint32_t ready = 0;  // A row slices already seen published
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         int tm, tn;
         tile_coords(t, num_m, num_n, p.group_m, tm, tn);
+        tm = (tm + p.a_first_row / TILE) % num_m;
         const int m0 = tm * TILE + crank * HALF, n0 = tn * TILE + crank * HALF;
+        if (p.a_slots != nullptr) {
+          const int j = (tm * TILE) / p.a_rows;
+          if (!((ready >> j) & 1u)) {
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_sys_u64(p.a_slots + j) < p.a_seq) {
+              if (*abort_flag || globaltimer() - t0 > p.wait_ns) {
+                if (!*abort_flag) record_status(p.status, kTimeoutPeer);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+              __nanosleep(128);
+            }
+            if (!ok) break;
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // peer-written rows, read by TMA
+            ready |= 1u << j;
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, abort_flag, p.status, kTimeoutProducer)) {
             ok = false;
@@ -279,6 +319,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
       int tm, tn;
       tile_coords(t, num_m, num_n, p.group_m, tm, tn);
+      tm = (tm + p.a_first_row / TILE) % num_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!__all_sync(0xffffffffu,
@@ -296,7 +337,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!row_ok || n >= p.N) continue;
         const bool full_chunk = (n + 32 <= p.N);
         if constexpr (EPI == kStoreBf16) {
-          __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
+          __nv_bfloat16* C = p.dst_rows > 0
+                                 ? reinterpret_cast<__nv_bfloat16*>(p.dst[m / p.dst_rows]) +
+                                       static_cast<int64_t>(p.dst_row0 + m % p.dst_rows) * p.ldc + n
+                                 : reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
           if (full_chunk && ((reinterpret_cast<uintptr_t>(C) & 15) == 0)) {
             uint4* dst = reinterpret_cast<uint4*>(C);
 #pragma unroll
@@ -340,6 +384,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       remote_arrive(leader_tempty0 + acc * 8);
     }
+    if (p.dst_rows > 0) __threadfence_system();  // routed rows visible to their owners before the publish
   }
 
   // Both CTAs: every role is done (the leader's MMAs have retired); then free the pair's TMEM.
@@ -413,9 +458,71 @@ void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, 
   p.ldc = c.stride(0);
   p.status = reinterpret_cast<int*>(status_ptr);
   p.group_m = 8;
+  p.a_slots = nullptr;
+  p.a_seq = 0;
+  p.a_rows = 0;
+  p.a_first_row = 0;
+  p.wait_ns = 0;
+  for (int j = 0; j < 8; ++j) p.dst[j] = nullptr;
+  p.dst_rows = 0;
+  p.dst_row0 = 0;
   const int sms = mvp::num_sms(a.get_device());
   const int epi = out_f32 ? (accumulate ? kAccumF32 : kStoreF32) : kStoreBf16;
   if (epi == kStoreBf16) dispatch<kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
   else if (epi == kStoreF32) dispatch<kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
   else dispatch<kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+}
+
+// Tensor-parallel GEMM on the two-SM kernel, bf16 out, K-major A [M, K] and B [N, K]
+// (or N-major B [K, N] when b_mn).
+//   a_slots != 0: A's rows arrive in slices of a_rows rows (slice j usable once slot j >= a_seq);
+//                 the rank owning slice a_first_row / a_rows starts there.
+//   dst non-empty: output row m is written to row dst_row0 + m % dst_rows of dst[m / dst_rows]
+//                  (row stride ldc); otherwise to c.
+void gemm_pair_tp(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const c10::optional<torch::Tensor>& c,
+                  int64_t ldc, int64_t a_slots, int64_t a_seq, int64_t a_rows, int64_t a_first_row,
+                  const std::vector<int64_t>& dst, int64_t dst_rows, int64_t dst_row0, int64_t status_ptr,
+                  int64_t wait_ns) {
+  using namespace mvp::gemm2;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "gemm_pair_tp: bf16 CUDA operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 && a.stride(0) % 8 == 0 &&
+                  b.stride(0) % 8 == 0,
+              "gemm_pair_tp: row-major operands with 16-byte row strides");
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_pair_tp: reduction sizes differ");
+  TORCH_CHECK(M >= TILE && N >= TILE && M % TILE == 0, "gemm_pair_tp: M, N >= 256 and M % 256 == 0");
+  TORCH_CHECK(a_slots == 0 || (a_rows % TILE == 0 && M % a_rows == 0 && M / a_rows <= 32 && a_first_row % TILE == 0),
+              "gemm_pair_tp: A slices must be whole 256-row tiles");
+  TORCH_CHECK(dst.empty() || (dst.size() <= 8 && dst_rows > 0 && M == dst_rows * static_cast<int64_t>(dst.size())),
+              "gemm_pair_tp: output routing covers M with <= 8 destinations");
+  TORCH_CHECK(!dst.empty() || (c.has_value() && c->scalar_type() == at::kBFloat16 && c->size(0) == M &&
+                               c->size(1) == N && c->stride(1) == 1),
+              "gemm_pair_tp: bf16 output [M, N]");
+  TORCH_CHECK(ldc % 8 == 0 && ldc >= N, "gemm_pair_tp: ldc");
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta, tb;
+  mvp::make_tmap_2d_bf16(&ta, a.data_ptr(), K, M, a.stride(0), 64, HALF);
+  if (!b_mn) mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), K, N, b.stride(0), 64, HALF);
+  else mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), N, K, b.stride(0), 64, 64);
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = dst.empty() ? c->data_ptr() : nullptr;
+  p.ldc = ldc;
+  p.status = reinterpret_cast<int*>(status_ptr);
+  p.group_m = 8;
+  p.a_slots = reinterpret_cast<const unsigned long long*>(a_slots);
+  p.a_seq = static_cast<unsigned long long>(a_seq);
+  p.a_rows = static_cast<int>(a_rows);
+  p.a_first_row = static_cast<int>(a_first_row);
+  p.wait_ns = static_cast<unsigned long long>(wait_ns);
+  for (int j = 0; j < 8; ++j) p.dst[j] = j < static_cast<int>(dst.size()) ? reinterpret_cast<void*>(dst[j]) : nullptr;
+  p.dst_rows = static_cast<int>(dst_rows);
+  p.dst_row0 = static_cast<int>(dst_row0);
+  const int sms = mvp::num_sms(a.get_device());
+  dispatch<kStoreBf16>(false, b_mn, ta, tb, p, sms, stream);
 }

@@ -207,9 +207,77 @@ def bench_peer_rs(mbytes: int, iters: int) -> None:
     dist.destroy_process_group()
 
 
+def bench_tp_gemm(tokens: int, hidden: int, iters: int) -> None:
+    """Tensor-parallel GEMMs with the collective fused over NVLink vs NCCL + GEMM (launch with torchrun).
+
+    column: y[T, H] = all_gather_seq(x[T/W, H]) @ Wc^T;  row: y[T/W, H] = reduce_scatter_seq(x[T, H] @ Wr^T).
+    Device time per call, median of `iters`, max over ranks; roofline = max(FLOPs at the measured bf16
+    burst peak, this rank's NVLink bytes at 770 GB/s)."""
+    import torch.distributed as dist
+
+    from mvp_engine import ops
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.ops import _ext
+    from mvp_engine.parallel.tensor_parallel import TensorParallel, _AGLinear, _RSLinear
+
+    initialize_process_group()
+    W, r = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tp = TensorParallel(dist.group.WORLD, sequence_parallel=True, fused=True)
+    rows = tokens // W
+    x_sp = torch.randn(rows, hidden, device=dev).bfloat16()
+    x_full = torch.randn(tokens, hidden, device=dev).bfloat16()
+    wc = torch.randn(hidden, hidden, device=dev).bfloat16()
+    wr = torch.randn(hidden, hidden, device=dev).bfloat16()
+    gathered = torch.empty(tokens, hidden, device=dev, dtype=torch.bfloat16)
+    out_sp = torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16)
+
+    def nccl_col():
+        dist.all_gather_into_tensor(gathered, x_sp)
+        return ops.gemm(gathered, wc)
+
+    def nccl_row():
+        dist.reduce_scatter_tensor(out_sp, ops.gemm(x_full, wr))
+
+    cases = {"column_fused": lambda: _AGLinear.apply(x_sp, wc, tp), "column_nccl": nccl_col,
+             "row_fused": lambda: _RSLinear.apply(x_full, wr, tp), "row_nccl": nccl_row}
+    res = {}
+    for name, fn in cases.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            dist.barrier()
+            torch.cuda.synchronize()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            fn()
+            e_.record()
+            torch.cuda.synchronize()
+            ts.append(s_.elapsed_time(e_))
+        t = torch.tensor([sorted(ts)[len(ts) // 2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = float(t)
+    _ext.check_status(dev)
+    flops = 2.0 * tokens * hidden * hidden
+    wire = (W - 1) / W * tokens * hidden * 2
+    peak = 1675e12
+    roof_ms = max(flops / peak, wire / 770e9) * 1e3
+    if r == 0:
+        print(json.dumps({"kernel": "gemm_pair_tp", "world": W, "tokens": tokens, "hidden": hidden,
+                          **{k + "_ms": round(v, 4) for k, v in res.items()},
+                          "roofline_ms": round(roof_ms, 4),
+                          "column_fused_frac_of_roofline": round(roof_ms / res["column_fused"], 3),
+                          "row_fused_frac_of_roofline": round(roof_ms / res["row_fused"], 3)}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "peer_rs"])
+    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm"])
+    ap.add_argument("--hidden", type=int, default=5120, help="tp_gemm: hidden size (square weights)")
     ap.add_argument("--mbytes", type=int, default=768, help="peer_rs: unit size in MiB")
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--heads", default="32,8")
@@ -225,6 +293,8 @@ def main() -> None:
             M, N, K = (int(v) for v in args.shape.split(","))
             shapes = {"custom": (M, N, K)}
         bench_gemm(shapes, args.iters)
+    elif args.what == "tp_gemm":
+        bench_tp_gemm(args.tokens if args.tokens != 8192 else 4096, args.hidden, args.iters)
     elif args.what == "peer_rs":
         bench_peer_rs(args.mbytes, args.iters)
     elif args.what == "attention":
