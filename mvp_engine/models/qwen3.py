@@ -180,9 +180,19 @@ class Qwen3DecoderLayer(nn.Module):
             h = x
         else:
             hn, h = self.input_layernorm(x, residual)
+        Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
+        cp = ctx.cp
+        if tp is None and cp is not None and cp.ulysses_fused(hn, Hq, Hkv, D):
+            # context parallel (Ulysses) with the all-to-alls fused into the producing kernels
+            o = cp.ulysses_block(hn, self.fused_weight("qkv", hn), _as_compute(attn.q_norm.weight, hn),
+                                 _as_compute(attn.k_norm.weight, hn), _as_compute(attn.o_proj.weight, hn), ctx,
+                                 Hq, Hkv, D, attn.q_norm.variance_epsilon, attn.scaling)
+            hn2, h2 = self.post_attention_layernorm(o, h)
+            wgu = self.fused_weight("gate_up", hn2)
+            act = ops.swiglu(ops.linear(hn2, wgu))
+            return ops.linear(act, _as_compute(self.mlp.down_proj.weight, act)), h2
         qkv = (tp.column_linear(hn, self.fused_weight("qkv", hn)) if tp is not None
                else ops.linear(hn, self.fused_weight("qkv", hn)))
-        Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
         q, k = ops.qk_norm_rope(
             qkv, Hq, Hkv, _as_compute(attn.q_norm.weight, hn), _as_compute(attn.k_norm.weight, hn),
             ctx.position_ids, ctx.rope, attn.q_norm.variance_epsilon,
@@ -345,6 +355,8 @@ class Qwen3ForCausalLM(nn.Module):
         if position_ids is None:
             position_ids = positions_from_cu_seqlens(cu, T)
         pos = position_ids.reshape(-1, T) if position_ids.dim() <= 2 else position_ids.reshape(position_ids.shape[0], -1)
+        if input_ids.is_cuda:  # RoPE tables cover every position of the longest document
+            self.model.rope.tables(input_ids.device, int(max_length_q))
         return PackedContext(pos, cu, int(max_length_q), self.model.rope, cp=cp)
 
     def forward(self, input_ids: torch.Tensor, *args: Any, **kwargs: Any) -> dict:

@@ -22,6 +22,7 @@ KERNELS_PER_CALL = {
     "swiglu_bwd": 1, "ce_fwd": 1, "ce_bwd_": 1, "adamw_step_": 1, "sumsq": 1, "embedding_fwd": 1,
     "embedding_bwd_": 1, "flash_attn_fwd": 1, "flash_attn_bwd": 3, "peer_reduce_scatter": 1, "peer_barrier": 1,
     "peer_push_rows": 2, "peer_wait_all": 1, "peer_slot_reduce": 1, "gemm_pair_tp": 1,
+    "peer_publish": 1, "peer_slot_sum_f32": 1, "gemm_ulysses": 1,
 }
 launch_count = 0
 counting = False

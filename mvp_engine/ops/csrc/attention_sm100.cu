@@ -39,6 +39,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "peer_host.h"
 #include "tma_host.h"
 
 namespace mvp {
@@ -62,6 +63,8 @@ struct FwdParams {
   float scale_log2;
   int causal;
   int* status;
+  PeerPull pull;  // optional copy of the next ring hop's K/V, carried by grid rows 0 .. pull.rows-1
+  UlyssesRoute route;  // optional: O rows also written to the token's rank (o_proj input layout)
 };
 
 // Largest d with cu[d] <= i (cu has n_docs + 1 entries): the non-empty document holding row i.
@@ -143,10 +146,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* lsum_bar = bars + 18; // the two halves exchanged their row sums (256 arrivals)
   float* xmax = reinterpret_cast<float*>(bars + 20);  // [2 parity][2 halves][128 rows] maxima, then [2][128] sums
 
+  if (static_cast<int>(blockIdx.y) < p.pull.rows) {  // copy CTA: pull the next hop's K/V, no attention
+    peer_pull_cta(p.pull, p.status, reinterpret_cast<int*>(smem));
+    return;
+  }
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int qb = blockIdx.x;
-  const int h = blockIdx.y;
+  const int h = blockIdx.y - p.pull.rows;
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qb * BLK;
 
@@ -397,6 +404,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + static_cast<int64_t>(i) * p.o_row_stride + h * D + half * 64;
+      __nv_bfloat16* urow = nullptr;  // the same row in the token rank's o_proj input (Ulysses)
+      if (p.route.dst[0] != nullptr && valid) {
+        int owner, lrow;
+        ulysses_home(p.route, i, owner, lrow);
+        urow = reinterpret_cast<__nv_bfloat16*>(p.route.dst[owner]) + static_cast<int64_t>(lrow) * p.route.ld +
+               p.route.col0 + h * D + half * 64;
+      }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t rr[32];
@@ -416,9 +430,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             pk.z = pack_bf16x2(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
             pk.w = pack_bf16x2(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = pk;
+            if (urow != nullptr) *reinterpret_cast<uint4*>(urow + c * 32 + v * 8) = pk;
           }
         }
       }
+      if (urow != nullptr) __threadfence_system();
       if (valid && half == 0) p.lse[static_cast<int64_t>(h) * p.T + i] = (l > 0.f) ? (m + log2f(l)) / kLog2e : -INFINITY;
     }
   }
@@ -442,7 +458,9 @@ constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 160 + 3 * 256 * 4;  // tiles, a
 // stream has its own documents; Tk == T otherwise).  Returns (o [T, Hq, 128], lse [Hq, T]).
 std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
-                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k) {
+                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k,
+                                          const c10::optional<std::vector<int64_t>>& pull,
+                                          const c10::optional<std::vector<int64_t>>& route) {
   using namespace mvp::attn;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
               "flash_attn_fwd: bf16 inputs");
@@ -465,13 +483,14 @@ std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::T
   const at::cuda::CUDAGuard guard(q.device());
   auto o = torch::empty({T, Hq, D}, q.options());
   auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
-  if (T == 0) return {o, lse};
-  CUtensorMap tq, tk, tv;
-  if (Tk == 0) {  // nothing to attend: zero output, -inf LSE
+  const mvp::PeerPull pj = mvp::make_peer_pull(pull);
+  if (T == 0 || Tk == 0) {  // nothing to attend: zero output, -inf LSE (the copy still runs)
     o.zero_();
     lse.fill_(-INFINITY);
+    mvp::launch_peer_pull(pj, reinterpret_cast<int*>(status_ptr), at::cuda::getCurrentCUDAStream());
     return {o, lse};
   }
+  CUtensorMap tq, tk, tv;
   mvp::make_tmap_2d_bf16(&tq, q.data_ptr(), static_cast<int64_t>(Hq) * D, T, q.stride(0), 64, BLK);
   mvp::make_tmap_2d_bf16(&tk, k.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, k.stride(0), 64, BLK);
   mvp::make_tmap_2d_bf16(&tv, v.data_ptr(), static_cast<int64_t>(Hkv) * D, Tk, v.stride(0), 64, BLK);
@@ -489,12 +508,16 @@ std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::T
   p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
   p.causal = causal ? 1 : 0;
   p.status = reinterpret_cast<int*>(status_ptr);
+  p.pull = pj;
+  p.route = mvp::make_ulysses_route(route);
+  TORCH_CHECK(p.route.dst[0] == nullptr || T == 2 * p.route.world * p.route.chunk,
+              "flash_attn_fwd: routed rows need T = 2 x world x chunk");
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
     configured = true;
   }
-  dim3 grid((T + BLK - 1) / BLK, Hq);
+  dim3 grid((T + BLK - 1) / BLK, Hq + pj.rows);
   fwd_kernel<<<grid, kFwdThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
@@ -531,6 +554,12 @@ struct BwdParams {
   float scale, scale_log2;
   int causal;
   int* status;
+  PeerPull pull;       // optional copy of the next ring hop's K/V, carried by grid rows 0 .. pull.rows-1
+  float* dk_f32;       // optional fp32 dK / dV destination (may be another rank's memory): written, or
+  float* dv_f32;       // added to when f32_accumulate, instead of the bf16 dk / dv
+  int64_t f32_row_stride;
+  int f32_accumulate;
+  UlyssesRoute route;  // optional: dV rows written to the token's rank (dqkv layout) instead of dv
 };
 
 constexpr int kBwdThreads = 320;  // 8 gradient warps + TMA warp + MMA warp
@@ -561,9 +590,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  if (static_cast<int>(blockIdx.y) < p.pull.rows) {  // copy CTA: pull the next hop's K/V, no gradients
+    peer_pull_cta(p.pull, p.status, reinterpret_cast<int*>(smem));
+    return;
+  }
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int hk = blockIdx.y;
+  const int hk = blockIdx.y - p.pull.rows;
   const int rep = p.Hq / p.Hkv;
   const int k0 = blockIdx.x * BLK;
   const int k_last = min(k0 + BLK, p.Tk) - 1;
@@ -766,6 +799,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t tacc = which == 0 ? tdK : tdV;
         __nv_bfloat16* out = which == 0 ? p.dk + static_cast<int64_t>(kc) * p.dk_row_stride + hk * D + half * 64
                                         : p.dv + static_cast<int64_t>(kc) * p.dv_row_stride + hk * D + half * 64;
+        if (which == 1 && p.route.dst[0] != nullptr && kvalid) {
+          int owner, lrow;
+          ulysses_home(p.route, kc, owner, lrow);
+          out = reinterpret_cast<__nv_bfloat16*>(p.route.dst[owner]) + static_cast<int64_t>(lrow) * p.route.ld +
+                p.route.col0 + hk * D + half * 64;
+        }
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
           uint32_t rr[32];
@@ -776,7 +815,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
             for (int t = 0; t < 32; ++t) rr[t] = 0u;
           }
-          if (kvalid) {
+          if (kvalid && p.dk_f32 != nullptr) {  // fp32 partial sums, possibly into the owner's memory
+            float* dst = (which == 0 ? p.dk_f32 : p.dv_f32) + static_cast<int64_t>(kc) * p.f32_row_stride + hk * D +
+                         half * 64 + ch * 32;
+            float4 acc[8];
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              acc[v] = make_float4(__uint_as_float(rr[4 * v]), __uint_as_float(rr[4 * v + 1]),
+                                   __uint_as_float(rr[4 * v + 2]), __uint_as_float(rr[4 * v + 3]));
+            if (p.f32_accumulate) {
+              float4 old[8];
+#pragma unroll
+              for (int v = 0; v < 8; ++v) old[v] = reinterpret_cast<const float4*>(dst)[v];
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                acc[v].x += old[v].x;
+                acc[v].y += old[v].y;
+                acc[v].z += old[v].z;
+                acc[v].w += old[v].w;
+              }
+            }
+#pragma unroll
+            for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = acc[v];
+          } else if (kvalid) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint4 pk;
@@ -792,6 +853,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   }
 
+  if (p.route.dst[0] != nullptr) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -844,7 +906,11 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
                                           int64_t status_ptr, const c10::optional<torch::Tensor>& dk_out,
                                           const c10::optional<torch::Tensor>& dv_out,
-                                          const c10::optional<torch::Tensor>& cu_seqlens_k) {
+                                          const c10::optional<torch::Tensor>& cu_seqlens_k,
+                                          const c10::optional<std::vector<int64_t>>& pull,
+                                          const c10::optional<torch::Tensor>& dq_accum,
+                                          const c10::optional<std::vector<int64_t>>& dkv_f32,
+                                          const c10::optional<std::vector<int64_t>>& route) {
   using namespace mvp::attn;
   TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && q.is_contiguous(), "flash_attn_bwd: contiguous q/o/do");
   TORCH_CHECK(k.stride(2) == 1 && v.stride(2) == 1 && k.stride(1) == D && v.stride(1) == D,
@@ -859,17 +925,42 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
   TORCH_CHECK(cu_seqlens_k.has_value() || Tk == T, "flash_attn_bwd: Tk != T needs cu_seqlens_k");
   const at::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  auto dq_acc = torch::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
+  // dq_accum: the caller's fp32 [T, Hq, 128] accumulator (dq is added to it and returned as is);
+  // dkv_f32 = [dk_ptr, dv_ptr, row_stride, accumulate]: fp32 dK / dV destinations (e.g. another
+  // rank's accumulator slot), written or added to, instead of bf16 outputs.
+  const bool ext_dq = dq_accum.has_value();
+  if (ext_dq)
+    TORCH_CHECK(dq_accum->scalar_type() == at::kFloat && dq_accum->is_contiguous() && dq_accum->dim() == 3 &&
+                    dq_accum->size(0) == T && dq_accum->size(1) == Hq && dq_accum->size(2) == D,
+                "flash_attn_bwd: dq_accum must be contiguous fp32 [T, Hq, 128]");
+  const bool f32_kv = dkv_f32.has_value() && !dkv_f32->empty();
+  if (f32_kv) {
+    TORCH_CHECK(dkv_f32->size() == 4, "dkv_f32 = [dk_ptr, dv_ptr, row_stride, accumulate]");
+    TORCH_CHECK((*dkv_f32)[0] % 16 == 0 && (*dkv_f32)[1] % 16 == 0 && (*dkv_f32)[2] % 4 == 0 &&
+                    (*dkv_f32)[2] >= static_cast<int64_t>(Hkv) * D,
+                "dkv_f32: 16-byte aligned rows of at least Hkv x 128 floats");
+  }
+  auto dq_acc = ext_dq ? *dq_accum : torch::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
   auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
-  torch::Tensor dk = dk_out.has_value() ? *dk_out : torch::empty({Tk, Hkv, D}, q.options());
-  torch::Tensor dv = dv_out.has_value() ? *dv_out : torch::empty({Tk, Hkv, D}, q.options());
+  torch::Tensor dk = f32_kv ? torch::empty({0, Hkv, D}, q.options())
+                            : (dk_out.has_value() ? *dk_out : torch::empty({Tk, Hkv, D}, q.options()));
+  const mvp::UlyssesRoute uroute = mvp::make_ulysses_route(route);
+  const bool routed_dv = uroute.dst[0] != nullptr;
+  TORCH_CHECK(!routed_dv || (!f32_kv && Tk == 2 * uroute.world * uroute.chunk),
+              "flash_attn_bwd: routed dV rows need bf16 outputs and Tk = 2 x world x chunk");
+  torch::Tensor dv = (f32_kv || routed_dv)
+                         ? torch::empty({0, Hkv, D}, q.options())
+                         : (dv_out.has_value() ? *dv_out : torch::empty({Tk, Hkv, D}, q.options()));
   TORCH_CHECK(dk.stride(2) == 1 && dv.stride(2) == 1 && dk.stride(1) == D && dv.stride(1) == D,
               "flash_attn_bwd: dk/dv head layout");
-  auto dq = torch::empty({T, Hq, D}, q.options());
+  auto dq = ext_dq ? dq_acc : torch::empty({T, Hq, D}, q.options());
+  const mvp::PeerPull pj = mvp::make_peer_pull(pull);
   if (T == 0 || Tk == 0) {
-    dq.zero_();
+    TORCH_CHECK(!f32_kv || Tk == 0, "flash_attn_bwd: fp32 dK / dV destinations with no queries");
+    if (!ext_dq) dq.zero_();
     dk.zero_();
     dv.zero_();
+    mvp::launch_peer_pull(pj, reinterpret_cast<int*>(status_ptr), stream);
     return {dq, dk, dv};
   }
   {
@@ -903,14 +994,21 @@ std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch
   p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
   p.causal = causal ? 1 : 0;
   p.status = reinterpret_cast<int*>(status_ptr);
+  p.pull = pj;
+  p.dk_f32 = f32_kv ? reinterpret_cast<float*>((*dkv_f32)[0]) : nullptr;
+  p.dv_f32 = f32_kv ? reinterpret_cast<float*>((*dkv_f32)[1]) : nullptr;
+  p.f32_row_stride = f32_kv ? (*dkv_f32)[2] : 0;
+  p.f32_accumulate = f32_kv ? static_cast<int>((*dkv_f32)[3] != 0) : 0;
+  p.route = uroute;
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
     configured = true;
   }
-  dim3 grid((Tk + BLK - 1) / BLK, Hkv);
+  dim3 grid((Tk + BLK - 1) / BLK, Hkv + pj.rows);
   bwd_kernel<<<grid, kBwdThreads, kBwdSmem, stream>>>(tq, tk, tv, tdo, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (ext_dq) return {dq, dk, dv};
   const int64_t n = static_cast<int64_t>(T) * Hq * D;
   f32_to_bf16_kernel<<<static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 16)), 256, 0, stream>>>(
       dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);

@@ -17,7 +17,8 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
                                             const torch::Tensor& wq, const torch::Tensor& wk,
                                             const torch::Tensor& pos, const torch::Tensor& axis_of,
                                             const torch::Tensor& cos_tab, const torch::Tensor& sin_tab,
-                                            const torch::Tensor& rstd);
+                                            const torch::Tensor& rstd,
+                                            const c10::optional<std::vector<int64_t>>& route);
 torch::Tensor swiglu_fwd(const torch::Tensor& gu);
 torch::Tensor swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& dout);
 
@@ -33,14 +34,20 @@ void embedding_bwd_(torch::Tensor& dw, const torch::Tensor& dout, const torch::T
 
 std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
-                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k);
+                                          int64_t status_ptr, const c10::optional<torch::Tensor>& cu_seqlens_k,
+                                          const c10::optional<std::vector<int64_t>>& pull,
+                                          const c10::optional<std::vector<int64_t>>& route);
 
 std::vector<torch::Tensor> flash_attn_bwd(const torch::Tensor& dout, const torch::Tensor& q, const torch::Tensor& k,
                                           const torch::Tensor& v, const torch::Tensor& out, const torch::Tensor& lse,
                                           const torch::Tensor& cu_seqlens, double softmax_scale, bool causal,
                                           int64_t status_ptr, const c10::optional<torch::Tensor>& dk_out,
                                           const c10::optional<torch::Tensor>& dv_out,
-                                          const c10::optional<torch::Tensor>& cu_seqlens_k);
+                                          const c10::optional<torch::Tensor>& cu_seqlens_k,
+                                          const c10::optional<std::vector<int64_t>>& pull,
+                                          const c10::optional<torch::Tensor>& dq_accum,
+                                          const c10::optional<std::vector<int64_t>>& dkv_f32,
+                                          const c10::optional<std::vector<int64_t>>& route);
 
 void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vector<int64_t>& peer_slots,
                          int64_t my_slots, int64_t rank, int64_t offset, int64_t shard, int64_t seq, double scale,
@@ -56,6 +63,13 @@ void peer_wait_all(const std::vector<int64_t>& peer_slots, int64_t my_slots, int
                    int64_t status_ptr, int64_t timeout_ns);
 void peer_slot_reduce(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
                       int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns);
+void peer_publish(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                  int64_t status_ptr, int64_t timeout_ns);
+void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
+                       int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns);
+void gemm_ulysses(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
+                  int64_t ld, int64_t rank, int64_t chunk, int64_t head_dim, const std::vector<int64_t>& secs,
+                  int64_t status_ptr);
 void gemm_pair_tp(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const c10::optional<torch::Tensor>& c,
                   int64_t ldc, int64_t a_slots, int64_t a_seq, int64_t a_rows, int64_t a_first_row,
                   const std::vector<int64_t>& dst, int64_t dst_rows, int64_t dst_row0, int64_t status_ptr,
@@ -67,7 +81,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
-  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd, py::arg("dq"), py::arg("dk"), py::arg("qkv"), py::arg("dqkv"),
+        py::arg("Hq"), py::arg("Hkv"), py::arg("wq"), py::arg("wk"), py::arg("pos"), py::arg("axis_of"),
+        py::arg("cos_tab"), py::arg("sin_tab"), py::arg("rstd"), py::arg("route") = py::none());
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
@@ -78,16 +94,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd_", &embedding_bwd_);
   m.def("flash_attn_fwd", &flash_attn_fwd, "varlen flash attention forward (tcgen05)", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"),
-        py::arg("cu_seqlens_k") = py::none());
+        py::arg("cu_seqlens_k") = py::none(), py::arg("pull") = py::none(), py::arg("route") = py::none());
   m.def("peer_reduce_scatter", &peer_reduce_scatter,
         "pull reduce-scatter of a symmetric fp32 buffer over NVLink peers (bounded waits)");
   m.def("peer_barrier", &peer_barrier, "device-side barrier over peer signal slots (bounded)");
   m.def("peer_push_rows", &peer_push_rows, "copy a row slice into every rank's gather buffer, then publish");
   m.def("peer_wait_all", &peer_wait_all, "wait (bounded) until every rank published a sequence number");
   m.def("peer_slot_reduce", &peer_slot_reduce, "sum routed partial slots after the publish / wait handshake");
+  m.def("gemm_ulysses", &gemm_ulysses, "two-SM GEMM whose epilogue scatters heads to their context ranks");
   m.def("gemm_pair_tp", &gemm_pair_tp, "two-SM GEMM with per-slice A readiness and routed output rows");
   m.def("flash_attn_bwd", &flash_attn_bwd, "varlen flash attention backward (tcgen05)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("cu_seqlens"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("status_ptr"), py::arg("dk_out") = py::none(),
-        py::arg("dv_out") = py::none(), py::arg("cu_seqlens_k") = py::none());
+        py::arg("dv_out") = py::none(), py::arg("cu_seqlens_k") = py::none(), py::arg("pull") = py::none(),
+        py::arg("dq_accum") = py::none(), py::arg("dkv_f32") = py::none(), py::arg("route") = py::none());
+  m.def("peer_publish", &peer_publish, "publish a sequence number into every rank's signal slot");
+  m.def("peer_slot_sum_f32", &peer_slot_sum_f32,
+        "publish, wait for every rank, then sum fp32 partial slots [W, n] into bf16 [n]");
 }

@@ -25,6 +25,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "peer_host.h"
 
 namespace mvp {
 namespace comm {
@@ -45,15 +46,6 @@ struct RsParams {
   int* status;
   unsigned long long timeout_ns;         // bound of every wait for a peer
 };
-
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(256) rs_pull_kernel(RsParams p) {
   __shared__ int s_ok;
@@ -366,5 +358,107 @@ void peer_slot_reduce(const torch::Tensor& slots, torch::Tensor& out, const std:
   slot_reduce_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       p, reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
       n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ----------------------------------------------------------------------------
+// Stand-alone peer pull (the compute kernels carry the same copy in extra CTAs).
+namespace mvp {
+
+__global__ void __launch_bounds__(256) peer_pull_kernel(PeerPull j, int* status) {
+  __shared__ int flag;
+  peer_pull_cta(j, status, &flag);
+}
+
+void launch_peer_pull(const PeerPull& j, int* status, cudaStream_t stream) {
+  if (j.rows == 0) return;
+  PeerPull k = j;
+  k.rows = 1;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(148, (j.n16 + 2047) / 2048)));
+  peer_pull_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(k, status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mvp
+
+// ----------------------------------------------------------------------------
+// Routed fp32 partial sums (ring attention dK / dV): every source rank writes its partial into
+// slot [source] of the owner's symmetric buffer; the owner publishes, waits for every source's
+// publication of the same sequence number and sums the slots into bf16.
+namespace mvp {
+namespace comm {
+
+__global__ void __launch_bounds__(256) slot_sum_f32_kernel(RsParams p, const float* __restrict__ slots,
+                                                           __nv_bfloat16* __restrict__ out, int64_t n) {
+  __shared__ int s_ok;
+  if (blockIdx.x == 0 && threadIdx.x < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_slots[threadIdx.x] + p.rank, p.seq);
+  }
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < p.world && ok; ++r) {
+      while (ld_acquire_sys(p.my_slots + r) < p.seq) {
+        if (globaltimer() - t0 > p.timeout_ns) {
+          atomicCAS(p.status, 0, kTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < p.world; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(slots + static_cast<int64_t>(s) * n)[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(acc.x, acc.y);
+    o.y = pack_bf16x2(acc.z, acc.w);
+    reinterpret_cast<uint2*>(out)[i] = o;
+  }
+}
+
+}  // namespace comm
+}  // namespace mvp
+
+void peer_publish(const std::vector<int64_t>& peer_slots, int64_t my_slots, int64_t rank, int64_t seq,
+                  int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  std::vector<int64_t> dummy(peer_slots.size(), 0);
+  RsParams p = make_params(dummy, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  publish_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out [n] (bf16) = sum over the `world` fp32 slots of `slots` [world, n], after the publish / wait
+// handshake on `seq` (every source's routed writes into this rank's slots are complete).
+void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
+                       int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns) {
+  using namespace mvp::comm;
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kFloat && slots.is_contiguous(),
+              "peer_slot_sum_f32: contiguous fp32 slots");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() % 4 == 0,
+              "peer_slot_sum_f32: contiguous bf16 output, 4-element multiple");
+  std::vector<int64_t> dummy(peer_slots.size(), 0);
+  RsParams p = make_params(dummy, peer_slots, my_slots, static_cast<int>(rank), seq, status_ptr, timeout_ns);
+  TORCH_CHECK(slots.numel() == out.numel() * p.world, "peer_slot_sum_f32: slots = world x output");
+  const at::cuda::CUDAGuard guard(out.device());
+  const int64_t n = out.numel();
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(2 * 148, (n / 4 + 255) / 256)));
+  slot_sum_f32_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p, slots.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -245,6 +245,93 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ------------------------------------------------------- peer memory (NVLink)
+// Release / acquire at system scope: a flag another GPU reads (or writes) orders the data around it.
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// A copy of another rank's buffer into this GPU's memory, carried by extra CTAs of a compute
+// kernel (grid rows blockIdx.y < rows) so that the transfer overlaps the kernel's own tiles.
+// The copy starts once the owner has published `seq` into `ready` (a slot in this GPU's memory
+// that the owner writes with a system-scope release); the wait is bounded by timeout_ns, after
+// which the status word records kTimeoutPeer and nothing is read.
+struct PeerPull {
+  const uint4* src;  // the owner's buffer, mapped into this process
+  uint4* dst;        // this GPU's buffer
+  int64_t n16;       // 16-byte units
+  const unsigned long long* ready;
+  unsigned long long seq;
+  unsigned long long timeout_ns;
+  int rows;  // grid rows given to the copy (0: no copy)
+};
+
+// Body of one copy CTA (all threads of the CTA call it; `flag` is one int of shared memory).
+__device__ __forceinline__ void peer_pull_cta(const PeerPull& j, int* status, int* flag) {
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(j.ready) < j.seq) {
+      if (globaltimer() - t0 > j.timeout_ns) {
+        record_status(status, kTimeoutPeer);
+        ok = 0;
+        break;
+      }
+      __nanosleep(128);
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    *flag = ok;
+  }
+  __syncthreads();
+  if (!*flag) return;
+  constexpr int kUnroll = 8;  // 16-byte loads in flight per thread: covers the NVLink round trip
+  const int64_t cta = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+  const int64_t stride = static_cast<int64_t>(j.rows) * gridDim.x * blockDim.x;
+  for (int64_t i0 = cta * blockDim.x + threadIdx.x; i0 < j.n16; i0 += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < j.n16) v[u] = j.src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < j.n16) j.dst[i] = v[u];
+    }
+  }
+}
+
+// ---------------------------------------------- Ulysses (sequence <-> head) routing
+// Context-parallel ranks hold a packed row in zig-zag order: with W ranks the row is cut into 2W chunks
+// of `chunk` tokens and rank r keeps chunks r and 2W-1-r (its local rows 0..chunk-1 and chunk..2chunk-1).
+// Head-parallel tensors ([T tokens, this rank's heads]) are written back to the token's rank by a
+// producing kernel through this descriptor.
+struct UlyssesRoute {
+  void* dst[8];  // every rank's destination buffer (peer-mapped); dst[0] == nullptr: no routing
+  int64_t ld;    // destination row stride in elements
+  int world, rank, chunk;
+  int col0;      // destination column of this rank's first head (first section)
+  int col0_k;    // same for a second section (kernels writing q and k)
+};
+
+// Rank and local row of global token i.
+__device__ __forceinline__ void ulysses_home(const UlyssesRoute& u, int i, int& owner, int& row) {
+  const int c = i / u.chunk;
+  owner = c < u.world ? c : 2 * u.world - 1 - c;
+  row = (c < u.world ? 0 : u.chunk) + (i - c * u.chunk);
+}
+
+// Global token of local row m on `rank`.
+__device__ __forceinline__ int ulysses_global_row(int world, int rank, int chunk, int m) {
+  return m < chunk ? rank * chunk + m : (2 * world - 1 - rank) * chunk + (m - chunk);
+}
+
 // Named barrier among a subset of warps (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

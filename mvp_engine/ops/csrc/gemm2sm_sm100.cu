@@ -67,6 +67,13 @@ struct Params {
   void* dst[8];
   int dst_rows;
   int dst_row0;
+  //  * Ulysses sequence -> head routing (u_world > 0): output row m (this rank's local token) goes to
+  //    global row ulysses_global_row(m) of dst[d], where column n of section s (u_sec[s] heads of
+  //    u_hd columns, each section split evenly over the u_world ranks) belongs to rank
+  //    d = head / (u_sec[s] / u_world); on rank d the sections are packed side by side (this rank's
+  //    share of section 0, then of section 1, ...), row stride ldc.
+  int u_world, u_rank, u_chunk, u_hd;
+  int u_sec[3];
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -341,6 +348,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                                  ? reinterpret_cast<__nv_bfloat16*>(p.dst[m / p.dst_rows]) +
                                        static_cast<int64_t>(p.dst_row0 + m % p.dst_rows) * p.ldc + n
                                  : reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
+          if (p.u_world > 0) {  // a 32-column chunk never straddles a head (u_hd % 32 == 0)
+            int col = n, prefix = 0, s = 0;
+            while (s < 2 && col >= p.u_sec[s] * p.u_hd) {
+              col -= p.u_sec[s] * p.u_hd;
+              prefix += (p.u_sec[s] / p.u_world) * p.u_hd;
+              ++s;
+            }
+            const int per = p.u_sec[s] / p.u_world;
+            const int head = col / p.u_hd;
+            const int d = head / per;
+            const int g = ulysses_global_row(p.u_world, p.u_rank, p.u_chunk, m);
+            C = reinterpret_cast<__nv_bfloat16*>(p.dst[d]) + static_cast<int64_t>(g) * p.ldc + prefix +
+                (head - d * per) * p.u_hd + col % p.u_hd;
+          }
           if (full_chunk && ((reinterpret_cast<uintptr_t>(C) & 15) == 0)) {
             uint4* dst = reinterpret_cast<uint4*>(C);
 #pragma unroll
@@ -384,7 +405,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       remote_arrive(leader_tempty0 + acc * 8);
     }
-    if (p.dst_rows > 0) __threadfence_system();  // routed rows visible to their owners before the publish
+    if (p.dst_rows > 0 || p.u_world > 0) __threadfence_system();  // routed rows visible before the publish
   }
 
   // Both CTAs: every role is done (the leader's MMAs have retired); then free the pair's TMEM.
@@ -466,6 +487,8 @@ void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, 
   for (int j = 0; j < 8; ++j) p.dst[j] = nullptr;
   p.dst_rows = 0;
   p.dst_row0 = 0;
+  p.u_world = p.u_rank = p.u_chunk = p.u_hd = 0;
+  p.u_sec[0] = p.u_sec[1] = p.u_sec[2] = 0;
   const int sms = mvp::num_sms(a.get_device());
   const int epi = out_f32 ? (accumulate ? kAccumF32 : kStoreF32) : kStoreBf16;
   if (epi == kStoreBf16) dispatch<kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
@@ -523,6 +546,68 @@ void gemm_pair_tp(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, con
   for (int j = 0; j < 8; ++j) p.dst[j] = j < static_cast<int>(dst.size()) ? reinterpret_cast<void*>(dst[j]) : nullptr;
   p.dst_rows = static_cast<int>(dst_rows);
   p.dst_row0 = static_cast<int>(dst_row0);
+  p.u_world = p.u_rank = p.u_chunk = p.u_hd = 0;
+  p.u_sec[0] = p.u_sec[1] = p.u_sec[2] = 0;
+  const int sms = mvp::num_sms(a.get_device());
+  dispatch<kStoreBf16>(false, b_mn, ta, tb, p, sms, stream);
+}
+
+// Ulysses projection on the two-SM kernel: Y = A[M = 2 x chunk local tokens, K] * B^T (B [N, K], or
+// N-major [K, N] when b_mn), bf16, with every output element written straight into the buffer of the
+// rank that owns its head (dst[d], [world x 2 x chunk tokens, ld]; see Params).  `secs` gives the heads
+// of each column section (e.g. q, k, v); N = head_dim x sum(secs).
+void gemm_ulysses(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
+                  int64_t ld, int64_t rank, int64_t chunk, int64_t head_dim, const std::vector<int64_t>& secs,
+                  int64_t status_ptr) {
+  using namespace mvp::gemm2;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "gemm_ulysses: bf16 CUDA operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 && a.stride(0) % 8 == 0 &&
+                  b.stride(0) % 8 == 0,
+              "gemm_ulysses: row-major operands with 16-byte row strides");
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t W = static_cast<int64_t>(dst.size());
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_ulysses: reduction sizes differ");
+  TORCH_CHECK(W >= 1 && W <= 8 && rank >= 0 && rank < W, "gemm_ulysses: 1..8 ranks");
+  TORCH_CHECK(M == 2 * chunk && M >= TILE && N >= TILE, "gemm_ulysses: M = 2 x chunk >= 256, N >= 256");
+  TORCH_CHECK(head_dim % 32 == 0 && secs.size() == 3, "gemm_ulysses: head_dim % 32 == 0, three sections");
+  int64_t heads = 0, per_rank = 0;
+  for (int64_t s : secs) {
+    TORCH_CHECK(s >= 0 && s % W == 0, "gemm_ulysses: every section's heads divisible by the ranks");
+    heads += s;
+    per_rank += s / W;
+  }
+  TORCH_CHECK(N == heads * head_dim, "gemm_ulysses: N = head_dim x heads");
+  TORCH_CHECK(ld % 8 == 0 && ld >= per_rank * head_dim, "gemm_ulysses: destination row stride");
+  for (int64_t d : dst) TORCH_CHECK(d != 0 && d % 16 == 0, "gemm_ulysses: 16-byte aligned destinations");
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta, tb;
+  mvp::make_tmap_2d_bf16(&ta, a.data_ptr(), K, M, a.stride(0), 64, HALF);
+  if (!b_mn) mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), K, N, b.stride(0), 64, HALF);
+  else mvp::make_tmap_2d_bf16(&tb, b.data_ptr(), N, K, b.stride(0), 64, 64);
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = nullptr;
+  p.ldc = ld;
+  p.status = reinterpret_cast<int*>(status_ptr);
+  p.group_m = 8;
+  p.a_slots = nullptr;
+  p.a_seq = 0;
+  p.a_rows = 0;
+  p.a_first_row = 0;
+  p.wait_ns = 0;
+  for (int j = 0; j < 8; ++j) p.dst[j] = j < W ? reinterpret_cast<void*>(dst[j]) : nullptr;
+  p.dst_rows = 0;
+  p.dst_row0 = 0;
+  p.u_world = static_cast<int>(W);
+  p.u_rank = static_cast<int>(rank);
+  p.u_chunk = static_cast<int>(chunk);
+  p.u_hd = static_cast<int>(head_dim);
+  for (int s = 0; s < 3; ++s) p.u_sec[s] = static_cast<int>(secs[s]);
   const int sms = mvp::num_sms(a.get_device());
   dispatch<kStoreBf16>(false, b_mn, ta, tb, p, sms, stream);
 }

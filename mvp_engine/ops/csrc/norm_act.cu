@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "peer_host.h"
 
 namespace mvp {
 namespace {
@@ -179,7 +180,10 @@ struct QKRopeArgs {
   float* rstd;           // [T, Hq + Hkv]
   int T, Hq, Hkv;
   float eps;
+  int tab_rows;          // rows of cos_tab / sin_tab; positions are clamped into [0, tab_rows)
 };
+
+__device__ __forceinline__ int clamp_pos(int p, int rows) { return min(max(p, 0), rows - 1); }
 
 __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
   constexpr int D = 128;
@@ -219,7 +223,7 @@ __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
   for (int i = 0; i < 4; ++i) {
     const int f = (lane * 4 + i) & 63;
     const int ax = a.axis_of[f];
-    const int p = a.pos[ax * a.pos_stride + t];
+    const int p = clamp_pos(a.pos[ax * a.pos_stride + t], a.tab_rows);
     const float c = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
     const float s = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
     o[i] = lo ? (y[i] * c - partner[i] * s) : (y[i] * c + partner[i] * s);
@@ -249,6 +253,8 @@ struct QKRopeBwdArgs {
   int64_t ld_dqkv;
   float* dw_partial;  // [gridDim.x, 2, D]
   int T, Hq, Hkv;
+  int tab_rows;
+  UlyssesRoute route;  // optional: dq / dk rows written to the token's rank (its dqkv) instead of dqkv
 };
 
 __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
@@ -284,7 +290,7 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
     for (int i = 0; i < 4; ++i) {
       const int f = (lane * 4 + i) & 63;
       const int ax = a.axis_of[f];
-      const int p = a.pos[ax * a.pos_stride + t];
+      const int p = clamp_pos(a.pos[ax * a.pos_stride + t], a.tab_rows);
       const float c = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
       const float s = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
       dy[i] = lo ? (g[i] * c + gp[i] * s) : (g[i] * c - gp[i] * s);
@@ -303,6 +309,12 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
       else acck[i] += dy[i] * xh;
     }
     __nv_bfloat16* dst = a.dqkv + static_cast<int64_t>(t) * a.ld_dqkv + static_cast<int64_t>(hd) * D + lane * 4;
+    if (a.route.dst[0] != nullptr) {  // Ulysses: back to the token's rank, global head columns
+      int owner, lrow;
+      ulysses_home(a.route, t, owner, lrow);
+      dst = reinterpret_cast<__nv_bfloat16*>(a.route.dst[owner]) + static_cast<int64_t>(lrow) * a.route.ld +
+            (is_q ? a.route.col0 + hd * D : a.route.col0_k + (hd - a.Hq) * D) + lane * 4;
+    }
     uint2 u;
     u.x = pack_bf16x2(dx[0], dx[1]);
     u.y = pack_bf16x2(dx[2], dx[3]);
@@ -316,6 +328,7 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
   __syncthreads();
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x)
     a.dw_partial[static_cast<int64_t>(blockIdx.x) * 2 * D + i] = (&red[0][0])[i];
+  if (a.route.dst[0] != nullptr) __threadfence_system();
 }
 
 // ------------------------------------------------------------------ SwiGLU
@@ -470,6 +483,8 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(const torch::Tensor& qkv, int64_t Hq
   a.Hq = static_cast<int>(Hq);
   a.Hkv = static_cast<int>(Hkv);
   a.eps = static_cast<float>(eps);
+  a.tab_rows = static_cast<int>(cos_tab.size(0));
+  TORCH_CHECK(a.tab_rows > 0 && sin_tab.size(0) == cos_tab.size(0), "qk_norm_rope: cos/sin tables");
   const int64_t items = static_cast<int64_t>(T) * (Hq + Hkv);
   const int threads = 256;
   mvp::qk_norm_rope_fwd_kernel<<<static_cast<int>((items + 7) / 8), threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
@@ -483,7 +498,8 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
                                             const torch::Tensor& wq, const torch::Tensor& wk,
                                             const torch::Tensor& pos, const torch::Tensor& axis_of,
                                             const torch::Tensor& cos_tab, const torch::Tensor& sin_tab,
-                                            const torch::Tensor& rstd) {
+                                            const torch::Tensor& rstd,
+                                            const c10::optional<std::vector<int64_t>>& route) {
   CHECK_BF16(dq);
   CHECK_BF16(dk);
   TORCH_CHECK(dqkv.stride(-1) == 1 && qkv.stride(-1) == 1, "qk_norm_rope_bwd: unit inner stride");
@@ -511,6 +527,10 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
   a.T = T;
   a.Hq = static_cast<int>(Hq);
   a.Hkv = static_cast<int>(Hkv);
+  a.tab_rows = static_cast<int>(cos_tab.size(0));
+  a.route = mvp::make_ulysses_route(route);
+  TORCH_CHECK(a.route.dst[0] == nullptr || T == 2 * a.route.world * a.route.chunk,
+              "qk_norm_rope_bwd: routed rows need T = 2 x world x chunk");
   mvp::qk_norm_rope_bwd_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto dw = partial.sum(0);

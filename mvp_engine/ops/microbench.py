@@ -4,6 +4,7 @@ Usage::
 
     python -m mvp_engine.ops.microbench gemm            # Qwen3-8B layer shapes, ours vs cuBLAS
     python -m mvp_engine.ops.microbench gemm --shape 8192,24576,4096 --iters 20
+    torchrun --nproc-per-node 2 -m mvp_engine.ops.microbench cp_attention --tokens 131072
 
 Prints one JSON line per case with the kernel time and achieved TFLOP/s.
 cuBLAS (``torch.matmul``) is timed alongside only as the comparison column.
@@ -274,9 +275,145 @@ def bench_tp_gemm(tokens: int, hidden: int, iters: int) -> None:
     dist.destroy_process_group()
 
 
+def bench_cp_attention(tokens: int, hq: int, hkv: int, iters: int, impls: list[str]) -> None:
+    """One attention layer (forward + backward) under context parallelism (launch with torchrun).
+
+    Workload: one packed row of ``tokens`` tokens, documents U[4096, 65536] (causal per document),
+    zig-zag sharded over the W ranks; cases ``ring`` / ``ulysses`` (NCCL collectives) and
+    ``ring_fused`` (K/V pulled over NVLink by copy CTAs of the attention kernel, dK/dV written into
+    the owners' slots).  Device time per call (CUDA events, median of ``iters``, max over ranks).
+    Roofline of the fused ring: max(attention FLOPs of this rank at the measured bf16 burst peak,
+    NVLink bytes into this rank at 770 GB/s) where the bytes are the other ranks' K/V (twice: forward
+    and backward) and the fp32 dK/dV partials of this rank's keys."""
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import PackedContext
+    from mvp_engine.ops import _ext
+    from mvp_engine.parallel.context import ContextParallel
+
+    initialize_process_group()
+    W, r = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lens = _doc_lens(tokens, 4096, 65536)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(7 + r)
+    L = tokens // W
+    q = torch.randn(L, hq, 128, device=dev, generator=g).bfloat16().requires_grad_()
+    k = torch.randn(L, hkv, 128, device=dev, generator=g).bfloat16().requires_grad_()
+    v = torch.randn(L, hkv, 128, device=dev, generator=g).bfloat16().requires_grad_()
+    do = torch.randn(L, hq, 128, device=dev, generator=g).bfloat16()
+    res = {}
+    for name in impls:
+        impl, fused = name.split("_")[0], name.endswith("_fused")
+        cp = ContextParallel(dist.group.WORLD, impl=impl, fused=fused)
+        ctx = PackedContext(torch.zeros(1, L, dtype=torch.long, device=dev), cu, max(lens), None, cp=cp)
+
+        def step():
+            o = cp.attention(q, k, v, ctx, 128**-0.5)
+            o.backward(do)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            dist.barrier()
+            torch.cuda.synchronize()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            step()
+            e_.record()
+            torch.cuda.synchronize()
+            ts.append(s_.elapsed_time(e_))
+        t = torch.tensor([sorted(ts)[len(ts) // 2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = float(t)
+    _ext.check_status(dev)
+    causal_pairs = sum(n * (n + 1) / 2 for n in lens)
+    flops = 4.0 * causal_pairs * 128 * hq * 3.5 / W  # fwd (2 GEMMs) + bwd (5 GEMMs), per rank
+    wire = (W - 1) / W * (2 * 2 * tokens * hkv * 128 * 2 + 2 * tokens * hkv * 128 * 4)
+    roof_ms = max(flops / 1675e12, wire / 770e9) * 1e3
+    if r == 0:
+        line = {"kernel": "cp_attention_fwd_bwd", "world": W, "tokens": tokens, "heads": [hq, hkv],
+                "docs": len(lens), **{k_ + "_ms": round(v_, 3) for k_, v_ in res.items()},
+                "roofline_ms": round(roof_ms, 3), "link_ms": round(wire / 770e9 * 1e3, 3)}
+        for k_, v_ in res.items():
+            line[k_ + "_frac_of_roofline"] = round(roof_ms / v_, 3)
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def bench_cp_layer(tokens: int, iters: int, impls: list[str]) -> None:
+    """One Qwen3-8B decoder layer (forward + backward) under context parallelism (launch with torchrun).
+
+    The layer sees this rank's zig-zag share of one ``tokens``-token packed row (documents U[4096, 65536]);
+    cases ``ulysses`` (NCCL all-to-alls around the attention), ``ulysses_fused`` (the all-to-alls folded
+    into the QKV GEMM, attention and QK-norm/RoPE kernels), ``ring`` and ``ring_fused``.  Device time per
+    call (median of ``iters``, max over ranks)."""
+    import torch.distributed as dist
+
+    from mvp_engine import ops
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import PackedContext, Qwen3DecoderLayer, load_qwen3_config, positions_from_cu_seqlens
+    from mvp_engine.ops import _ext
+    from mvp_engine.parallel.context import ContextParallel
+
+    initialize_process_group()
+    W, r = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = load_qwen3_config("Qwen/Qwen3-8B-Base")
+    layer = Qwen3DecoderLayer(cfg, 0).to(dev).to(torch.bfloat16)
+    with torch.no_grad():
+        for name, p_ in layer.named_parameters():
+            p_.copy_(torch.randn_like(p_) * 0.02 + (1.0 if "norm" in name else 0.0))
+    lens = _doc_lens(tokens, 4096, 65536)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+    L = tokens // W
+    x = (torch.randn(L, cfg.hidden_size, device=dev) * 0.5).bfloat16().requires_grad_()
+    dy1 = torch.randn(L, cfg.hidden_size, device=dev).bfloat16()
+    rope = ops.RopeCache(cfg.head_dim, cfg.rope_theta, max_positions=max(lens))
+    res = {}
+    for name in impls:
+        impl, fused = name.split("_")[0], name.endswith("_fused")
+        cp = ContextParallel(dist.group.WORLD, impl=impl, fused=fused)
+        idx = cp.local_indices(tokens).to(dev)
+        pos = positions_from_cu_seqlens(cu, tokens)[idx].view(1, -1).to(torch.int32)
+        ctx = PackedContext(pos, cu, max(lens), rope, cp=cp)
+
+        def step():
+            out, _ = layer(x, None, ctx)
+            out.backward(dy1)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            dist.barrier()
+            torch.cuda.synchronize()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            step()
+            e_.record()
+            torch.cuda.synchronize()
+            ts.append(s_.elapsed_time(e_))
+        t = torch.tensor([sorted(ts)[len(ts) // 2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = float(t)
+    _ext.check_status(dev)
+    if r == 0:
+        print(json.dumps({"kernel": "cp_decoder_layer_fwd_bwd", "model": "Qwen3-8B", "world": W, "tokens": tokens,
+                          "docs": len(lens), **{k_ + "_ms": round(v_, 3) for k_, v_ in res.items()}}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm"])
+    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer"])
+    ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
     ap.add_argument("--hidden", type=int, default=5120, help="tp_gemm: hidden size (square weights)")
     ap.add_argument("--mbytes", type=int, default=768, help="peer_rs: unit size in MiB")
     ap.add_argument("--tokens", type=int, default=8192)
@@ -297,6 +434,11 @@ def main() -> None:
         bench_tp_gemm(args.tokens if args.tokens != 8192 else 4096, args.hidden, args.iters)
     elif args.what == "peer_rs":
         bench_peer_rs(args.mbytes, args.iters)
+    elif args.what == "cp_layer":
+        bench_cp_layer(args.tokens, args.iters, args.impls.split(","))
+    elif args.what == "cp_attention":
+        hq, hkv = (int(v) for v in args.heads.split(","))
+        bench_cp_attention(args.tokens, hq, hkv, args.iters, args.impls.split(","))
     elif args.what == "attention":
         hq, hkv = (int(v) for v in args.heads.split(","))
         bench_attention(args.tokens, hq, hkv, args.iters)
