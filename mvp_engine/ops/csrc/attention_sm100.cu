@@ -19,19 +19,20 @@
 // Forward CTA = one 128-row query block of one head (grid = q blocks x Hq):
 //   warps 0-7  softmax, two warpgroups: thread (warp % 4, lane) owns query row
 //              r = TMEM lane, warpgroup h its keys 64h .. 64h+63 of each
-//              block.  Each reads its half of S from TMEM, applies the
-//              document mask (skipped for blocks entirely inside the row's
-//              window), exchanges its partial row max with the other half
-//              through shared memory, keeps the running max and its partial
-//              sum, rescales its half of O in TMEM only when the max grows by
-//              more than 2^8 (lazy rescale), and writes its half of P (bf16)
-//              into the 128-byte swizzled shared-memory tile of the next MMA.
-//              Two warps per SM sub-partition hide the exp2 / TMEM latency
-//              that a single warpgroup cannot.
-//   warp 8     TMA producer: Q once, then K/V blocks into a 2-deep ring.
+//              block, with its own running max, sum and O accumulator (the two
+//              partial softmaxes are merged once, in the epilogue, so the
+//              halves never wait for each other per block).  Each reads its
+//              half of S from TMEM, applies the document mask (skipped for
+//              blocks entirely inside the row's window), rescales its O only
+//              when its max grows by more than 2^8 (lazy rescale), and writes
+//              P (bf16 pairs) back into the first 32 columns of its half of S,
+//              where the PV MMA reads it as a tensor-memory A operand.
+//   warp 8     TMA producer: Q once, then K/V blocks into a 3-deep ring.
 //   warp 9     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before waiting for
-//              P_j so the tensor core overlaps the softmax; then O += P_j V_j.
-// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+//              P_j so the tensor core overlaps the softmax; then, per half,
+//              O_h += P_j,h V_j,h as soon as that half's P is in place.
+// TMEM: S double buffer (2 x 128 columns, P aliased) + two O accumulators
+// (2 x 128 columns).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -120,6 +121,13 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t base, int s) {
 constexpr int kFwdThreads = 320;  // 8 softmax warps + TMA warp + MMA warp
 constexpr int kTmaWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kKvStages = 3;  // K/V ring depth
+
+// D[tmem] (+)= A[tmem] * B[smem]: tcgen05.mma with the A operand (P) read from tensor memory.
+__device__ __forceinline__ void mma_p_tmem(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  mma_bf16_ts(d_tmem, a_tmem, b_desc, idesc, accumulate);
+}
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -127,24 +135,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;       // [2]
-  uint8_t* sV = sK + 2 * TILE_BYTES;   // [2]
-  uint8_t* sP = sV + 2 * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+  uint8_t* sK = sQ + TILE_BYTES;                 // [kKvStages]
+  uint8_t* sV = sK + kKvStages * TILE_BYTES;     // [kKvStages]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKvStages * TILE_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_ready = bars + 12;
-  uint64_t* done_bar = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;                   // [kKvStages]
+  uint64_t* v_full = k_full + kKvStages;         // [kKvStages]
+  uint64_t* kv_empty = v_full + kKvStages;       // [kKvStages]
+  uint64_t* s_full = kv_empty + kKvStages;       // [2]
+  uint64_t* p_full = s_full + 2;                 // [2 halves] (128 arrivals each)
+  uint64_t* o_ready = p_full + 2;                // [2 halves]
+  uint64_t* done_bar = o_ready + 2;
+  uint64_t* lsum_bar = done_bar + 1;             // the halves exchanged (max, sum) once (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lsum_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* xchg = bars + 16;     // [2] the two softmax halves exchanged their row maxima (256 arrivals)
-  uint64_t* lsum_bar = bars + 18; // the two halves exchanged their row sums (256 arrivals)
-  float* xmax = reinterpret_cast<float*>(bars + 20);  // [2 parity][2 halves][128 rows] maxima, then [2][128] sums
+  // [2 halves][2 (max, sum)][128 rows], exchanged in the epilogue once every MMA (and so every K/V load
+  // it waited for) has retired: it reuses the first K stage.
+  float* xml = reinterpret_cast<float*>(sK);
 
   if (static_cast<int>(blockIdx.y) < p.pull.rows) {  // copy CTA: pull the next hop's K/V, no attention
     peer_pull_cta(p.pull, p.status, reinterpret_cast<int*>(smem));
@@ -167,19 +174,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kKvStages; ++b) {
       mbar_init(&k_full[b], 1);
       mbar_init(&v_full[b], 1);
       mbar_init(&kv_empty[b], 1);
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 256);
     }
-    mbar_init(p_full, 256);
-    mbar_init(&xchg[0], 256);
-    mbar_init(&xchg[1], 256);
-    mbar_init(lsum_bar, 256);
-    mbar_init(o_ready, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_ready[b], 1);
+    }
     mbar_init(done_bar, 1);
+    mbar_init(lsum_bar, 256);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -191,8 +197,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;         // [2] x 128 columns
-  const uint32_t tO = tmem + 256;   // 128 columns
+  const uint32_t tS = tmem;         // [2] x 128 columns; P_j (bf16 pairs) overwrites S_j's first 32 columns per half
+  const uint32_t tO = tmem + 256;   // [2 halves] x 128 columns
 
   if (warp == kTmaWarp) {
     // --------------------------------------------------------------- TMA
@@ -207,8 +213,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t issued_phase = 0;
       bool ok = true;
       for (int j = 0; j < n_blocks; ++j) {
-        const int b = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int b = j % kKvStages;
+        const uint32_t ph = (j / kKvStages) & 1;
         if (!mbar_wait_bounded(&kv_empty[b], ph ^ 1, abort_flag, p.status, kTimeoutProducer)) {
           ok = false;
           break;
@@ -228,7 +234,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < 200000000ull) {
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kKvStages; ++b) {
           if (!((issued >> b) & 1u)) continue;
           const uint32_t par = (issued_phase >> b) & 1u;
           const uint64_t t1 = globaltimer();
@@ -240,23 +246,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // --------------------------------------------------------------- MMA
+    // tcgen05.mma operations of this thread execute in issue order, so S_{j+2} (written into the
+    // columns that hold P_j) is issued only after PV_j, which reads P_j.
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BLK, BLK, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(BLK, D, false, true);
       const uint32_t q_base = smem_u32(sQ);
-      const uint32_t p_base = smem_u32(sP);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kTimeoutMma);
       auto issue_s = [&](int j) -> bool {
-        const int b = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(&k_full[b], ph, abort_flag, p.status, kTimeoutMma)) return false;
-        if (!mbar_wait_bounded(&s_empty[b], ph ^ 1, abort_flag, p.status, kTimeoutMma)) return false;
+        const int st = j % kKvStages;
+        const uint32_t ph = (j / kKvStages) & 1;
+        if (!mbar_wait_bounded(&k_full[st], ph, abort_flag, p.status, kTimeoutMma)) return false;
         tc_fence_after();
-        const uint32_t k_base = smem_u32(sK + b * TILE_BYTES);
+        const uint32_t k_base = smem_u32(sK + st * TILE_BYTES);
 #pragma unroll
         for (int s = 0; s < D / 16; ++s)
-          mma_bf16_ss(tS + b * BLK, kmajor_desc(q_base, s), kmajor_desc(k_base, s), idesc_s, s > 0 ? 1u : 0u);
-        mma_commit(&s_full[b]);
+          mma_bf16_ss(tS + (j & 1) * BLK, kmajor_desc(q_base, s), kmajor_desc(k_base, s), idesc_s, s > 0 ? 1u : 0u);
+        mma_commit(&s_full[j & 1]);
         return true;
       };
       if (ok && n_blocks > 0) ok = issue_s(0);
@@ -265,37 +271,45 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           ok = false;
           break;
         }
-        const int b = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(p_full, j & 1, abort_flag, p.status, kTimeoutMma)) {
+        const int st = j % kKvStages;
+        const uint32_t ph = (j / kKvStages) & 1;
+        if (!mbar_wait_bounded(&v_full[st], ph, abort_flag, p.status, kTimeoutMma)) {
           ok = false;
           break;
         }
-        if (!mbar_wait_bounded(&v_full[b], ph, abort_flag, p.status, kTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(sV + b * TILE_BYTES);
+        const uint32_t v_base = smem_u32(sV + st * TILE_BYTES);
+        for (int hf = 0; hf < 2 && ok; ++hf) {
+          // O_hf += P_j[:, keys 64hf..64hf+63] V_j[keys 64hf.., :], P from tensor memory
+          if (!mbar_wait_bounded(&p_full[hf], j & 1, abort_flag, p.status, kTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int s = 0; s < BLK / 16; ++s)
-          mma_bf16_ss(tO, kmajor_desc(p_base, s), vmajor_desc(v_base, s), idesc_o, (j > 0 || s > 0) ? 1u : 0u);
-        mma_commit(o_ready);
-        mma_commit(&kv_empty[b]);
+          for (int s = 0; s < 4; ++s)
+            mma_p_tmem(tO + hf * D, tS + (j & 1) * BLK + hf * 64 + s * 8, vmajor_desc(v_base, 4 * hf + s), idesc_o,
+                       (j > 0 || s > 0) ? 1u : 0u);
+          mma_commit(&o_ready[hf]);
+        }
+        if (!ok) break;
+        mma_commit(&kv_empty[st]);
       }
-      // Retire everything issued before TMEM is released.
+      // Retire everything issued before TMEM is released (the epilogue waits on the same barrier).
       mma_commit(done_bar);
       mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
     }
   } else {
     // ----------------------------------------------------------- softmax
+    // Warpgroup `half` owns keys 64*half .. +63 of every block with its own running max, sum and
+    // O accumulator, so the halves never wait for each other until the final merge.
     const int r = (warp & 3) * 32 + lane;  // query row = TMEM lane
-    const int half = warp >> 2;             // keys / O columns 64*half .. 64*half+63
+    const int half = warp >> 2;
     const int i = q0 + r;
     const bool valid = i < p.T;
     int start_i = 0, hi_i = -1;  // allowed keys start_i .. hi_i
     if (valid) key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, i, start_i, hi_i);
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tOh = tO + half * D + lane_addr;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_blocks; ++j) {
@@ -304,17 +318,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[b], ph, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t tSh = tS + b * BLK + lane_addr + half * 64;
       float s[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t rr[32];
-        tmem_ld_32x32b_x32(tS + b * BLK + lane_addr + half * 64 + c * 32, rr);
+        tmem_ld_32x32b_x32(tSh + c * 32, rr);
         tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(rr[t]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[b]);
       const int k0 = kv_lo + j * BLK + half * 64;
       float mb = -INFINITY;
       if (valid && k0 >= start_i && k0 + 63 <= hi_i) {  // whole half-block visible: no mask
@@ -332,77 +345,77 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mb = fmaxf(mb, s[c]);
         }
       }
-      // row max over both halves (bounded mbarrier exchange: a half that gave up cannot hang the other)
-      float* xm = xmax + (j & 1) * 256;
-      xm[half * 128 + r] = mb;
-      mbar_arrive(&xchg[j & 1]);
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&xchg[j & 1], ph, abort_flag, p.status, kTimeoutEpilogue));
-      if (!ok) break;
-      mb = fmaxf(mb, xm[(half ^ 1) * 128 + r]);
       const float m_new = fmaxf(m, mb);
       float m_use = m, alpha = 1.f;
       if (m_new > m + kRescaleThreshold || (m == -INFINITY && m_new != -INFINITY)) {
         m_use = m_new;
         alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
       }
-      // O and the P tile are free once PV_{j-1} has retired.
-      if (j > 0) {
+      // PV_{j-1} of this half must have retired before O is rescaled, and before P_j is published
+      // (so p_full never runs two phases ahead of the MMA warp).  s_full_j implies PV_{j-2} has
+      // retired, so o_ready is at most one phase behind and its parity is unambiguous.
+      bool waited = false;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         ok = __all_sync(0xffffffffu,
-                        mbar_wait_bounded(o_ready, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+                        mbar_wait_bounded(&o_ready[half], (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
         if (!ok) break;
+        waited = true;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t rr[16];
-            tmem_ld_32x32b_x16(tO + lane_addr + half * 64 + c * 16, rr);
-            tmem_wait_ld();
+        for (int c = 0; c < 8; ++c) {
+          uint32_t rr[16];
+          tmem_ld_32x32b_x16(tOh + c * 16, rr);
+          tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 16; ++t) rr[t] = __float_as_uint(__uint_as_float(rr[t]) * alpha);
-            tmem_st_32x32b_x16(tO + lane_addr + half * 64 + c * 16, rr);
-          }
-          tmem_wait_st();
+          for (int t = 0; t < 16; ++t) rr[t] = __float_as_uint(__uint_as_float(rr[t]) * alpha);
+          tmem_st_32x32b_x16(tOh + c * 16, rr);
         }
+        tmem_wait_st();
       }
       m = m_use;
-      float rowsum = 0.f;
-      // P = exp2(s - m) as bf16 into this half's 64-key chunk of the swizzled K-major tile.
-      uint8_t* row_base = sP + half * CHUNK_BYTES + r * 128;
+      // P = exp2(s - m) as bf16 pairs over S_j's first 32 columns of this half (A operand of PV_j).
       const bool live = m != -INFINITY;
+      float rowsum = 0.f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float e[8];
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          e[t] = live ? exp2f(s[u * 8 + t] - m) : 0.f;  // exp2f(-inf) = 0 for masked keys
-          rowsum += e[t];
+        for (int t = 0; t < 16; ++t) {
+          const float e0 = live ? exp2f(s[c * 32 + 2 * t] - m) : 0.f;  // exp2f(-inf) = 0 for masked keys
+          const float e1 = live ? exp2f(s[c * 32 + 2 * t + 1] - m) : 0.f;
+          rowsum += e0 + e1;
+          pk[t] = pack_bf16x2(e0, e1);
         }
-        uint4 pk;
-        pk.x = pack_bf16x2(e[0], e[1]);
-        pk.y = pack_bf16x2(e[2], e[3]);
-        pk.z = pack_bf16x2(e[4], e[5]);
-        pk.w = pack_bf16x2(e[6], e[7]);
-        *reinterpret_cast<uint4*>(row_base + ((u ^ (r & 7)) << 4)) = pk;
+        tmem_st_32x32b_x16(tSh + c * 16, pk);
+      }
+      tmem_wait_st();
+      if (j > 0 && !waited) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_bounded(&o_ready[half], (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+        if (!ok) break;
       }
       l = l * alpha + rowsum;
-      fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[half]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && n_blocks > 0) {
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait_bounded(o_ready, (n_blocks - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
-    }
-    // row sum over both halves
-    float* xl = xmax + 512;
-    xl[half * 128 + r] = l;
+    // Every MMA has retired once done_bar completes; merge the two halves' (max, sum, O).
+    if (ok && n_blocks > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutEpilogue));
+    xml[(half * 2 + 0) * 128 + r] = m;
+    xml[(half * 2 + 1) * 128 + r] = l;
     mbar_arrive(lsum_bar);
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(lsum_bar, 0, abort_flag, p.status, kTimeoutEpilogue));
-    if (ok) l += xl[(half ^ 1) * 128 + r];
     if (ok) {
       tc_fence_after();
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const float m0 = xml[0 * 128 + r], l0 = xml[1 * 128 + r];
+      const float m1 = xml[2 * 128 + r], l1 = xml[3 * 128 + r];
+      const float mx = fmaxf(m0, m1);
+      const float f0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mx);
+      const float f1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mx);
+      const float lt = l0 * f0 + l1 * f1;
+      const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
+      const float w0 = f0 * inv, w1 = f1 * inv;
       __nv_bfloat16* orow = p.o + static_cast<int64_t>(i) * p.o_row_stride + h * D + half * 64;
       __nv_bfloat16* urow = nullptr;  // the same row in the token rank's o_proj input (Ulysses)
       if (p.route.dst[0] != nullptr && valid) {
@@ -413,29 +426,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t rr[32];
+        uint32_t a0[32], a1[32];
         if (n_blocks > 0) {
-          tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, rr);
+          tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, a0);
+          tmem_ld_32x32b_x32(tO + D + lane_addr + half * 64 + c * 32, a1);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) rr[t] = 0u;
+          for (int t = 0; t < 32; ++t) a0[t] = a1[t] = 0u;
         }
         if (valid) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
+            float o8[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              o8[t] = __uint_as_float(a0[8 * v + t]) * w0 + __uint_as_float(a1[8 * v + t]) * w1;
             uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
-            pk.y = pack_bf16x2(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
-            pk.z = pack_bf16x2(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
-            pk.w = pack_bf16x2(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
+            pk.x = pack_bf16x2(o8[0], o8[1]);
+            pk.y = pack_bf16x2(o8[2], o8[3]);
+            pk.z = pack_bf16x2(o8[4], o8[5]);
+            pk.w = pack_bf16x2(o8[6], o8[7]);
             *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = pk;
             if (urow != nullptr) *reinterpret_cast<uint4*>(urow + c * 32 + v * 8) = pk;
           }
         }
       }
       if (urow != nullptr) __threadfence_system();
-      if (valid && half == 0) p.lse[static_cast<int64_t>(h) * p.T + i] = (l > 0.f) ? (m + log2f(l)) / kLog2e : -INFINITY;
+      if (valid && half == 0)
+        p.lse[static_cast<int64_t>(h) * p.T + i] = (lt > 0.f) ? (mx + log2f(lt)) / kLog2e : -INFINITY;
     }
   }
 
@@ -448,7 +467,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-constexpr int kFwdSmem = 6 * TILE_BYTES + 1024 + 160 + 3 * 256 * 4;  // tiles, align, barriers, exchange
+// tiles, align, barriers (9 + 3 * stages), TMEM slot / abort flag
+constexpr int kFwdSmem = (1 + 2 * kKvStages) * TILE_BYTES + 1024 + (9 + 3 * kKvStages) * 8 + 16;
+static_assert(kFwdSmem <= 232448, "forward kernel exceeds 227 KB of shared memory");
 
 }  // namespace attn
 }  // namespace mvp
@@ -561,6 +582,13 @@ struct BwdParams {
   int f32_accumulate;
   UlyssesRoute route;  // optional: dV rows written to the token's rank (dqkv layout) instead of dv
 };
+
+// Fire-and-forget fp32 x4 reduction into global memory (no return value, so no scoreboard wait).
+__device__ __forceinline__ void red_add_v4(float* addr, const uint32_t* v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(__uint_as_float(v[0])),
+               "f"(__uint_as_float(v[1])), "f"(__uint_as_float(v[2])), "f"(__uint_as_float(v[3]))
+               : "memory");
+}
 
 constexpr int kBwdThreads = 320;  // 8 gradient warps + TMA warp + MMA warp
 
@@ -772,25 +800,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(mma2_done, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
-      // dQ rows: thread c now owns query row q0 + c, d columns 64*half .. +63.
+      // dQ rows: thread c now owns query row q0 + c, d columns 64*half .. +63.  Both chunks are read
+      // out of TMEM first, so the MMA warp can reuse the columns while the reductions are issued.
       const int qi = q0 + c;
       float* dst = p.dq_acc + (static_cast<int64_t>(qi) * p.Hq + h) * D + half * 64;
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t rr[32];
-        tmem_ld_32x32b_x32(tS + lane_addr + half * 64 + ch * 32, rr);
-        tmem_wait_ld();
-        if (qi < p.T) {
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            atomicAdd(reinterpret_cast<float4*>(dst + ch * 32) + v,
-                      make_float4(__uint_as_float(rr[4 * v]), __uint_as_float(rr[4 * v + 1]),
-                                  __uint_as_float(rr[4 * v + 2]), __uint_as_float(rr[4 * v + 3])));
-          }
-        }
-      }
+      uint32_t rq[64];
+      tmem_ld_32x32b_x32(tS + lane_addr + half * 64, *reinterpret_cast<uint32_t(*)[32]>(rq));
+      tmem_ld_32x32b_x32(tS + lane_addr + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(rq + 32));
+      tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_read);
+      if (qi < p.T) {
+#pragma unroll
+        for (int v = 0; v < 16; ++v) red_add_v4(dst + 4 * v, rq + 4 * v);
+      }
     }
     if (ok) {  // keys no query sees (n_iter == 0) get zero gradients
       tc_fence_after();

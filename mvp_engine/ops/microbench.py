@@ -414,6 +414,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer"])
     ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
+    ap.add_argument("--docs", default="256,4096", help="attention: document lengths U[lo, hi]")
     ap.add_argument("--hidden", type=int, default=5120, help="tp_gemm: hidden size (square weights)")
     ap.add_argument("--mbytes", type=int, default=768, help="peer_rs: unit size in MiB")
     ap.add_argument("--tokens", type=int, default=8192)
@@ -441,7 +442,8 @@ def main() -> None:
         bench_cp_attention(args.tokens, hq, hkv, args.iters, args.impls.split(","))
     elif args.what == "attention":
         hq, hkv = (int(v) for v in args.heads.split(","))
-        bench_attention(args.tokens, hq, hkv, args.iters)
+        lo, hi = (int(v) for v in args.docs.split(","))
+        bench_attention(args.tokens, hq, hkv, args.iters, lo, hi)
 
 
 if __name__ == "__main__":
