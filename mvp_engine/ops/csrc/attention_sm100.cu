@@ -123,6 +123,14 @@ constexpr int kTmaWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kKvStages = 3;  // K/V ring depth
 
+// 2^x with the MUFU.EX2 instruction (PTX ex2.approx.ftz.f32: relative error ~2^-22, 2^-inf = 0); the
+// result is rounded to bf16 right after, so the approximation is far below the storage precision.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]: tcgen05.mma with the A operand (P) read from tensor memory.
 __device__ __forceinline__ void mma_p_tmem(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -319,32 +327,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tSh = tS + b * BLK + lane_addr + half * 64;
-      float s[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t rr[32];
-        tmem_ld_32x32b_x32(tSh + c * 32, rr);
+      float s[64];  // raw logits; scaled inside the exponent
+      {
+        uint32_t rr[64];
+        tmem_ld_32x32b_x32(tSh, *reinterpret_cast<uint32_t(*)[32]>(rr));
+        tmem_ld_32x32b_x32(tSh + 32, *reinterpret_cast<uint32_t(*)[32]>(rr + 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(rr[t]);
+        for (int t = 0; t < 64; ++t) s[t] = __uint_as_float(rr[t]);
       }
       const int k0 = kv_lo + j * BLK + half * 64;
-      float mb = -INFINITY;
-      if (valid && k0 >= start_i && k0 + 63 <= hi_i) {  // whole half-block visible: no mask
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          s[c] *= p.scale_log2;
-          mb = fmaxf(mb, s[c]);
-        }
-      } else {
+      if (!(valid && k0 >= start_i && k0 + 63 <= hi_i)) {  // some keys of this half-block are masked
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const int key = k0 + c;
-          const bool allowed = valid && key >= start_i && key <= hi_i;
-          s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
-          mb = fmaxf(mb, s[c]);
+          s[c] = (valid && key >= start_i && key <= hi_i) ? s[c] : -INFINITY;
         }
       }
+      // row max as an 8-way tree (a 64-long dependent chain would serialise the warp)
+      float mx8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(s[t], s[t + 8]);
+#pragma unroll
+      for (int c = 16; c < 64; c += 8) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], s[c + t]);
+      }
+      const float mb = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
       const float m_new = fmaxf(m, mb);
       float m_use = m, alpha = 1.f;
       if (m_new > m + kRescaleThreshold || (m == -INFINITY && m_new != -INFINITY)) {
@@ -373,21 +383,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_wait_st();
       }
       m = m_use;
-      // P = exp2(s - m) as bf16 pairs over S_j's first 32 columns of this half (A operand of PV_j).
-      const bool live = m != -INFINITY;
-      float rowsum = 0.f;
+      // P = 2^(s * scale_log2 - m) as bf16 pairs over S_j's first 32 columns of this half (A operand
+      // of PV_j); masked keys (s = -inf) give 0.  A dead row (m = -inf) writes zeros.
+      const float neg_m = (m != -INFINITY) ? -m : -INFINITY;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float e0 = live ? exp2f(s[c * 32 + 2 * t] - m) : 0.f;  // exp2f(-inf) = 0 for masked keys
-          const float e1 = live ? exp2f(s[c * 32 + 2 * t + 1] - m) : 0.f;
-          rowsum += e0 + e1;
+          const float e0 = ex2_approx(fmaf(s[c * 32 + 2 * t], p.scale_log2, neg_m));
+          const float e1 = ex2_approx(fmaf(s[c * 32 + 2 * t + 1], p.scale_log2, neg_m));
+          rs8[(2 * t) & 7] += e0;
+          rs8[(2 * t + 1) & 7] += e1;
           pk[t] = pack_bf16x2(e0, e1);
         }
         tmem_st_32x32b_x16(tSh + c * 16, pk);
       }
+      const float rowsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       tmem_wait_st();
       if (j > 0 && !waited) {
         ok = __all_sync(0xffffffffu,
@@ -765,14 +778,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld_32x32b_x32(tdP + lane_addr + col0, dr);
         tmem_wait_ld();
         float pv[32], ds[32];
+        const int qc = q0 + col0;
+        if (kvalid && qc >= lo_c && qc + 31 < ke && qc + 31 < p.T) {  // all 32 queries see this key
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int r = col0 + t;
-          const int qr = q0 + r;
-          const bool allowed = kvalid && qr >= lo_c && qr < ke && qr < p.T;
-          const float pe = allowed ? exp2f(__uint_as_float(sr[t]) * p.scale_log2 - lse_b[r]) : 0.f;
-          pv[t] = pe;
-          ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+          for (int t = 0; t < 32; ++t) {
+            const int r = col0 + t;
+            const float pe = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -lse_b[r]));
+            pv[t] = pe;
+            ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int r = col0 + t;
+            const int qr = q0 + r;
+            const bool allowed = kvalid && qr >= lo_c && qr < ke && qr < p.T;
+            const float pe = allowed ? ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -lse_b[r])) : 0.f;
+            pv[t] = pe;
+            ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+          }
         }
         // 32 q columns = half of one 64-wide chunk = four 16-byte units.
         uint8_t* prow = sPt + half * CHUNK_BYTES + c * 128;
