@@ -566,10 +566,13 @@ std::vector<torch::Tensor> flash_attn_fwd(const torch::Tensor& q, const torch::T
 //   P^T  = exp(S^T*scale - lse),  dS^T = P^T * (dP^T - delta) * scale
 //   dV  += P^T dO,  dK += dS^T Q   (TMEM accumulators)
 //   dQ   = dS K  -> TMEM (lane = query row) -> fp32 vector atomics into dq_acc
-// P^T and dS^T are written once into 128-byte-swizzled smem tiles; the dS^T
-// tile serves both as the K-major A operand of dK and, read MN-major, as the
-// A operand of dQ.  Q/dO tiles serve as K-major B (S^T, dP^T) and as MN-major
-// B (dK, dV).  TMEM: S^T | dP^T | dV | dK (4 x 128 columns); dQ reuses S^T.
+// P^T is written back into S^T's TMEM columns (bf16 pairs) and read from there
+// as the A operand of dV; dS^T goes once into a 128-byte-swizzled smem tile
+// that serves both as the K-major A operand of dK and, read MN-major, as the A
+// operand of dQ.  Q/dO tiles (a 2-deep ring, so the next query block loads
+// while this one computes) serve as K-major B (S^T, dP^T) and as MN-major B
+// (dK, dV).  TMEM: S^T | dP^T | dV | dK (4 x 128 columns); dQ goes into dP^T's
+// columns and is issued before dV / dK so its read-out overlaps them.
 namespace mvp {
 namespace attn {
 
@@ -604,6 +607,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, const uint32_t* v) {
 }
 
 constexpr int kBwdThreads = 320;  // 8 gradient warps + TMA warp + MMA warp
+constexpr int kQdStages = 2;       // Q / dO ring depth
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -612,23 +616,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + TILE_BYTES;
-  uint8_t* sQ = sV + TILE_BYTES;
-  uint8_t* sdO = sQ + TILE_BYTES;
-  uint8_t* sPt = sdO + TILE_BYTES;
-  uint8_t* sdSt = sPt + TILE_BYTES;
-  float* s_lse = reinterpret_cast<float*>(sdSt + TILE_BYTES);  // [2][128]
-  float* s_delta = s_lse + 2 * BLK;                             // [2][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 2 * BLK);
+  uint8_t* sQ = sV + TILE_BYTES;                  // [kQdStages]
+  uint8_t* sdO = sQ + kQdStages * TILE_BYTES;     // [kQdStages]
+  uint8_t* sdSt = sdO + kQdStages * TILE_BYTES;
+  float* s_lse = reinterpret_cast<float*>(sdSt + TILE_BYTES);  // [128] LSE (log2 units) of this query block
+  float* s_delta = s_lse + BLK;                                 // [128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + BLK);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* p_full = bars + 4;
-  uint64_t* mma2_done = bars + 5;
-  uint64_t* dq_read = bars + 6;
-  uint64_t* done_bar = bars + 7;
-  uint64_t* stage = bars + 8;  // [2] lse / delta of the next query block staged (256 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* qd_full = bars + 1;                   // [kQdStages]
+  uint64_t* qd_empty = bars + 1 + kQdStages;      // [kQdStages] dV / dK of the stage's iteration retired
+  uint64_t* s_full = bars + 1 + 2 * kQdStages;    // S^T, dP^T in TMEM
+  uint64_t* p_full = s_full + 1;                  // P^T in TMEM, dS^T in smem (256 arrivals)
+  uint64_t* dq_full = s_full + 2;                 // dQ in TMEM
+  uint64_t* dq_read = s_full + 3;                 // dQ read out of TMEM (256 arrivals)
+  uint64_t* done_bar = s_full + 4;
+  uint64_t* stg_full = s_full + 5;                // LSE / delta of this query block staged (256 arrivals)
+  uint64_t* stg_free = s_full + 6;                // ... and no longer read (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if (static_cast<int>(blockIdx.y) < p.pull.rows) {  // copy CTA: pull the next hop's K/V, no gradients
@@ -649,15 +653,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qd_full, 1);
-    mbar_init(qd_empty, 1);
+    for (int st = 0; st < kQdStages; ++st) {
+      mbar_init(&qd_full[st], 1);
+      mbar_init(&qd_empty[st], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(p_full, 256);
-    mbar_init(mma2_done, 1);
+    mbar_init(dq_full, 1);
     mbar_init(dq_read, 256);
-    mbar_init(&stage[0], 256);
-    mbar_init(&stage[1], 256);
     mbar_init(done_bar, 1);
+    mbar_init(stg_full, 256);
+    mbar_init(stg_free, 256);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -669,9 +675,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // S^T (then P^T as bf16 pairs) | dP^T (then dQ) | dV | dK
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
 
   if (warp == 8) {
+    // ------------------------------------------------------------ TMA
     if (elect_one_sync()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -684,58 +692,71 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_load_2d(sV + CHUNK_BYTES, &tmV, kv_full, hk * D + 64, k0);
       int issued = 0;
       for (int n = 0; n < n_iter; ++n) {
-        if (!mbar_wait_bounded(qd_empty, (n & 1) ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
+        const int st = n % kQdStages;
+        const uint32_t ph = (n / kQdStages) & 1;
+        if (!mbar_wait_bounded(&qd_empty[st], ph ^ 1, abort_flag, p.status, kTimeoutProducer)) break;
         const int h = hk * rep + n / nq;
         const int q0 = q_lo + (n % nq) * BLK;
-        mbar_arrive_expect_tx(qd_full, 2 * TILE_BYTES);
-        tma_load_2d(sQ, &tmQ, qd_full, h * D, q0);
-        tma_load_2d(sQ + CHUNK_BYTES, &tmQ, qd_full, h * D + 64, q0);
-        tma_load_2d(sdO, &tmdO, qd_full, h * D, q0);
-        tma_load_2d(sdO + CHUNK_BYTES, &tmdO, qd_full, h * D + 64, q0);
+        mbar_arrive_expect_tx(&qd_full[st], 2 * TILE_BYTES);
+        tma_load_2d(sQ + st * TILE_BYTES, &tmQ, &qd_full[st], h * D, q0);
+        tma_load_2d(sQ + st * TILE_BYTES + CHUNK_BYTES, &tmQ, &qd_full[st], h * D + 64, q0);
+        tma_load_2d(sdO + st * TILE_BYTES, &tmdO, &qd_full[st], h * D, q0);
+        tma_load_2d(sdO + st * TILE_BYTES + CHUNK_BYTES, &tmdO, &qd_full[st], h * D + 64, q0);
         issued = n + 1;
       }
-      if (*abort_flag) {
+      if (*abort_flag) {  // let copies already issued land (bounded) before the CTA can exit
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(kv_full, 0) && globaltimer() - t0 < 200000000ull) {
         }
-        if (issued > 0) {
+        for (int n = max(0, issued - kQdStages); n < issued; ++n) {
           const uint64_t t1 = globaltimer();
-          while (!mbar_try_wait(qd_full, (issued - 1) & 1) && globaltimer() - t1 < 200000000ull) {
+          while (!mbar_try_wait(&qd_full[n % kQdStages], (n / kQdStages) & 1) && globaltimer() - t1 < 200000000ull) {
           }
         }
       }
     }
   } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA
+    // tcgen05.mma operations of this thread execute in issue order: S^T(n+1) overwrites P^T(n) only
+    // after dV(n) (issued before it) has read it.
     if (elect_one_sync()) {
       constexpr uint32_t id_kk = make_idesc_bf16(BLK, BLK, false, false);
       constexpr uint32_t id_km = make_idesc_bf16(BLK, D, false, true);
       constexpr uint32_t id_mm = make_idesc_bf16(BLK, D, true, true);
-      const uint32_t bK = smem_u32(sK), bV = smem_u32(sV), bQ = smem_u32(sQ), bdO = smem_u32(sdO);
-      const uint32_t bPt = smem_u32(sPt), bdSt = smem_u32(sdSt);
+      const uint32_t bK = smem_u32(sK), bV = smem_u32(sV), bdSt = smem_u32(sdSt);
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, p.status, kTimeoutMma);
       for (int n = 0; n < n_iter && ok; ++n) {
-        ok = mbar_wait_bounded(qd_full, n & 1, abort_flag, p.status, kTimeoutMma) &&
-             mbar_wait_bounded(dq_read, (n & 1) ^ 1, abort_flag, p.status, kTimeoutMma);
+        const int st = n % kQdStages;
+        ok = mbar_wait_bounded(&qd_full[st], (n / kQdStages) & 1, abort_flag, p.status, kTimeoutMma);
         if (!ok) break;
         tc_fence_after();
+        const uint32_t bQ = smem_u32(sQ + st * TILE_BYTES), bdO = smem_u32(sdO + st * TILE_BYTES);
 #pragma unroll
         for (int s = 0; s < D / 16; ++s) mma_bf16_ss(tS, kmajor_desc(bK, s), kmajor_desc(bQ, s), id_kk, s > 0);
+        // dP^T goes where dQ(n-1) was: wait until it has been read out
+        if (n > 0) {
+          ok = mbar_wait_bounded(dq_read, (n - 1) & 1, abort_flag, p.status, kTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+        }
 #pragma unroll
         for (int s = 0; s < D / 16; ++s) mma_bf16_ss(tdP, kmajor_desc(bV, s), kmajor_desc(bdO, s), id_kk, s > 0);
         mma_commit(s_full);
         ok = mbar_wait_bounded(p_full, n & 1, abort_flag, p.status, kTimeoutMma);
         if (!ok) break;
         tc_fence_after();
+        // dQ = dS K first (the gradient warps wait for it), into dP^T's columns
+#pragma unroll
+        for (int s = 0; s < BLK / 16; ++s) mma_bf16_ss(tdP, vmajor_desc(bdSt, s), vmajor_desc(bK, s), id_mm, s > 0);
+        mma_commit(dq_full);
+        // dV += P^T dO with P^T from tensor memory (query columns 64h.. of half h at S^T column 64h)
 #pragma unroll
         for (int s = 0; s < BLK / 16; ++s)
-          mma_bf16_ss(tdV, kmajor_desc(bPt, s), vmajor_desc(bdO, s), id_km, (n > 0 || s > 0) ? 1u : 0u);
+          mma_bf16_ts(tdV, tS + (s >> 2) * 64 + (s & 3) * 8, vmajor_desc(bdO, s), id_km, (n > 0 || s > 0) ? 1u : 0u);
 #pragma unroll
         for (int s = 0; s < BLK / 16; ++s)
           mma_bf16_ss(tdK, kmajor_desc(bdSt, s), vmajor_desc(bQ, s), id_km, (n > 0 || s > 0) ? 1u : 0u);
-#pragma unroll
-        for (int s = 0; s < BLK / 16; ++s) mma_bf16_ss(tS, vmajor_desc(bdSt, s), vmajor_desc(bK, s), id_mm, s > 0);
-        mma_commit(mma2_done);
-        mma_commit(qd_empty);
+        mma_commit(&qd_empty[st]);
       }
       mma_commit(done_bar);
       mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutDrain);
@@ -755,18 +776,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int n = 0; n < n_iter; ++n) {
       const int h = hk * rep + n / nq;
       const int q0 = q_lo + (n % nq) * BLK;
-      float* lse_b = s_lse + (n & 1) * BLK;
-      float* del_b = s_delta + (n & 1) * BLK;
-      {
-        const int qi = q0 + c;
-        const bool qv = qi < p.T;
-        if (half == 0) lse_b[c] = qv ? p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e : INFINITY;
-        else del_b[c] = qv ? p.delta[static_cast<int64_t>(h) * p.T + qi] : 0.f;
+      // stage this query block's LSE (log2 units) and delta once the previous block's are no longer read
+      if (n > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(stg_free, (n - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+        if (!ok) break;
       }
-      mbar_arrive(&stage[n & 1]);
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait_bounded(&stage[n & 1], (n >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
+      {
+        const int qi = min(q0 + c, p.T - 1);
+        if (half == 0) s_lse[c] = p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e;
+        else s_delta[c] = p.delta[static_cast<int64_t>(h) * p.T + qi];
+      }
+      mbar_arrive(stg_full);
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(stg_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
+      // s_full(n) also means dK(n-1) and dQ(n-1) have retired, so the dS^T tile is free again.
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(s_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
@@ -783,9 +806,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int r = col0 + t;
-            const float pe = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -lse_b[r]));
+            const float pe = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[r]));
             pv[t] = pe;
-            ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+            ds[t] = pe * (__uint_as_float(dr[t]) - s_delta[r]) * p.scale;
           }
         } else {
 #pragma unroll
@@ -793,35 +816,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const int r = col0 + t;
             const int qr = q0 + r;
             const bool allowed = kvalid && qr >= lo_c && qr < ke && qr < p.T;
-            const float pe = allowed ? ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -lse_b[r])) : 0.f;
+            const float pe = allowed ? ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[r])) : 0.f;
             pv[t] = pe;
-            ds[t] = pe * (__uint_as_float(dr[t]) - del_b[r]) * p.scale;
+            ds[t] = pe * (__uint_as_float(dr[t]) - s_delta[r]) * p.scale;
           }
         }
-        // 32 q columns = half of one 64-wide chunk = four 16-byte units.
-        uint8_t* prow = sPt + half * CHUNK_BYTES + c * 128;
+        // P^T (bf16 pairs) back into this half's S^T columns (already read): A operand of dV
+        {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(pv[2 * t], pv[2 * t + 1]);
+          tmem_st_32x32b_x16(tS + lane_addr + half * 64 + ch * 16, pk);
+        }
+        // dS^T: 32 q columns = half of one 64-wide swizzled chunk = four 16-byte units.
         uint8_t* drow = sdSt + half * CHUNK_BYTES + c * 128;
         const int u0 = ch * 4;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          uint4 a, b;
-          a.x = pack_bf16x2(pv[8 * u + 0], pv[8 * u + 1]);
-          a.y = pack_bf16x2(pv[8 * u + 2], pv[8 * u + 3]);
-          a.z = pack_bf16x2(pv[8 * u + 4], pv[8 * u + 5]);
-          a.w = pack_bf16x2(pv[8 * u + 6], pv[8 * u + 7]);
+          uint4 b;
           b.x = pack_bf16x2(ds[8 * u + 0], ds[8 * u + 1]);
           b.y = pack_bf16x2(ds[8 * u + 2], ds[8 * u + 3]);
           b.z = pack_bf16x2(ds[8 * u + 4], ds[8 * u + 5]);
           b.w = pack_bf16x2(ds[8 * u + 6], ds[8 * u + 7]);
-          const int off = ((u0 + u) ^ (c & 7)) << 4;
-          *reinterpret_cast<uint4*>(prow + off) = a;
-          *reinterpret_cast<uint4*>(drow + off) = b;
+          *reinterpret_cast<uint4*>(drow + (((u0 + u) ^ (c & 7)) << 4)) = b;
         }
       }
+      mbar_arrive(stg_free);
+      tmem_wait_st();
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(p_full);
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(mma2_done, n & 1, abort_flag, p.status, kTimeoutEpilogue));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(dq_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
       tc_fence_after();
       // dQ rows: thread c now owns query row q0 + c, d columns 64*half .. +63.  Both chunks are read
@@ -829,8 +854,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int qi = q0 + c;
       float* dst = p.dq_acc + (static_cast<int64_t>(qi) * p.Hq + h) * D + half * 64;
       uint32_t rq[64];
-      tmem_ld_32x32b_x32(tS + lane_addr + half * 64, *reinterpret_cast<uint32_t(*)[32]>(rq));
-      tmem_ld_32x32b_x32(tS + lane_addr + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(rq + 32));
+      tmem_ld_32x32b_x32(tdP + lane_addr + half * 64, *reinterpret_cast<uint32_t(*)[32]>(rq));
+      tmem_ld_32x32b_x32(tdP + lane_addr + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(rq + 32));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_read);
@@ -839,6 +864,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int v = 0; v < 16; ++v) red_add_v4(dst + 4 * v, rq + 4 * v);
       }
     }
+    // dK / dV are final once every MMA has retired
+    if (ok && n_iter > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(done_bar, 0, abort_flag, p.status, kTimeoutEpilogue));
     if (ok) {  // keys no query sees (n_iter == 0) get zero gradients
       tc_fence_after();
 #pragma unroll
@@ -941,7 +969,9 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
   }
 }
 
-constexpr int kBwdSmem = 6 * TILE_BYTES + 4 * BLK * 4 + 1024 + 256;  // tiles, lse/delta, align, barriers
+// tiles (K, V, Q and dO rings, dS^T), LSE / delta, align, barriers + TMEM slot
+constexpr int kBwdSmem = (3 + 2 * kQdStages) * TILE_BYTES + 2 * BLK * 4 + 1024 + 256;
+static_assert(kBwdSmem <= 232448, "backward kernel exceeds 227 KB of shared memory");
 
 }  // namespace attn
 }  // namespace mvp
