@@ -11,7 +11,9 @@ Weight gradients: a weight tensor may carry a ``_mvp_grad_acc`` attribute
 buffer owned by the data-parallel wrapper).  When present, the backward of
 :func:`linear` / :func:`embedding` accumulates the weight gradient straight
 into it with the GEMM's fp32 accumulate epilogue, and no per-parameter
-gradient tensor is materialised.
+gradient tensor is materialised.  The forward reads the attribute (``grad_acc``)
+and keeps it on the autograd context: under activation checkpointing the
+backward sees a detached alias of the weight, without the attribute.
 """
 
 from __future__ import annotations
@@ -82,9 +84,15 @@ def gemm(
     return out
 
 
-def _wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor) -> Optional[torch.Tensor]:
-    """dW = dY^T X, accumulated into ``w._mvp_grad_acc`` when present."""
-    acc = getattr(w, "_mvp_grad_acc", None)
+def grad_acc(w: torch.Tensor) -> Optional[torch.Tensor]:
+    """The fp32 gradient accumulator attached to weight ``w`` (``None`` if it has none)."""
+    return getattr(w, "_mvp_grad_acc", None)
+
+
+def _wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor,
+           acc: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """dW = dY^T X, accumulated into ``acc`` (default: ``w._mvp_grad_acc``) when present."""
+    acc = acc if acc is not None else grad_acc(w)
     if acc is not None:
         gemm(dy2, x2, a_mn=True, b_mn=True, out=acc, accumulate=True)
         return None
@@ -99,6 +107,7 @@ class _Linear(torch.autograd.Function):
             x2 = x2.contiguous()
         y = gemm(x2, w)
         ctx.save_for_backward(x2, w)
+        ctx.acc = grad_acc(w)
         return y.view(*x.shape[:-1], w.shape[0])
 
     @staticmethod
@@ -111,8 +120,8 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             dx = gemm(dy2, w, b_mn=True).view(*dy.shape[:-1], w.shape[1])
         dw = None
-        if getattr(w, "_mvp_grad_acc", None) is not None or ctx.needs_input_grad[1]:
-            dw = _wgrad(dy2, x2, w)
+        if ctx.acc is not None or ctx.needs_input_grad[1]:
+            dw = _wgrad(dy2, x2, w, ctx.acc)
         return dx, dw
 
 
@@ -138,6 +147,7 @@ class _RMSNorm(torch.autograd.Function):
         y, rstd = outs[0], outs[1]
         h = outs[2] if residual is not None else x2
         ctx.save_for_backward(h, rstd, w)
+        ctx.acc = grad_acc(w)
         ctx.has_res = residual is not None
         ctx.shape = shape
         return y.view(shape), h.view(shape)
@@ -151,7 +161,7 @@ class _RMSNorm(torch.autograd.Function):
         outs = _ext.ext().rmsnorm_bwd(dy2, h, rstd, w, dh2, True)
         dx = outs[0].view(ctx.shape)
         dw = outs[1]
-        acc = getattr(w, "_mvp_grad_acc", None)
+        acc = ctx.acc
         if acc is not None:
             acc.add_(dw)
             dw = None
@@ -235,6 +245,7 @@ class _QKNormRope(torch.autograd.Function):
         q, k, rstd = _ext.ext().qk_norm_rope_fwd(qkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, eps)
         ctx.save_for_backward(qkv, wq, wk, pos, rstd)
         ctx.meta = (hq, hkv, cache)
+        ctx.accs = (grad_acc(wq), grad_acc(wk))
         return q, k
 
     @staticmethod
@@ -247,8 +258,7 @@ class _QKNormRope(torch.autograd.Function):
             dq.contiguous(), dk.contiguous(), qkv, dqkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, rstd
         )
         out_w = []
-        for w, dw in ((wq, dwq), (wk, dwk)):
-            acc = getattr(w, "_mvp_grad_acc", None)
+        for w, dw, acc in ((wq, dwq, ctx.accs[0]), (wk, dwk, ctx.accs[1])):
             if acc is not None:
                 acc.add_(dw)
                 out_w.append(None)
@@ -327,13 +337,14 @@ class _Embedding(torch.autograd.Function):
     @staticmethod
     def forward(ctx, ids, w, anchor):
         ctx.save_for_backward(ids, w)
+        ctx.acc = grad_acc(w)
         return _ext.ext().embedding_fwd(w, ids.reshape(-1).contiguous(),
                                         _ext.status_buffer(w.device).data_ptr()).view(*ids.shape, w.shape[1])
 
     @staticmethod
     def backward(ctx, dout):
         ids, w = ctx.saved_tensors
-        acc = getattr(w, "_mvp_grad_acc", None)
+        acc = ctx.acc
         dw = None
         if acc is not None:
             _ext.ext().embedding_bwd_(acc, dout.reshape(-1, w.shape[1]).contiguous(), ids.reshape(-1).contiguous())
@@ -368,6 +379,7 @@ class _LinearCE(torch.autograd.Function):
             del logits
         ctx.save_for_backward(h, w, labels, lses)
         ctx.chunk = chunk
+        ctx.acc = grad_acc(w)
         return losses
 
     @staticmethod
@@ -379,7 +391,7 @@ class _LinearCE(torch.autograd.Function):
             g = g.reshape(1).expand(h.shape[0])
         g = g.contiguous()
         dh = torch.empty_like(h)
-        acc = getattr(w, "_mvp_grad_acc", None)
+        acc = ctx.acc
         dw = None
         if acc is None and ctx.needs_input_grad[1]:
             dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)

@@ -419,8 +419,7 @@ class _UlyssesPeer:
         ext.peer_wait_all(self.peer_slots, self.my_slots, self.rank, self.seq, _status(), _WAIT_NS)
 
 
-def _grad_into(w: torch.Tensor, dw: torch.Tensor) -> Optional[torch.Tensor]:
-    acc = getattr(w, "_mvp_grad_acc", None)
+def _grad_into(w: torch.Tensor, dw: torch.Tensor, acc: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     if acc is not None:
         acc.add_(dw)
         return None
@@ -467,6 +466,9 @@ class _UlyssesBlock(torch.autograd.Function):
         y = ops.gemm(oa_local, w_o)
         ctx.save_for_backward(hn, w_qkv, wq, wk, w_o, qkv_h, q, k, o_h, lse, rstd, oa_local, pos)
         ctx.meta = meta
+        # gradient accumulators, read here: under activation checkpointing the saved weights are
+        # detached aliases without the attribute
+        ctx.accs = tuple(ops.grad_acc(t) for t in (w_qkv, wq, wk, w_o))
         return y
 
     @staticmethod
@@ -483,7 +485,8 @@ class _UlyssesBlock(torch.autograd.Function):
         hq, hkv = Hq // W, Hkv // W
         pe = cp.ulysses_peer(hn.device)
         dy = dy.contiguous()
-        dwo = ops._wgrad(dy, oa_local, w_o)
+        acc_qkv, acc_q, acc_k, acc_o = ctx.accs
+        dwo = ops._wgrad(dy, oa_local, w_o, acc_o)
         # dO to the head ranks: the input-gradient GEMM's epilogue scatters heads
         doh, doh_bases = pe.buffer("do_heads", (T, hq * D))
         ext.gemm_ulysses(dy, w_o, True, doh_bases, hq * D, r, C, D, [Hq, 0, 0], _status())
@@ -501,8 +504,8 @@ class _UlyssesBlock(torch.autograd.Function):
                                         route=[W, r, C, full, r * hq * D, Hq * D + r * hkv * D, *dqkv_bases])
         pe.sync()
         dhn = ops.gemm(dqkv, w_qkv, b_mn=True)
-        dwqkv = ops._wgrad(dqkv, hn, w_qkv)
-        return dhn, dwqkv, _grad_into(wq, dwq), _grad_into(wk, dwk), dwo, None
+        dwqkv = ops._wgrad(dqkv, hn, w_qkv, acc_qkv)
+        return dhn, dwqkv, _grad_into(wq, dwq, acc_q), _grad_into(wk, dwk, acc_k), dwo, None
 
 
 # ------------------------------------------------------------------ Ulysses

@@ -246,11 +246,13 @@ def _status():
     return _ext.status_buffer().data_ptr()
 
 
-def _wgrad(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor):
-    """dW = dY^T X accumulated into the runtime's fp32 gradient buffer when the weight has one."""
+def _wgrad(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor, acc: Optional[torch.Tensor] = None):
+    """dW = dY^T X accumulated into the runtime's fp32 gradient buffer when the weight has one
+    (``acc``, captured in the forward: under activation checkpointing the saved weight is a
+    detached alias without the attribute)."""
     from .. import ops
 
-    acc = getattr(w, "_mvp_grad_acc", None)
+    acc = acc if acc is not None else getattr(w, "_mvp_grad_acc", None)
     if acc is not None:
         ops.gemm(dy, x, a_mn=True, b_mn=True, out=acc, accumulate=True)
         return None
@@ -276,6 +278,7 @@ class _AGLinear(torch.autograd.Function):
         ext.gemm_pair_tp(g, w, False, y, w.shape[0], pe.my_slots, seq, rows, r * rows, [], 0, 0, _status(), _WAIT_NS)
         ctx.save_for_backward(x_sp, w)
         ctx.tp = tp
+        ctx.acc = getattr(w, "_mvp_grad_acc", None)
         return y
 
     @staticmethod
@@ -301,7 +304,7 @@ class _AGLinear(torch.autograd.Function):
         ext.peer_push_rows(x_sp.contiguous(), g_bases, r * rows, pe.peer_slots, pe.my_slots, r, seq2, _status(),
                            _WAIT_NS)
         ext.peer_wait_all(pe.peer_slots, pe.my_slots, r, seq2, _status(), _WAIT_NS)
-        dw = _wgrad(dy, g, w)
+        dw = _wgrad(dy, g, w, ctx.acc)
         return dx, dw, None
 
 
@@ -325,6 +328,7 @@ class _RSLinear(torch.autograd.Function):
         ext.peer_slot_reduce(s, y, pe.peer_slots, pe.my_slots, r, seq, _status(), _WAIT_NS)
         ctx.save_for_backward(x, w)
         ctx.tp = tp
+        ctx.acc = getattr(w, "_mvp_grad_acc", None)
         return y
 
     @staticmethod
@@ -343,7 +347,7 @@ class _RSLinear(torch.autograd.Function):
         K = w.shape[1]
         dx = torch.empty(rows * W, K, dtype=torch.bfloat16, device=dy_sp.device)
         ext.gemm_pair_tp(g, w, True, dx, K, pe.my_slots, seq, rows, r * rows, [], 0, 0, _status(), _WAIT_NS)
-        dw = _wgrad(g, x, w)  # the input-grad GEMM above has waited for every slice
+        dw = _wgrad(g, x, w, ctx.acc)  # the input-grad GEMM above has waited for every slice
         return dx, dw, None
 
 

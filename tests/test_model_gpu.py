@@ -90,6 +90,36 @@ def test_native_grads_match_eager_fp32():
 
 
 @cuda
+def test_checkpointed_layers_accumulate_into_the_flat_buffer():
+    """Activation checkpointing recomputes layers with detached aliases of the weights; their
+    gradients must still land in the runtime's fp32 buffer through the GEMM epilogue (no bf16
+    per-parameter .grad) and agree with the run without checkpointing."""
+    model = _tiny(layers=3)
+    runs = []
+    for ckpt in (False, True):
+        gpu = _wrap(copy.deepcopy(model).cuda())
+        if ckpt:
+            gpu.module.gradient_checkpointing_enable({"num_layers": 2})
+        gpu.train()
+        folded = []  # weights whose gradient came back through autograd's .grad (bf16) instead
+        for u in gpu.units:
+            for e in u.entries:
+                if e.shape.numel() > 4096:  # matrices: every one goes through a native GEMM
+                    for mod, pname in e.owners[:1]:
+                        getattr(mod, pname).register_hook(
+                            lambda g, n=e.fqns[0]: folded.append(n) if g is not None else None)
+        T = 512
+        ids, cu, pos = _batch(T, 512, [200], "cuda")
+        loss = gpu(input_ids=ids, labels=ids, position_ids=pos, cu_seq_lens_q=cu, max_length_q=312)["loss"].sum()
+        (loss / T).backward()
+        torch.cuda.synchronize()
+        assert not folded, f"gradients bypassed the fp32 buffer: {folded}"
+        runs.append(torch.cat([u.grad.float().cpu() for u in gpu.units if u.trainable]))
+    a, b = runs
+    assert ((a - b).norm() / b.norm()).item() < 1e-3
+
+
+@cuda
 def test_ce_large_vocab():
     from mvp_engine import ops
 
