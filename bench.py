@@ -238,8 +238,10 @@ def run_ours(args) -> None:
     H, F, L = cfgm.hidden_size, cfgm.intermediate_size, cfgm.num_hidden_layers
     qkv = (cfgm.num_attention_heads + 2 * cfgm.num_key_value_heads) * cfgm.head_dim
     local_tokens = args.seq_len // cp  # context ranks hold 1/cp of the row
+    # saved per token and layer (bf16): norms / residuals, qkv, q + k, attention output and the
+    # SwiGLU input (the activation itself is recomputed in the backward)
     per_layer = local_tokens * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
-                                    cfgm.head_dim + 3 * F) * 1.1
+                                    cfgm.head_dim + 2 * F) * 1.1
     head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
     budget = free - head_ws - (10 << 30)
     keep = max(0, min(L, int(budget // per_layer)))

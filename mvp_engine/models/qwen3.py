@@ -188,26 +188,30 @@ class Qwen3DecoderLayer(nn.Module):
                                  _as_compute(attn.k_norm.weight, hn), _as_compute(attn.o_proj.weight, hn), ctx,
                                  Hq, Hkv, D, attn.q_norm.variance_epsilon, attn.scaling)
             hn2, h2 = self.post_attention_layernorm(o, h)
-            wgu = self.fused_weight("gate_up", hn2)
-            act = ops.swiglu(ops.linear(hn2, wgu))
-            return ops.linear(act, _as_compute(self.mlp.down_proj.weight, act)), h2
+            gu = ops.linear(hn2, self.fused_weight("gate_up", hn2))
+            return ops.swiglu_linear(gu, _as_compute(self.mlp.down_proj.weight, gu)), h2
         qkv = (tp.column_linear(hn, self.fused_weight("qkv", hn)) if tp is not None
                else ops.linear(hn, self.fused_weight("qkv", hn)))
-        q, k = ops.qk_norm_rope(
-            qkv, Hq, Hkv, _as_compute(attn.q_norm.weight, hn), _as_compute(attn.k_norm.weight, hn),
-            ctx.position_ids, ctx.rope, attn.q_norm.variance_epsilon,
-        )
-        v = qkv[:, (Hq + Hkv) * D:].view(-1, Hkv, D)
-        o = ctx.attention(q, k, v, attn.scaling)
+        wq, wk = _as_compute(attn.q_norm.weight, hn), _as_compute(attn.k_norm.weight, hn)
+        if cp is None and ctx.causal:  # one autograd node: all of q/k/v's gradients land in one dqkv buffer
+            o = ops.qk_norm_rope_attention(qkv, Hq, Hkv, wq, wk, ctx.position_ids, ctx.rope,
+                                           attn.q_norm.variance_epsilon, ctx.cu_seqlens, ctx.max_seqlen,
+                                           attn.scaling)
+        else:
+            q, k = ops.qk_norm_rope(qkv, Hq, Hkv, wq, wk, ctx.position_ids, ctx.rope, attn.q_norm.variance_epsilon)
+            v = qkv[:, (Hq + Hkv) * D:].view(-1, Hkv, D)
+            o = ctx.attention(q, k, v, attn.scaling)
         o = o.reshape(o.shape[0], Hq * D)
         wo = _as_compute(attn.o_proj.weight, hn)
         o = tp.row_linear(o, wo) if tp is not None else ops.linear(o, wo)
         hn2, h2 = self.post_attention_layernorm(o, h)
         wgu = self.fused_weight("gate_up", hn2)
         gu = tp.column_linear(hn2, wgu) if tp is not None else ops.linear(hn2, wgu)
-        act = ops.swiglu(gu)
-        wd = _as_compute(self.mlp.down_proj.weight, act)
-        out = tp.row_linear(act, wd) if tp is not None else ops.linear(act, wd)
+        wd = _as_compute(self.mlp.down_proj.weight, gu)
+        if tp is not None:
+            out = tp.row_linear(ops.swiglu(gu), wd)
+        else:  # the activation is recomputed in the backward instead of being kept
+            out = ops.swiglu_linear(gu, wd)
         return out, h2
 
 

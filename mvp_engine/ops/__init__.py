@@ -31,8 +31,10 @@ __all__ = [
     "linear",
     "rms_norm",
     "qk_norm_rope",
+    "qk_norm_rope_attention",
     "RopeCache",
     "swiglu",
+    "swiglu_linear",
     "embedding",
     "fused_linear_cross_entropy",
     "adamw_step_",
@@ -273,6 +275,65 @@ class _QKNormRope(torch.autograd.Function):
         return torch.zeros_like(qkv)
 
 
+class _QKNormRopeAttention(torch.autograd.Function):
+    """QK-norm + RoPE + varlen flash attention on one ``qkv`` buffer.  The backward writes dV (from the
+    attention kernel) and dQ / dK (from the norm/RoPE kernel) straight into one ``dqkv`` buffer, so no
+    zero fill, slice copy or gradient sum over ``qkv`` is needed."""
+
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, pos, hq, hkv, cache, eps, cu, scale, causal):
+        D = cache.head_dim
+        cos_t, sin_t, axis = cache.tables(qkv.device)
+        ext = _ext.ext()
+        q, k, rstd = ext.qk_norm_rope_fwd(qkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, eps)
+        v = qkv[:, (hq + hkv) * D:].view(qkv.shape[0], hkv, D)
+        o, lse = ext.flash_attn_fwd(q, k, v, cu, scale, causal, _ext.status_buffer(q.device).data_ptr())
+        ctx.save_for_backward(qkv, wq, wk, pos, rstd, q, k, o, lse, cu)
+        ctx.meta = (hq, hkv, cache, scale, causal)
+        ctx.accs = (grad_acc(wq), grad_acc(wk))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, wq, wk, pos, rstd, q, k, o, lse, cu = ctx.saved_tensors
+        hq, hkv, cache, scale, causal = ctx.meta
+        D = cache.head_dim
+        T = qkv.shape[0]
+        ext = _ext.ext()
+        dqkv = torch.empty_like(qkv)
+        v = qkv[:, (hq + hkv) * D:].view(T, hkv, D)
+        dk_buf = torch.empty(T, hkv, D, dtype=qkv.dtype, device=qkv.device)
+        dq, dk, _ = ext.flash_attn_bwd(do.contiguous(), q, k, v, o, lse, cu, scale, causal,
+                                       _ext.status_buffer(q.device).data_ptr(), dk_out=dk_buf,
+                                       dv_out=dqkv[:, (hq + hkv) * D:].view(T, hkv, D))
+        cos_t, sin_t, axis = cache.tables(qkv.device, 0)
+        dwq, dwk = ext.qk_norm_rope_bwd(dq, dk, qkv, dqkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, rstd)
+        out_w = []
+        for w, dw, acc in ((wq, dwq, ctx.accs[0]), (wk, dwk, ctx.accs[1])):
+            if acc is not None:
+                acc.add_(dw)
+                out_w.append(None)
+            else:
+                out_w.append(dw.to(w.dtype))
+        return dqkv, out_w[0], out_w[1], None, None, None, None, None, None, None, None
+
+
+def qk_norm_rope_attention(qkv: torch.Tensor, n_q: int, n_kv: int, wq: torch.Tensor, wk: torch.Tensor,
+                           pos: torch.Tensor, cache: "RopeCache", eps: float, cu_seqlens: torch.Tensor,
+                           max_seqlen: int, scale: float, causal: bool = True) -> torch.Tensor:
+    """``flash_attn_varlen(*qk_norm_rope(qkv), v)`` over packed documents; returns ``o [T, n_q, D]``."""
+    D = cache.head_dim
+    if not _native(qkv) or D != 128 or qkv.dtype != torch.bfloat16 or qkv.stride(-1) != 1:
+        from .attention import flash_attn_varlen
+
+        q, k = qk_norm_rope(qkv, n_q, n_kv, wq, wk, pos, cache, eps)
+        v = qkv[:, (n_q + n_kv) * D:].view(-1, n_kv, D)
+        return flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=causal, softmax_scale=scale)
+    pos = pos.to(torch.int32).contiguous()
+    cu = cu_seqlens.to(device=qkv.device, dtype=torch.int32)
+    return _QKNormRopeAttention.apply(qkv, wq, wk, pos, n_q, n_kv, cache, float(eps), cu, float(scale), bool(causal))
+
+
 def _rotate_half(x):
     x1, x2 = x.chunk(2, dim=-1)
     return torch.cat((-x2, x1), dim=-1)
@@ -330,6 +391,42 @@ def swiglu(gu: torch.Tensor) -> torch.Tensor:
         g, u = gu.chunk(2, dim=-1)
         return F.silu(g) * u
     return _SwiGLU.apply(gu)
+
+
+class _SwiGLULinear(torch.autograd.Function):
+    """``swiglu(gu) @ w^T`` that keeps only ``gu`` for the backward: the activation (half the size of
+    ``gu``) is recomputed there, one bandwidth-bound pass, instead of being held from forward to
+    backward.  The memory saved lets more decoder layers skip activation checkpointing."""
+
+    @staticmethod
+    def forward(ctx, gu, w):
+        gu = gu.contiguous()
+        act = _ext.ext().swiglu_fwd(gu)
+        y = gemm(act, w)
+        ctx.save_for_backward(gu, w)
+        ctx.acc = grad_acc(w)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        gu, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        act = _ext.ext().swiglu_fwd(gu)
+        dw = None
+        if ctx.acc is not None or ctx.needs_input_grad[1]:
+            dw = _wgrad(dy, act, w, ctx.acc)
+        dact = gemm(dy, w, b_mn=True)
+        del act
+        return _ext.ext().swiglu_bwd(gu, dact), dw
+
+
+def swiglu_linear(gu: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``linear(swiglu(gu), w)`` (the SwiGLU MLP's down projection) without keeping the activation."""
+    if not _native(gu):
+        return F.linear(swiglu(gu), w.to(gu.dtype))
+    if w.dtype != torch.bfloat16 or gu.dtype != torch.bfloat16:
+        return linear(swiglu(gu), w)
+    return _SwiGLULinear.apply(gu, w)
 
 
 # ---------------------------------------------------------------- embedding

@@ -188,6 +188,27 @@ def test_swiglu():
 
 
 @cuda
+def test_swiglu_linear_matches_fp32():
+    """The SwiGLU + down-projection op that recomputes the activation in its backward."""
+    ops = _ops()
+    torch.manual_seed(9)
+    T, F_, H = 512, 768, 512
+    gu = torch.randn(T, 2 * F_, device="cuda").bfloat16().requires_grad_()
+    w = (torch.randn(H, F_, device="cuda") * 0.05).bfloat16().requires_grad_()
+    out = ops.swiglu_linear(gu, w)
+    g = torch.randn_like(out)
+    out.backward(g)
+    guf = gu.detach().float().requires_grad_()
+    wf = w.detach().float().requires_grad_()
+    a, b = guf.chunk(2, -1)
+    of = (torch.nn.functional.silu(a) * b) @ wf.t()
+    of.backward(g.float())
+    assert _rel_err(out, of) < 2e-2
+    assert _rel_err(gu.grad, guf.grad) < 2e-2
+    assert _rel_err(w.grad, wf.grad) < 2e-2
+
+
+@cuda
 def test_embedding():
     ops = _ops()
     torch.manual_seed(6)
