@@ -160,15 +160,16 @@ class _RMSNorm(torch.autograd.Function):
         H = ctx.shape[-1]
         dy2 = dy.reshape(-1, H).contiguous()
         dh2 = dh.reshape(-1, H).contiguous() if dh is not None else None
-        outs = _ext.ext().rmsnorm_bwd(dy2, h, rstd, w, dh2, True)
+        acc = ctx.acc if (ctx.acc is not None and ctx.acc.is_contiguous() and ctx.acc.dtype == torch.float32) else None
+        outs = _ext.ext().rmsnorm_bwd(dy2, h, rstd, w, dh2, True, dw_acc=acc)
         dx = outs[0].view(ctx.shape)
-        dw = outs[1]
-        acc = ctx.acc
-        if acc is not None:
-            acc.add_(dw)
+        if acc is not None:  # added into the fp32 accumulator by the kernel
+            dw = None
+        elif ctx.acc is not None:
+            ctx.acc.add_(outs[1])
             dw = None
         else:
-            dw = dw.to(w.dtype)
+            dw = outs[1].to(w.dtype)
         return dx, dw, (dx if ctx.has_res else None), None
 
 
@@ -307,6 +308,13 @@ class _QKNormRopeAttention(torch.autograd.Function):
                                        _ext.status_buffer(q.device).data_ptr(), dk_out=dk_buf,
                                        dv_out=dqkv[:, (hq + hkv) * D:].view(T, hkv, D))
         cos_t, sin_t, axis = cache.tables(qkv.device, 0)
+        aq, ak = ctx.accs
+        if (aq is not None and ak is not None and aq.is_contiguous() and ak.is_contiguous() and
+                aq.dtype == torch.float32 and ak.dtype == torch.float32):
+            # norm-weight gradients added into the fp32 accumulators by the kernel itself
+            ext.qk_norm_rope_bwd(dq, dk, qkv, dqkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, rstd,
+                                 dwq_acc=aq, dwk_acc=ak)
+            return dqkv, None, None, None, None, None, None, None, None, None, None
         dwq, dwk = ext.qk_norm_rope_bwd(dq, dk, qkv, dqkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, rstd)
         out_w = []
         for w, dw, acc in ((wq, dwq, ctx.accs[0]), (wk, dwk, ctx.accs[1])):

@@ -7,7 +7,8 @@ void gemm_sm100(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool 
 std::vector<torch::Tensor> rmsnorm_fwd(const torch::Tensor& x, const c10::optional<torch::Tensor>& res,
                                        const torch::Tensor& w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& h, const torch::Tensor& rstd,
-                                       const torch::Tensor& w, const c10::optional<torch::Tensor>& dres, bool need_dw);
+                                       const torch::Tensor& w, const c10::optional<torch::Tensor>& dres, bool need_dw,
+                                       const c10::optional<torch::Tensor>& dw_acc);
 std::vector<torch::Tensor> qk_norm_rope_fwd(const torch::Tensor& qkv, int64_t Hq, int64_t Hkv,
                                             const torch::Tensor& wq, const torch::Tensor& wk,
                                             const torch::Tensor& pos, const torch::Tensor& axis_of,
@@ -18,7 +19,9 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
                                             const torch::Tensor& pos, const torch::Tensor& axis_of,
                                             const torch::Tensor& cos_tab, const torch::Tensor& sin_tab,
                                             const torch::Tensor& rstd,
-                                            const c10::optional<std::vector<int64_t>>& route);
+                                            const c10::optional<std::vector<int64_t>>& route,
+                                            const c10::optional<torch::Tensor>& dwq_acc,
+                                            const c10::optional<torch::Tensor>& dwk_acc);
 torch::Tensor swiglu_fwd(const torch::Tensor& gu);
 torch::Tensor swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& dout);
 
@@ -79,11 +82,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mvp_engine sm_100a kernels";
   m.def("gemm", &gemm_sm100, "tcgen05 bf16 GEMM C (+)= A * B^T with K- or MN-major operands");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("h"), py::arg("rstd"), py::arg("w"), py::arg("dres"),
+        py::arg("need_dw"), py::arg("dw_acc") = py::none());
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd, py::arg("dq"), py::arg("dk"), py::arg("qkv"), py::arg("dqkv"),
         py::arg("Hq"), py::arg("Hkv"), py::arg("wq"), py::arg("wk"), py::arg("pos"), py::arg("axis_of"),
-        py::arg("cos_tab"), py::arg("sin_tab"), py::arg("rstd"), py::arg("route") = py::none());
+        py::arg("cos_tab"), py::arg("sin_tab"), py::arg("rstd"), py::arg("route") = py::none(),
+        py::arg("dwq_acc") = py::none(), py::arg("dwk_acc") = py::none());
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);

@@ -128,7 +128,7 @@ __global__ void rmsnorm_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy, cons
 // of a row strip; partial[blockIdx.y, col].
 __global__ void rmsnorm_bwd_dw_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ h,
                                       const float* __restrict__ rstd_in, float* __restrict__ partial, int rows, int H,
-                                      int rows_per_split) {
+                                      int rows_per_split, int accumulate) {
   __shared__ float red[8][64];
   const int col = blockIdx.x * 64 + threadIdx.x * 2;
   const int r0 = blockIdx.y * rows_per_split;
@@ -154,8 +154,13 @@ __global__ void rmsnorm_bwd_dw_kernel(const __nv_bfloat16* __restrict__ dy, cons
       s0 += red[j][threadIdx.x * 2];
       s1 += red[j][threadIdx.x * 2 + 1];
     }
-    partial[static_cast<int64_t>(blockIdx.y) * H + col] = s0;
-    partial[static_cast<int64_t>(blockIdx.y) * H + col + 1] = s1;
+    if (accumulate) {  // straight into the caller's fp32 gradient accumulator
+      atomicAdd(partial + col, s0);
+      atomicAdd(partial + col + 1, s1);
+    } else {
+      partial[static_cast<int64_t>(blockIdx.y) * H + col] = s0;
+      partial[static_cast<int64_t>(blockIdx.y) * H + col + 1] = s1;
+    }
   }
 }
 
@@ -185,55 +190,55 @@ struct QKRopeArgs {
 
 __device__ __forceinline__ int clamp_pos(int p, int rows) { return min(max(p, 0), rows - 1); }
 
+// One warp per token: the lane's cos / sin (four frequencies) and norm weights are loaded once and
+// reused for every head of the token; heads are processed four at a time for independent reductions.
 __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
   constexpr int D = 128;
   const int warps = blockDim.x / 32;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32;
+  const int t = blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  if (t >= a.T) return;
   const int heads = a.Hq + a.Hkv;
-  if (item >= static_cast<int64_t>(a.T) * heads) return;
-  const int t = static_cast<int>(item / heads);
-  const int hd = static_cast<int>(item % heads);
-  const bool is_q = hd < a.Hq;
-  const __nv_bfloat16* src = a.qkv + static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(hd) * D + lane * 4;
-  const __nv_bfloat16* w = (is_q ? a.wq : a.wk) + lane * 4;
-  float x[4], wf[4];
-  {
-    const uint2 u = *reinterpret_cast<const uint2*>(src);
-    const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-    const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-    x[0] = p0.x; x[1] = p0.y; x[2] = p1.x; x[3] = p1.y;
-    const uint2 v = *reinterpret_cast<const uint2*>(w);
-    const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-    const float2 q1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
-    wf[0] = q0.x; wf[1] = q0.y; wf[2] = q1.x; wf[3] = q1.y;
-  }
-  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-  ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / D + a.eps);
-  if (lane == 0) a.rstd[static_cast<int64_t>(t) * heads + hd] = rstd;
-  float y[4], partner[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) y[i] = bf16r(wf[i] * bf16r(x[i] * rstd));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
-  const bool lo = lane < 16;
-  float o[4];
+  float c[4], sn[4], wq[4], wk[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int f = (lane * 4 + i) & 63;
-    const int ax = a.axis_of[f];
-    const int p = clamp_pos(a.pos[ax * a.pos_stride + t], a.tab_rows);
-    const float c = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
-    const float s = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
-    o[i] = lo ? (y[i] * c - partner[i] * s) : (y[i] * c + partner[i] * s);
+    const int p = clamp_pos(a.pos[a.axis_of[f] * a.pos_stride + t], a.tab_rows);
+    c[i] = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
+    sn[i] = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
+    wq[i] = __bfloat162float(a.wq[lane * 4 + i]);
+    wk[i] = __bfloat162float(a.wk[lane * 4 + i]);
   }
-  __nv_bfloat16* dst = is_q ? a.q_out + (static_cast<int64_t>(t) * a.Hq + hd) * D
-                            : a.k_out + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D;
-  uint2 u;
-  u.x = pack_bf16x2(o[0], o[1]);
-  u.y = pack_bf16x2(o[2], o[3]);
-  *reinterpret_cast<uint2*>(dst + lane * 4) = u;
+  const bool lo = lane < 16;
+  const __nv_bfloat16* row = a.qkv + static_cast<int64_t>(t) * a.ld_qkv + lane * 4;
+#pragma unroll 4
+  for (int hd = 0; hd < heads; ++hd) {
+    const bool is_q = hd < a.Hq;
+    float x[4];
+    {
+      const uint2 u = *reinterpret_cast<const uint2*>(row + static_cast<int64_t>(hd) * D);
+      const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      x[0] = p0.x; x[1] = p0.y; x[2] = p1.x; x[3] = p1.y;
+    }
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / D + a.eps);
+    if (lane == 0) a.rstd[static_cast<int64_t>(t) * heads + hd] = rstd;
+    float y[4], partner[4], o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = bf16r((is_q ? wq[i] : wk[i]) * bf16r(x[i] * rstd));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = lo ? (y[i] * c[i] - partner[i] * sn[i]) : (y[i] * c[i] + partner[i] * sn[i]);
+    __nv_bfloat16* dst = is_q ? a.q_out + (static_cast<int64_t>(t) * a.Hq + hd) * D
+                              : a.k_out + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D;
+    uint2 u;
+    u.x = pack_bf16x2(o[0], o[1]);
+    u.y = pack_bf16x2(o[2], o[3]);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = u;
+  }
 }
 
 struct QKRopeBwdArgs {
@@ -251,12 +256,23 @@ struct QKRopeBwdArgs {
   const float* rstd;
   __nv_bfloat16* dqkv;  // [T, ld_dqkv]: q and k parts written
   int64_t ld_dqkv;
-  float* dw_partial;  // [gridDim.x, 2, D]
+  float* dw_partial;  // [gridDim.x, 2, D], or with dw_accumulate the fp32 accumulators dwq, dwk
+  float* dwk_acc;
+  int dw_accumulate;
   int T, Hq, Hkv;
   int tab_rows;
   UlyssesRoute route;  // optional: dq / dk rows written to the token's rank (its dqkv) instead of dqkv
 };
 
+__device__ __forceinline__ void load_bf16x4(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  v[0] = p0.x; v[1] = p0.y; v[2] = p1.x; v[3] = p1.y;
+}
+
+// One warp per token (grid-stride): cos / sin and the norm weights of the lane's four elements are
+// loaded once per token and reused for every head; 8-byte loads and stores per lane.
 __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
   constexpr int D = 128;
   __shared__ float red[2][D];
@@ -265,60 +281,56 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   const int heads = a.Hq + a.Hkv;
-  const int64_t total = static_cast<int64_t>(a.T) * heads;
+  const bool lo = lane < 16;
+  float wq[4], wk[4];
+  load_bf16x4(a.wq + lane * 4, wq);
+  load_bf16x4(a.wk + lane * 4, wk);
   float accq[4] = {0.f, 0.f, 0.f, 0.f}, acck[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32; item < total;
-       item += static_cast<int64_t>(gridDim.x) * warps) {
-    const int t = static_cast<int>(item / heads);
-    const int hd = static_cast<int>(item % heads);
-    const bool is_q = hd < a.Hq;
-    const __nv_bfloat16* g_src = is_q ? a.dq + (static_cast<int64_t>(t) * a.Hq + hd) * D
-                                      : a.dk + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D;
-    float g[4], x[4], wf[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      g[i] = __bfloat162float(g_src[lane * 4 + i]);
-      x[i] = __bfloat162float(a.qkv[static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(hd) * D + lane * 4 + i]);
-      wf[i] = __bfloat162float((is_q ? a.wq : a.wk)[lane * 4 + i]);
-    }
-    float gp[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) gp[i] = __shfl_xor_sync(0xffffffffu, g[i], 16);
-    const bool lo = lane < 16;
-    float dy[4];
+  for (int t = blockIdx.x * warps + threadIdx.x / 32; t < a.T; t += gridDim.x * warps) {
+    float c[4], sn[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int f = (lane * 4 + i) & 63;
-      const int ax = a.axis_of[f];
-      const int p = clamp_pos(a.pos[ax * a.pos_stride + t], a.tab_rows);
-      const float c = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
-      const float s = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
-      dy[i] = lo ? (g[i] * c + gp[i] * s) : (g[i] * c - gp[i] * s);
+      const int p = clamp_pos(a.pos[a.axis_of[f] * a.pos_stride + t], a.tab_rows);
+      c[i] = bf16r(a.cos_tab[static_cast<int64_t>(p) * 64 + f]);
+      sn[i] = bf16r(a.sin_tab[static_cast<int64_t>(p) * 64 + f]);
     }
-    const float rstd = a.rstd[static_cast<int64_t>(t) * heads + hd];
-    float dot = 0.f;
+    int owner = 0, lrow = 0;
+    if (a.route.dst[0] != nullptr) ulysses_home(a.route, t, owner, lrow);
+#pragma unroll 4
+    for (int hd = 0; hd < heads; ++hd) {
+      const bool is_q = hd < a.Hq;
+      float g[4], x[4];
+      load_bf16x4(is_q ? a.dq + (static_cast<int64_t>(t) * a.Hq + hd) * D + lane * 4
+                       : a.dk + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D + lane * 4, g);
+      load_bf16x4(a.qkv + static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(hd) * D + lane * 4, x);
+      float gp[4], dy[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) dot += dy[i] * wf[i] * x[i] * rstd;
-    dot = warp_sum(dot) / D;
-    float dx[4];
+      for (int i = 0; i < 4; ++i) gp[i] = __shfl_xor_sync(0xffffffffu, g[i], 16);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      dx[i] = rstd * (wf[i] * dy[i] - x[i] * rstd * dot);
-      const float xh = bf16r(x[i] * rstd);
-      if (is_q) accq[i] += dy[i] * xh;
-      else acck[i] += dy[i] * xh;
+      for (int i = 0; i < 4; ++i) dy[i] = lo ? (g[i] * c[i] + gp[i] * sn[i]) : (g[i] * c[i] - gp[i] * sn[i]);
+      const float rstd = a.rstd[static_cast<int64_t>(t) * heads + hd];
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dot += dy[i] * (is_q ? wq[i] : wk[i]) * x[i] * rstd;
+      dot = warp_sum(dot) / D;
+      float dx[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        dx[i] = rstd * ((is_q ? wq[i] : wk[i]) * dy[i] - x[i] * rstd * dot);
+        const float xh = bf16r(x[i] * rstd);
+        if (is_q) accq[i] += dy[i] * xh;
+        else acck[i] += dy[i] * xh;
+      }
+      __nv_bfloat16* dst = a.dqkv + static_cast<int64_t>(t) * a.ld_dqkv + static_cast<int64_t>(hd) * D + lane * 4;
+      if (a.route.dst[0] != nullptr)  // Ulysses: back to the token's rank, global head columns
+        dst = reinterpret_cast<__nv_bfloat16*>(a.route.dst[owner]) + static_cast<int64_t>(lrow) * a.route.ld +
+              (is_q ? a.route.col0 + hd * D : a.route.col0_k + (hd - a.Hq) * D) + lane * 4;
+      uint2 u;
+      u.x = pack_bf16x2(dx[0], dx[1]);
+      u.y = pack_bf16x2(dx[2], dx[3]);
+      *reinterpret_cast<uint2*>(dst) = u;
     }
-    __nv_bfloat16* dst = a.dqkv + static_cast<int64_t>(t) * a.ld_dqkv + static_cast<int64_t>(hd) * D + lane * 4;
-    if (a.route.dst[0] != nullptr) {  // Ulysses: back to the token's rank, global head columns
-      int owner, lrow;
-      ulysses_home(a.route, t, owner, lrow);
-      dst = reinterpret_cast<__nv_bfloat16*>(a.route.dst[owner]) + static_cast<int64_t>(lrow) * a.route.ld +
-            (is_q ? a.route.col0 + hd * D : a.route.col0_k + (hd - a.Hq) * D) + lane * 4;
-    }
-    uint2 u;
-    u.x = pack_bf16x2(dx[0], dx[1]);
-    u.y = pack_bf16x2(dx[2], dx[3]);
-    *reinterpret_cast<uint2*>(dst) = u;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -326,8 +338,10 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
     atomicAdd(&red[1][lane * 4 + i], acck[i]);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x)
-    a.dw_partial[static_cast<int64_t>(blockIdx.x) * 2 * D + i] = (&red[0][0])[i];
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+    if (a.dw_accumulate) atomicAdd(i < D ? a.dw_partial + i : a.dwk_acc + (i - D), (&red[0][0])[i]);
+    else a.dw_partial[static_cast<int64_t>(blockIdx.x) * 2 * D + i] = (&red[0][0])[i];
+  }
   if (a.route.dst[0] != nullptr) __threadfence_system();
 }
 
@@ -419,7 +433,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(const torch::Tensor& x, const c10::option
 
 std::vector<torch::Tensor> rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& h, const torch::Tensor& rstd,
                                        const torch::Tensor& w, const c10::optional<torch::Tensor>& dres,
-                                       bool need_dw) {
+                                       bool need_dw, const c10::optional<torch::Tensor>& dw_acc) {
   CHECK_BF16(dy);
   CHECK_BF16(h);
   CHECK_BF16(w);
@@ -442,12 +456,21 @@ std::vector<torch::Tensor> rmsnorm_bwd(const torch::Tensor& dy, const torch::Ten
   if (!need_dw) return {dx};
   const int splits = std::max(1, std::min(64, rows / 64));
   const int rows_per_split = (rows + splits - 1) / splits;
-  auto partial = torch::empty({splits, H}, h.options().dtype(at::kFloat));
   dim3 grid((H + 63) / 64, splits), block(32, 8);
+  if (dw_acc.has_value()) {  // dW added to the caller's fp32 accumulator [H]: no partials, no reduction
+    TORCH_CHECK(dw_acc->scalar_type() == at::kFloat && dw_acc->is_contiguous() && dw_acc->numel() == H,
+                "rmsnorm_bwd: dw_acc must be contiguous fp32 [H]");
+    mvp::rmsnorm_bwd_dw_kernel<<<grid, block, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()),
+        rstd.data_ptr<float>(), dw_acc->data_ptr<float>(), rows, H, rows_per_split, 1);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {dx, *dw_acc};
+  }
+  auto partial = torch::empty({splits, H}, h.options().dtype(at::kFloat));
   mvp::rmsnorm_bwd_dw_kernel<<<grid, block, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
                                                          reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()),
                                                          rstd.data_ptr<float>(), partial.data_ptr<float>(), rows, H,
-                                                         rows_per_split);
+                                                         rows_per_split, 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dx, partial.sum(0)};
 }
@@ -485,9 +508,8 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(const torch::Tensor& qkv, int64_t Hq
   a.eps = static_cast<float>(eps);
   a.tab_rows = static_cast<int>(cos_tab.size(0));
   TORCH_CHECK(a.tab_rows > 0 && sin_tab.size(0) == cos_tab.size(0), "qk_norm_rope: cos/sin tables");
-  const int64_t items = static_cast<int64_t>(T) * (Hq + Hkv);
-  const int threads = 256;
-  mvp::qk_norm_rope_fwd_kernel<<<static_cast<int>((items + 7) / 8), threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  const int threads = 256;  // 8 tokens per block
+  mvp::qk_norm_rope_fwd_kernel<<<static_cast<int>((T + 7) / 8), threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {q, k, rstd};
 }
@@ -499,7 +521,9 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
                                             const torch::Tensor& pos, const torch::Tensor& axis_of,
                                             const torch::Tensor& cos_tab, const torch::Tensor& sin_tab,
                                             const torch::Tensor& rstd,
-                                            const c10::optional<std::vector<int64_t>>& route) {
+                                            const c10::optional<std::vector<int64_t>>& route,
+                                            const c10::optional<torch::Tensor>& dwq_acc,
+                                            const c10::optional<torch::Tensor>& dwk_acc) {
   CHECK_BF16(dq);
   CHECK_BF16(dk);
   TORCH_CHECK(dqkv.stride(-1) == 1 && qkv.stride(-1) == 1, "qk_norm_rope_bwd: unit inner stride");
@@ -507,7 +531,15 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
   const at::cuda::CUDAGuard guard(qkv.device());
   const int threads = 256;
   const int blocks = 148 * 4;
-  auto partial = torch::empty({blocks, 2, 128}, qkv.options().dtype(at::kFloat));
+  // dwq_acc / dwk_acc (both or neither): the norm-weight gradients are added straight into these fp32
+  // accumulators [128] and returned as they are.
+  const bool acc = dwq_acc.has_value() && dwk_acc.has_value();
+  if (acc)
+    TORCH_CHECK(dwq_acc->scalar_type() == at::kFloat && dwk_acc->scalar_type() == at::kFloat &&
+                    dwq_acc->is_contiguous() && dwk_acc->is_contiguous() && dwq_acc->numel() == 128 &&
+                    dwk_acc->numel() == 128,
+                "qk_norm_rope_bwd: fp32 [128] accumulators");
+  auto partial = acc ? torch::Tensor() : torch::empty({blocks, 2, 128}, qkv.options().dtype(at::kFloat));
   mvp::QKRopeBwdArgs a;
   a.dq = reinterpret_cast<const __nv_bfloat16*>(dq.data_ptr());
   a.dk = reinterpret_cast<const __nv_bfloat16*>(dk.data_ptr());
@@ -523,7 +555,9 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
   a.rstd = rstd.data_ptr<float>();
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.ld_dqkv = dqkv.stride(0);
-  a.dw_partial = partial.data_ptr<float>();
+  a.dw_partial = acc ? dwq_acc->data_ptr<float>() : partial.data_ptr<float>();
+  a.dwk_acc = acc ? dwk_acc->data_ptr<float>() : nullptr;
+  a.dw_accumulate = acc ? 1 : 0;
   a.T = T;
   a.Hq = static_cast<int>(Hq);
   a.Hkv = static_cast<int>(Hkv);
@@ -533,6 +567,7 @@ std::vector<torch::Tensor> qk_norm_rope_bwd(const torch::Tensor& dq, const torch
               "qk_norm_rope_bwd: routed rows need T = 2 x world x chunk");
   mvp::qk_norm_rope_bwd_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (acc) return {*dwq_acc, *dwk_acc};
   auto dw = partial.sum(0);
   return {dw[0], dw[1]};
 }
