@@ -126,6 +126,93 @@ __global__ void rmsnorm_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy, cons
 
 // Column partial sums of dy * bf16(h * rstd): block (32 x 8) covers 64 columns
 // of a row strip; partial[blockIdx.y, col].
+// Row-resident variants for H = CH x 1024: one 128-thread CTA per row, each thread keeps its CH x 8
+// elements in registers between the reduction and the output pass, so every input is read once.
+__device__ __forceinline__ float block_sum_128(float v, float* part) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return (part[0] + part[1]) + (part[2] + part[3]);
+}
+
+template <int CH>
+__global__ void __launch_bounds__(128) rmsnorm_fwd_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              const __nv_bfloat16* __restrict__ res,
+                                                              const __nv_bfloat16* __restrict__ w,
+                                                              __nv_bfloat16* __restrict__ y,
+                                                              __nv_bfloat16* __restrict__ h_out,
+                                                              float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float part[4];
+  const int64_t off = static_cast<int64_t>(blockIdx.x) * H;
+  float f[CH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (k * 128 + threadIdx.x) * 8;
+    load8(x + off + c, f[k]);
+    if (res != nullptr) {
+      float r[8];
+      load8(res + off + c, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[k][i] = bf16r(f[k][i] + r[i]);
+      store8(h_out + off + c, f[k]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[k][i] * f[k][i];
+  }
+  const float rstd = rsqrtf(block_sum_128(ss, part) / static_cast<float>(H) + eps);
+  if (threadIdx.x == 0) rstd_out[blockIdx.x] = rstd;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (k * 128 + threadIdx.x) * 8;
+    float wf[8], o[8];
+    load8(w + c, wf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = wf[i] * bf16r(f[k][i] * rstd);
+    store8(y + off + c, o);
+  }
+}
+
+template <int CH>
+__global__ void __launch_bounds__(128) rmsnorm_bwd_dx_row_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                                 const __nv_bfloat16* __restrict__ h,
+                                                                 const float* __restrict__ rstd_in,
+                                                                 const __nv_bfloat16* __restrict__ w,
+                                                                 const __nv_bfloat16* __restrict__ dres,
+                                                                 __nv_bfloat16* __restrict__ dx, int H) {
+  __shared__ float part[4];
+  const int64_t off = static_cast<int64_t>(blockIdx.x) * H;
+  const float rstd = rstd_in[blockIdx.x];
+  float g[CH][8], hv[CH][8];
+  float dot = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (k * 128 + threadIdx.x) * 8;
+    float wf[8];
+    load8(dy + off + c, g[k]);
+    load8(h + off + c, hv[k]);
+    load8(w + c, wf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dot += g[k][i] * wf[i] * hv[k][i] * rstd;
+  }
+  dot = block_sum_128(dot, part) / static_cast<float>(H);
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (k * 128 + threadIdx.x) * 8;
+    float wf[8], o[8];
+    load8(w + c, wf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = rstd * (wf[i] * g[k][i] - hv[k][i] * rstd * dot);
+    if (dres != nullptr) {
+      float r[8];
+      load8(dres + off + c, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += r[i];
+    }
+    store8(dx + off + c, o);
+  }
+}
+
 __global__ void rmsnorm_bwd_dw_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ h,
                                       const float* __restrict__ rstd_in, float* __restrict__ partial, int rows, int H,
                                       int rows_per_split, int accumulate) {
@@ -421,12 +508,27 @@ std::vector<torch::Tensor> rmsnorm_fwd(const torch::Tensor& x, const c10::option
     rp = reinterpret_cast<const __nv_bfloat16*>(res->data_ptr());
   }
   const int threads = 256, per = threads / 32;
-  mvp::rmsnorm_fwd_kernel<<<(rows + per - 1) / per, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rp, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
-      h.defined() ? reinterpret_cast<__nv_bfloat16*>(h.data_ptr()) : nullptr, rstd.data_ptr<float>(), rows, H,
-      static_cast<float>(eps));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  auto* hp = h.defined() ? reinterpret_cast<__nv_bfloat16*>(h.data_ptr()) : nullptr;
+  auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto fwd_rows = [&](auto kern) {
+    kern<<<rows, 128, 0, stream>>>(xp, rp, wp, yp, hp, rstd.data_ptr<float>(), H, static_cast<float>(eps));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  };
+  if (rows == 0) {
+  } else if (H == 4096) {
+    fwd_rows(mvp::rmsnorm_fwd_row_kernel<4>);
+  } else if (H == 5120) {
+    fwd_rows(mvp::rmsnorm_fwd_row_kernel<5>);
+  } else if (H == 2048) {
+    fwd_rows(mvp::rmsnorm_fwd_row_kernel<2>);
+  } else {
+    mvp::rmsnorm_fwd_kernel<<<(rows + per - 1) / per, threads, 0, stream>>>(xp, rp, wp, yp, hp, rstd.data_ptr<float>(),
+                                                                          rows, H, static_cast<float>(eps));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   if (h.defined()) return {y, rstd, h};
   return {y, rstd};
 }
@@ -448,11 +550,26 @@ std::vector<torch::Tensor> rmsnorm_bwd(const torch::Tensor& dy, const torch::Ten
     dr = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
   }
   const int threads = 256, per = threads / 32;
-  mvp::rmsnorm_bwd_dx_kernel<<<(rows + per - 1) / per, threads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()),
-      rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), dr,
-      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), rows, H);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto* dyp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  auto* hp = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
+  auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto* dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  auto bwd_rows = [&](auto kern) {
+    kern<<<rows, 128, 0, stream>>>(dyp, hp, rstd.data_ptr<float>(), wp, dr, dxp, H);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  };
+  if (rows == 0) {
+  } else if (H == 4096) {
+    bwd_rows(mvp::rmsnorm_bwd_dx_row_kernel<4>);
+  } else if (H == 5120) {
+    bwd_rows(mvp::rmsnorm_bwd_dx_row_kernel<5>);
+  } else if (H == 2048) {
+    bwd_rows(mvp::rmsnorm_bwd_dx_row_kernel<2>);
+  } else {
+    mvp::rmsnorm_bwd_dx_kernel<<<(rows + per - 1) / per, threads, 0, stream>>>(dyp, hp, rstd.data_ptr<float>(), wp, dr,
+                                                                             dxp, rows, H);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   if (!need_dw) return {dx};
   const int splits = std::max(1, std::min(64, rows / 64));
   const int rows_per_split = (rows + splits - 1) / splits;
