@@ -357,8 +357,11 @@ def run_ours(args) -> None:
         "scaling": "weak" if cp == 1 and "global_batch" not in wl else "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": f"synthetic: uniform token ids over 151936, document lengths U[{lo},{hi}] packed to "
-                f"{args.seq_len} tokens (causal mask per document); random-init {wl['model_name']} weights",
+        "data": (f"synthetic: 1-4 images per sample, sides multiples of 32 in [{lo},{hi}] px, N(0,1) pixels, "
+                 f"interleaved with uniform-random text tokens, packed to {args.seq_len} tokens, loss on text "
+                 f"positions; random-init {wl['model_name']} weights" if recipe == "qwen3_vl" else
+                 f"synthetic: uniform token ids over 151936, document lengths U[{lo},{hi}] packed to "
+                 f"{args.seq_len} tokens (causal mask per document); random-init {wl['model_name']} weights"),
         "config": {"model": wl["model_name"], "global_batch": global_batch, "seq_len": args.seq_len,
                    "parallelism": (f"fsdp{world}" if cp == 1 and tp == 1 else
                                    f"cp{cp}-{wl['cp']}" if cp > 1 else f"tp{tp}-sp x fsdp{dp}"),
