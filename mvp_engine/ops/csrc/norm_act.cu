@@ -434,48 +434,41 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
 
 // ------------------------------------------------------------------ SwiGLU
 // gu = [T, 2F] with gate in columns [0, F) and up in [F, 2F); out = silu(g)*u.
+// One thread per 8 columns of one row (grid.x = row, grid.y = column block): no index division, 16-byte accesses, the
+// sigmoid through the fast exp / divide intrinsics.
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int64_t T,
                                   int F) {
-  const int64_t n8 = T * F / 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e = i * 8;
-    const int64_t t = e / F;
-    const int c = static_cast<int>(e % F);
-    float g[8], u[8], o[8];
-    load8(gu + t * 2 * F + c, g);
-    load8(gu + t * 2 * F + F + c, u);
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  const int64_t t = blockIdx.x;
+  if (c >= F) return;
+  float g[8], u[8], o[8];
+  load8(gu + t * 2 * F + c, g);
+  load8(gu + t * 2 * F + F + c, u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float s = g[j] / (1.f + __expf(-g[j]));
-      o[j] = bf16r(s) * u[j];
-    }
-    store8(out + e, o);
+  for (int j = 0; j < 8; ++j) {
+    const float s = __fdividef(g[j], 1.f + __expf(-g[j]));
+    o[j] = bf16r(s) * u[j];
   }
+  store8(out + t * F + c, o);
 }
-
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dout,
                                   __nv_bfloat16* __restrict__ dgu, int64_t T, int F) {
-  const int64_t n8 = T * F / 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e = i * 8;
-    const int64_t t = e / F;
-    const int c = static_cast<int>(e % F);
-    float g[8], u[8], d[8], dg[8], du[8];
-    load8(gu + t * 2 * F + c, g);
-    load8(gu + t * 2 * F + F + c, u);
-    load8(dout + e, d);
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  const int64_t t = blockIdx.x;
+  if (c >= F) return;
+  float g[8], u[8], d[8], dg[8], du[8];
+  load8(gu + t * 2 * F + c, g);
+  load8(gu + t * 2 * F + F + c, u);
+  load8(dout + t * F + c, d);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float sig = 1.f / (1.f + __expf(-g[j]));
-      const float s = g[j] * sig;
-      du[j] = d[j] * bf16r(s);
-      dg[j] = d[j] * u[j] * sig * (1.f + g[j] * (1.f - sig));
-    }
-    store8(dgu + t * 2 * F + c, dg);
-    store8(dgu + t * 2 * F + F + c, du);
+  for (int j = 0; j < 8; ++j) {
+    const float sig = __fdividef(1.f, 1.f + __expf(-g[j]));
+    const float s = g[j] * sig;
+    du[j] = d[j] * bf16r(s);
+    dg[j] = d[j] * u[j] * sig * (1.f + g[j] * (1.f - sig));
   }
+  store8(dgu + t * 2 * F + c, dg);
+  store8(dgu + t * 2 * F + F + c, du);
 }
 
 inline int grid_for(int64_t n, int threads) {
@@ -696,7 +689,10 @@ torch::Tensor swiglu_fwd(const torch::Tensor& gu) {
   TORCH_CHECK(F % 8 == 0, "swiglu: F must be a multiple of 8");
   const at::cuda::CUDAGuard guard(gu.device());
   auto out = torch::empty({T, F}, gu.options());
-  mvp::swiglu_fwd_kernel<<<grid_for(T * F / 8, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  if (T == 0) return out;
+  TORCH_CHECK(T <= 0x7fffffff && (F / 8 + 255) / 256 <= 65535, "swiglu: shape beyond the launch grid");
+  mvp::swiglu_fwd_kernel<<<dim3(static_cast<unsigned>(T), (F / 8 + 255) / 256), 256, 0,
+                           at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, F);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
@@ -709,7 +705,10 @@ torch::Tensor swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& dout) {
   const int F = static_cast<int>(gu.size(1) / 2);
   const at::cuda::CUDAGuard guard(gu.device());
   auto dgu = torch::empty_like(gu);
-  mvp::swiglu_bwd_kernel<<<grid_for(T * F / 8, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  if (T == 0) return dgu;
+  TORCH_CHECK(F % 8 == 0 && T <= 0x7fffffff && (F / 8 + 255) / 256 <= 65535, "swiglu: shape beyond the launch grid");
+  mvp::swiglu_bwd_kernel<<<dim3(static_cast<unsigned>(T), (F / 8 + 255) / 256), 256, 0,
+                           at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), T, F);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
