@@ -59,7 +59,7 @@ WORKLOADS = {
                                 metric="tokens/s (Qwen3-8B, 131072-token packed sequences, Ulysses context "
                                        "parallel; whole job)", model_name="Qwen3-8B"),
     "qwen3-vl-8b": dict(model="Qwen/Qwen3-VL-8B-Instruct", seq=16384, seqs_per_dp=4, docs=(448, 1344),
-                        recipe="qwen3_vl", config="recipes/qwen3_vl/configs/train.yaml",
+                        recipe="qwen3_vl", config="recipes/qwen3_vl/configs/train.yaml", reserve_gb=12,
                         metric="tokens/s (Qwen3-VL-8B SFT, 16384-token packs of 1-4 images + text; whole job)",
                         model_name="Qwen3-VL-8B"),
     "qwen3-32b-tp": dict(model="Qwen/Qwen3-32B", seq=4096, global_batch=32, docs=(256, 4096), tp=8, ckpt_all=True,
@@ -243,7 +243,9 @@ def run_ours(args) -> None:
     per_layer = local_tokens * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
                                     cfgm.head_dim + 2 * F) * 1.1
     head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
-    budget = free - head_ws - (10 << 30)
+    # 10 GiB of slack; the multimodal workload also keeps the vision tower's per-block checkpoint inputs,
+    # the image embeddings and a block's recomputed activations, which vary with the images of a pack
+    budget = free - head_ws - (10 << 30) - int(wl.get("reserve_gb", 0)) * (1 << 30)
     keep = max(0, min(L, int(budget // per_layer)))
     ckpt_layers = L - keep if args.ckpt_layers < 0 else args.ckpt_layers
     if wl.get("ckpt_all") and args.ckpt_layers < 0:  # long sequences / activation checkpointing on by config

@@ -131,7 +131,15 @@ def _linear(x: torch.Tensor, lin: nn.Linear) -> torch.Tensor:
 
 
 def _ln(x: torch.Tensor, ln: nn.LayerNorm) -> torch.Tensor:
-    return F.layer_norm(x, ln.normalized_shape, _as_compute(ln.weight, x), _as_compute(ln.bias, x), ln.eps)
+    """LayerNorm with bias: the sm_100a kernel pair on CUDA bf16, ``F.layer_norm`` elsewhere."""
+    return ops.layer_norm(x, _as_compute(ln.weight, x), _as_compute(ln.bias, x), ln.eps)
+
+
+def _linear_gelu(x: torch.Tensor, lin: nn.Linear, approximate: str) -> torch.Tensor:
+    """``gelu(x @ W^T + b)``: GEMM without bias, then one fused bias + GELU kernel on CUDA bf16."""
+    if x.is_cuda and x.dtype == torch.bfloat16 and lin.bias is not None:
+        return ops.bias_gelu(ops.linear(x, _as_compute(lin.weight, x)), _as_compute(lin.bias, x), approximate)
+    return F.gelu(_linear(x, lin), approximate=approximate)
 
 
 def linear_fp32_accurate(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor]) -> torch.Tensor:
@@ -174,10 +182,6 @@ class _SplitLinear(torch.autograd.Function):
         return dx, dw, db
 
 
-def _gelu_tanh(x: torch.Tensor) -> torch.Tensor:
-    return F.gelu(x, approximate="tanh")
-
-
 # ---------------------------------------------------------------- vision tower
 class Qwen3VLVisionPatchEmbed(nn.Module):
     def __init__(self, c: Qwen3VLVisionConfig):
@@ -198,7 +202,7 @@ class Qwen3VLVisionMLP(nn.Module):
         self.linear_fc2 = nn.Linear(c.intermediate_size, c.hidden_size, bias=True)
 
     def forward(self, x):
-        return _linear(_gelu_tanh(_linear(x, self.linear_fc1)), self.linear_fc2)
+        return _linear(_linear_gelu(x, self.linear_fc1, "tanh"), self.linear_fc2)
 
 
 class Qwen3VLVisionAttention(nn.Module):
@@ -210,12 +214,21 @@ class Qwen3VLVisionAttention(nn.Module):
         self.proj = nn.Linear(c.hidden_size, c.hidden_size, bias=True)
 
     def forward(self, x: torch.Tensor, cu: torch.Tensor, max_len: int, cos: torch.Tensor, sin: torch.Tensor):
+        """``cos`` / ``sin``: ``[N, head_dim / 2]`` fp32 of the rotary angles (both halves share them)."""
         N = x.shape[0]
-        qkv = _linear(x, self.qkv).view(N, 3, self.num_heads, self.head_dim)
-        q, k, v = qkv.unbind(1)
+        D = self.head_dim
+        qkv = _linear(x, self.qkv)
+        if qkv.is_cuda and qkv.dtype == torch.bfloat16 and D <= 128:
+            # RoPE kernel writes q / k / v zero-padded to the head_dim-128 attention layout directly
+            q, k, v = ops.vision_rope_pad(qkv, self.num_heads, cos, sin, 128)
+            o = flash_attn_varlen(q, k, v, cu, max_len, causal=False, softmax_scale=D**-0.5)[..., :D]
+            return _linear(o.reshape(N, -1), self.proj)
+        q, k, v = qkv.view(N, 3, self.num_heads, D).unbind(1)
+        c = torch.cat([cos, cos], -1).unsqueeze(1)
+        s = torch.cat([sin, sin], -1).unsqueeze(1)
         qf, kf = q.float(), k.float()
-        q = (qf * cos + _rotate_half(qf) * sin).to(x.dtype)
-        k = (kf * cos + _rotate_half(kf) * sin).to(x.dtype)
+        q = (qf * c + _rotate_half(qf) * s).to(x.dtype)
+        k = (kf * c + _rotate_half(kf) * s).to(x.dtype)
         o = vision_attention(q, k, v, cu, max_len)
         return _linear(o.reshape(N, -1), self.proj)
 
@@ -255,7 +268,7 @@ class Qwen3VLVisionPatchMerger(nn.Module):
     def forward(self, x):
         x = _ln(x.reshape(-1, self.hidden_size), self.norm) if self.use_postshuffle_norm else \
             _ln(x, self.norm).reshape(-1, self.hidden_size)
-        return _linear(F.gelu(_linear(x, self.linear_fc1)), self.linear_fc2)
+        return _linear(_linear_gelu(x, self.linear_fc1, "none"), self.linear_fc2)
 
 
 class Qwen3VLVisionModel(nn.Module):
@@ -292,9 +305,8 @@ class Qwen3VLVisionModel(nn.Module):
         pos = (F.embedding(meta["pos_idx"], _as_compute(pe, x)) * meta["pos_w"].unsqueeze(-1).to(x.dtype)).sum(0)
         x = (x + pos).to(dtype)
         ang = meta["rope_angles"]
-        emb = torch.cat([ang, ang], dim=-1)
-        cos = emb.cos().unsqueeze(1)
-        sin = emb.sin().unsqueeze(1)
+        cos = ang.cos()
+        sin = ang.sin()
         cu, max_len = meta["cu_seqlens"], int(meta["max_len"])
         deep = []
         for i, blk in enumerate(self.blocks):

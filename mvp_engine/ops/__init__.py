@@ -39,6 +39,9 @@ __all__ = [
     "fused_linear_cross_entropy",
     "adamw_step_",
     "sumsq",
+    "layer_norm",
+    "bias_gelu",
+    "vision_rope_pad",
 ]
 
 
@@ -567,6 +570,129 @@ def adamw_step_(
     _ext.ext().adamw_step_(
         p, g, m, v, p_bf16, lr, beta1, beta2, eps, weight_decay, int(step), grad_scale, norm_sq, max_norm
     )
+
+
+# ------------------------------------------------- vision tower (LayerNorm, bias + GELU, RoPE)
+def _acc_of(t: torch.Tensor, acc: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """``acc`` if the kernel can add into it directly (contiguous fp32 of ``t``'s size)."""
+    if acc is not None and acc.is_contiguous() and acc.dtype == torch.float32 and acc.numel() == t.numel():
+        return acc
+    return None
+
+
+def _param_grad(g32: torch.Tensor, p: torch.Tensor, acc: Optional[torch.Tensor], added: bool):
+    """Route an fp32 parameter gradient: already added by the kernel, added here, or returned."""
+    if added:
+        return None
+    if acc is not None:
+        acc.add_(g32.view_as(acc))
+        return None
+    return g32.view_as(p).to(p.dtype)
+
+
+class _LayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y, mean, rstd = _ext.ext().layernorm_fwd(x2, w.contiguous(), b.contiguous(), eps)
+        ctx.save_for_backward(x2, mean, rstd, w)
+        ctx.acc = (grad_acc(w), grad_acc(b))
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, mean, rstd, w = ctx.saved_tensors
+        aw, ab = ctx.acc
+        kw, kb = _acc_of(w, aw), _acc_of(w, ab)
+        dx, dw, db = _ext.ext().layernorm_bwd(dy.reshape(x2.shape).contiguous(), x2, mean, rstd, w.contiguous(),
+                                              dw_acc=kw, db_acc=kb)
+        return (dx.view(ctx.shape), _param_grad(dw, w, aw, kw is not None), _param_grad(db, w, ab, kb is not None),
+                None)
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -> torch.Tensor:
+    """LayerNorm over the last dimension with weight and bias (fp32 statistics, one bf16 rounding).
+
+    On CUDA bf16 input it runs the sm_100a kernel pair; elsewhere ``F.layer_norm``.
+    """
+    if not _native(x) or x.dtype != torch.bfloat16:
+        return F.layer_norm(x, (x.shape[-1],), w.to(x.dtype), b.to(x.dtype), eps)
+    return _LayerNorm.apply(x, w.to(x.dtype), b.to(x.dtype), float(eps))
+
+
+class _BiasGelu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, b, tanh_form):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y = _ext.ext().bias_gelu_fwd(x2, b.contiguous(), tanh_form)
+        ctx.save_for_backward(x2, b)
+        ctx.acc = grad_acc(b)
+        ctx.tanh_form = tanh_form
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, b = ctx.saved_tensors
+        kb = _acc_of(b, ctx.acc)
+        dx, db = _ext.ext().bias_gelu_bwd(dy.reshape(x2.shape).contiguous(), x2, b.contiguous(), ctx.tanh_form,
+                                          db_acc=kb)
+        return dx.view(ctx.shape), _param_grad(db, b, ctx.acc, kb is not None), None
+
+
+def bias_gelu(x: torch.Tensor, b: torch.Tensor, approximate: str = "none") -> torch.Tensor:
+    """``gelu(x + b)`` with ``approximate`` "tanh" or "none" (erf), the bias add rounded as eager rounds it."""
+    if approximate not in ("none", "tanh"):
+        raise ValueError(f"bias_gelu: approximate must be 'none' or 'tanh', got {approximate!r}")
+    if not _native(x) or x.dtype != torch.bfloat16:
+        return F.gelu(x + b.to(x.dtype), approximate=approximate)
+    return _BiasGelu.apply(x, b.to(x.dtype), approximate == "tanh")
+
+
+class _VisionRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv2, nh, cos, sin, pad_to):
+        q, k, v = _ext.ext().vision_rope_fwd(qkv2, nh, cos, sin, pad_to)
+        ctx.save_for_backward(cos, sin)
+        ctx.D = qkv2.shape[1] // (3 * nh)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos, sin = ctx.saved_tensors
+        dq, dk, dv = (t.contiguous() if t is not None else None for t in (dq, dk, dv))
+        zero = next(t for t in (dq, dk, dv) if t is not None)
+        dq, dk, dv = (t if t is not None else torch.zeros_like(zero) for t in (dq, dk, dv))
+        return _ext.ext().vision_rope_bwd(dq, dk, dv, cos, sin, ctx.D), None, None, None, None
+
+
+def vision_rope_pad(qkv: torch.Tensor, nh: int, cos: torch.Tensor, sin: torch.Tensor,
+                    pad_to: int = 128) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rotate-half RoPE of the vision tower applied to q and k of a fused ``qkv`` ``[N, 3 * nh * D]``.
+
+    ``cos`` / ``sin`` are ``[N, D / 2]`` fp32 (the rotary angles' cos / sin; each is used for both halves).
+    Returns ``q, k, v`` as ``[N, nh, pad_to]`` with columns ``D..pad_to-1`` zero, the layout the
+    head_dim-128 attention kernel takes (zero columns leave QK^T and the output's first D columns exact).
+    The rotation is computed in fp32 and rounded to the activation dtype once.
+    """
+    N = qkv.shape[0]
+    D = qkv.shape[-1] // (3 * nh)
+    if not _native(qkv) or qkv.dtype != torch.bfloat16:
+        t = qkv.view(N, 3, nh, D)
+        c = torch.cat([cos, cos], -1).unsqueeze(1)
+        s = torch.cat([sin, sin], -1).unsqueeze(1)
+        out = []
+        for i in range(2):
+            xf = t[:, i].float()
+            a, bb = xf.chunk(2, dim=-1)
+            out.append((xf * c + torch.cat((-bb, a), -1) * s).to(qkv.dtype))
+        out.append(t[:, 2])
+        return tuple(F.pad(o, (0, pad_to - D)) for o in out)
+    return _VisionRope.apply(qkv.reshape(N, -1).contiguous(), int(nh), cos.float().contiguous(),
+                             sin.float().contiguous(), int(pad_to))
 
 
 def sumsq(x: torch.Tensor) -> torch.Tensor:

@@ -78,6 +78,20 @@ void gemm_pair_tp(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, con
                   const std::vector<int64_t>& dst, int64_t dst_rows, int64_t dst_row0, int64_t status_ptr,
                   int64_t wait_ns);
 
+std::vector<torch::Tensor> layernorm_fwd(const torch::Tensor& x, const torch::Tensor& w, const torch::Tensor& b,
+                                         double eps);
+std::vector<torch::Tensor> layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& mean,
+                                         const torch::Tensor& rstd, const torch::Tensor& w,
+                                         const c10::optional<torch::Tensor>& dw_acc,
+                                         const c10::optional<torch::Tensor>& db_acc);
+torch::Tensor bias_gelu_fwd(const torch::Tensor& x, const torch::Tensor& b, bool tanh_form);
+std::vector<torch::Tensor> bias_gelu_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& b,
+                                         bool tanh_form, const c10::optional<torch::Tensor>& db_acc);
+std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh, const torch::Tensor& cosv,
+                                           const torch::Tensor& sinv, int64_t DP);
+torch::Tensor vision_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const torch::Tensor& dv,
+                              const torch::Tensor& cosv, const torch::Tensor& sinv, int64_t D);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mvp_engine sm_100a kernels";
   m.def("gemm", &gemm_sm100, "tcgen05 bf16 GEMM C (+)= A * B^T with K- or MN-major operands");
@@ -91,6 +105,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dwq_acc") = py::none(), py::arg("dwk_acc") = py::none());
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("layernorm_fwd", &layernorm_fwd, "LayerNorm with bias (vision tower)");
+  m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"), py::arg("w"),
+        py::arg("dw_acc") = py::none(), py::arg("db_acc") = py::none());
+  m.def("bias_gelu_fwd", &bias_gelu_fwd, "y = gelu(x + b), tanh or erf form");
+  m.def("bias_gelu_bwd", &bias_gelu_bwd, py::arg("dy"), py::arg("x"), py::arg("b"), py::arg("tanh_form"),
+        py::arg("db_acc") = py::none());
+  m.def("vision_rope_fwd", &vision_rope_fwd, "rotate-half RoPE of q / k, q / k / v padded to DP columns");
+  m.def("vision_rope_bwd", &vision_rope_bwd, "inverse rotation of dq / dk, written with dv into dqkv");
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd_", &ce_bwd_);
   m.def("adamw_step_", &adamw_step_);

@@ -4,6 +4,7 @@ Usage::
 
     python -m mvp_engine.ops.microbench gemm            # Qwen3-8B layer shapes, ours vs cuBLAS
     python -m mvp_engine.ops.microbench gemm --shape 8192,24576,4096 --iters 20
+    python -m mvp_engine.ops.microbench vision          # Qwen3-VL ViT LayerNorm / bias+GELU / RoPE
     torchrun --nproc-per-node 2 -m mvp_engine.ops.microbench cp_attention --tokens 131072
 
 Prints one JSON line per case with the kernel time and achieved TFLOP/s.
@@ -410,9 +411,86 @@ def bench_cp_layer(tokens: int, iters: int, impls: list[str]) -> None:
     dist.destroy_process_group()
 
 
+def bench_vision(tokens: int, iters: int) -> None:
+    """Vision-tower kernels on Qwen3-VL ViT shapes (hidden 1152, MLP 4304, 16 heads of 72), ours vs eager.
+
+    ``tokens`` patches (28224 = four 1344x1344 images).  Bytes are the algorithmic HBM traffic of each op.
+    """
+    from mvp_engine import ops
+
+    H, Fd, nh, D = 1152, 4304, 16, 72
+    N = tokens
+    x = torch.randn(N, H, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    b = (0.1 * torch.randn(H, device="cuda")).bfloat16()
+    h = torch.randn(N, Fd, device="cuda").bfloat16()
+    bf = (0.1 * torch.randn(Fd, device="cuda")).bfloat16()
+    qkv = torch.randn(N, 3 * H, device="cuda").bfloat16()
+    ang = torch.rand(N, D // 2, device="cuda") * 30
+    cos, sin = ang.cos(), ang.sin()
+    e = _ext_mod()
+    y, mean, rstd = e.layernorm_fwd(x, w, b, 1e-6)
+    dq = torch.randn(N, nh, 128, device="cuda").bfloat16()
+
+    def eager_rope():
+        t = qkv.view(N, 3, nh, D)
+        c = torch.cat([cos, cos], -1).unsqueeze(1)
+        sn = torch.cat([sin, sin], -1).unsqueeze(1)
+        out = []
+        for i in range(2):
+            xf = t[:, i].float()
+            a, bb = xf.chunk(2, dim=-1)
+            out.append((xf * c + torch.cat((-bb, a), -1) * sn).to(qkv.dtype))
+        out.append(t[:, 2])
+        return [torch.nn.functional.pad(o, (0, 128 - D)) for o in out]
+
+    cases = {
+        # name: (ours, eager, algorithmic bytes)
+        "layernorm_fwd": (lambda: e.layernorm_fwd(x, w, b, 1e-6),
+                          lambda: torch.nn.functional.layer_norm(x, (H,), w, b, 1e-6), 2 * N * H * 2 + N * 8),
+        "layernorm_bwd": (lambda: e.layernorm_bwd(y, x, mean, rstd, w),
+                          None, 3 * N * H * 2 + N * 8),
+        "bias_gelu_fwd_tanh": (lambda: e.bias_gelu_fwd(h, bf, True),
+                               lambda: torch.nn.functional.gelu(h + bf, approximate="tanh"), 2 * N * Fd * 2),
+        "bias_gelu_bwd_tanh": (lambda: e.bias_gelu_bwd(h, h, bf, True), None, 3 * N * Fd * 2),
+        "vision_rope_fwd": (lambda: e.vision_rope_fwd(qkv, nh, cos, sin, 128), eager_rope,
+                            N * 3 * H * 2 + 3 * N * nh * 128 * 2 + 2 * N * (D // 2) * 4),
+        "vision_rope_bwd": (lambda: e.vision_rope_bwd(dq, dq, dq, cos, sin, D), None,
+                            3 * N * nh * 128 * 2 + N * 3 * H * 2 + 2 * N * (D // 2) * 4),
+    }
+    peak = _hbm_peak()
+    for name, (ours, eager, nbytes) in cases.items():
+        t = _time(ours, iters)
+        row = {"case": name, "tokens": N, "ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),
+               "frac_of_measured_hbm": round(nbytes / t / 1e6 / peak, 3) if peak else None}
+        if eager is not None and _WITH_REF:
+            te = _time(eager, iters)
+            row["eager_ms"] = round(te, 4)
+            row["speedup_vs_eager"] = round(te / t, 2)
+        print(json.dumps(row), flush=True)
+
+
+def _ext_mod():
+    from mvp_engine.ops import _ext
+
+    return _ext.ext()
+
+
+def _hbm_peak() -> float:
+    """Measured HBM copy bandwidth (GB/s) from the repository's peaks file, if present."""
+    import os
+
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 0.0
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer"])
+    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer", "vision"])
     ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
     ap.add_argument("--docs", default="256,4096", help="attention: document lengths U[lo, hi]")
     ap.add_argument("--hidden", type=int, default=5120, help="tp_gemm: hidden size (square weights)")
@@ -440,6 +518,8 @@ def main() -> None:
     elif args.what == "cp_attention":
         hq, hkv = (int(v) for v in args.heads.split(","))
         bench_cp_attention(args.tokens, hq, hkv, args.iters, args.impls.split(","))
+    elif args.what == "vision":
+        bench_vision(args.tokens if args.tokens != 8192 else 28224, args.iters)
     elif args.what == "attention":
         hq, hkv = (int(v) for v in args.heads.split(","))
         lo, hi = (int(v) for v in args.docs.split(","))

@@ -44,3 +44,24 @@ def test_forward_backward_and_image_scatter():
     assert model.model.visual.deepstack_merger_list[0].linear_fc2.weight.grad.abs().sum() > 0
     fl = model.calculate_model_flops(batch_size=1, seq_len=ids.shape[1], image_grid_thw=grid)
     assert fl > 0
+
+
+def test_vision_op_fallbacks_match_eager_math():
+    """CPU paths of the vision-tower ops (LayerNorm, bias + GELU, padded RoPE) equal the eager formulas."""
+    from mvp_engine import ops
+
+    torch.manual_seed(0)
+    N, nh, D = 7, 2, 8
+    qkv = torch.randn(N, 3 * nh * D)
+    ang = torch.rand(N, D // 2) * 10
+    q, k, v = ops.vision_rope_pad(qkv, nh, ang.cos(), ang.sin(), 16)
+    t = qkv.view(N, 3, nh, D)
+    c = torch.cat([ang.cos(), ang.cos()], -1).unsqueeze(1)
+    s = torch.cat([ang.sin(), ang.sin()], -1).unsqueeze(1)
+    rq = t[:, 0] * c + torch.cat((-t[:, 0, :, D // 2:], t[:, 0, :, :D // 2]), -1) * s
+    assert torch.allclose(q[..., :D], rq, atol=1e-6) and q[..., D:].abs().max() == 0
+    assert torch.equal(v[..., :D], t[:, 2])
+    x, b = torch.randn(5, 16), torch.randn(16)
+    assert torch.allclose(ops.bias_gelu(x, b, "tanh"), torch.nn.functional.gelu(x + b, approximate="tanh"))
+    w = torch.randn(16)
+    assert torch.allclose(ops.layer_norm(x, w, b, 1e-6), torch.nn.functional.layer_norm(x, (16,), w, b, 1e-6))
