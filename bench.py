@@ -380,7 +380,7 @@ def run_ours(args) -> None:
         "e2e": {"value": round(tokens_per_step / (e_ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(e_ms, 3),
                 "h2d_bytes_per_step": int(h2d_bytes),
                 "d2h_bytes_per_step": 8 * 2 + 4 * 1,
-                "api": "recipes.qwen3 Qwen3Engine.train_step(host micro-batches)"},
+                "api": f"recipes.{recipe} {EngineClass.__name__}.train_step(host micro-batches)"},
         "gpu_launches": int(launches),
         "loss_last": round(losses[-1], 4) if losses else None,
         "impl": "ours",

@@ -304,6 +304,94 @@ __global__ void __launch_bounds__(256) vision_rope_bwd_kernel(const __nv_bfloat1
   for (int i = lane; i < D; i += 32) ov[i] = dv[src + i];
 }
 
+// Row-vectorised RoPE for head dims that are multiples of 8 (64, 72): one thread per [q|k|v] row of one
+// (token, head), 16-byte loads and stores, the row held in registers.  Thread i handles the i-th row of qkv
+// in memory order ([N, 3, nh, D]), so neighbouring threads touch neighbouring rows.
+template <int D>
+__global__ void __launch_bounds__(128) vision_rope_fwd_vec_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                  const float* __restrict__ cosv,
+                                                                  const float* __restrict__ sinv,
+                                                                  __nv_bfloat16* __restrict__ qo,
+                                                                  __nv_bfloat16* __restrict__ ko,
+                                                                  __nv_bfloat16* __restrict__ vo, int64_t N, int nh,
+                                                                  int DP) {
+  constexpr int h = D / 2;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= N * 3 * nh) return;
+  const int64_t n = idx / (3 * nh);
+  const int rem = static_cast<int>(idx - n * 3 * nh);
+  const int t = rem / nh, hd = rem % nh;
+  float x[D];
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float f[8];
+    vload8(qkv + idx * D + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[c * 8 + i] = f[i];
+  }
+  if (t < 2) {
+    const float* cr = cosv + n * h;
+    const float* sr = sinv + n * h;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float c = cr[i], sn = sr[i], a = x[i], b = x[i + h];
+      x[i] = a * c - b * sn;
+      x[i + h] = b * c + a * sn;
+    }
+  }
+  __nv_bfloat16* o = (t == 0 ? qo : (t == 1 ? ko : vo)) + (n * nh + hd) * DP;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = x[c * 8 + i];
+    vstore8(o + c * 8, f);
+  }
+  for (int c = D; c < DP; c += 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) vision_rope_bwd_vec_kernel(const __nv_bfloat16* __restrict__ dq,
+                                                                  const __nv_bfloat16* __restrict__ dk,
+                                                                  const __nv_bfloat16* __restrict__ dv,
+                                                                  const float* __restrict__ cosv,
+                                                                  const float* __restrict__ sinv,
+                                                                  __nv_bfloat16* __restrict__ dqkv, int64_t N, int nh,
+                                                                  int DP) {
+  constexpr int h = D / 2;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= N * 3 * nh) return;
+  const int64_t n = idx / (3 * nh);
+  const int rem = static_cast<int>(idx - n * 3 * nh);
+  const int t = rem / nh, hd = rem % nh;
+  const __nv_bfloat16* src = (t == 0 ? dq : (t == 1 ? dk : dv)) + (n * nh + hd) * DP;
+  float x[D];
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float f[8];
+    vload8(src + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[c * 8 + i] = f[i];
+  }
+  if (t < 2) {
+    const float* cr = cosv + n * h;
+    const float* sr = sinv + n * h;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float c = cr[i], sn = sr[i], a = x[i], b = x[i + h];
+      x[i] = a * c + b * sn;
+      x[i + h] = b * c - a * sn;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = x[c * 8 + i];
+    vstore8(dqkv + idx * D + c * 8, f);
+  }
+}
+
 void check_bf16_2d(const torch::Tensor& t, const char* what) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.is_contiguous(), what,
               ": expected a contiguous 2-D bf16 CUDA tensor");
@@ -486,8 +574,28 @@ std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh,
   auto q = torch::empty({N, nh, DP}, qkv.options());
   auto k = torch::empty_like(q);
   auto v = torch::empty_like(q);
+  if (N == 0) return {q, k, v};
+  const bool vec = DP % 8 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0;
+  if (vec && (D == 64 || D == 72)) {
+    const int64_t rows = N * 3 * nh;
+    TORCH_CHECK((rows + 127) / 128 <= 0x7fffffff, "vision_rope_fwd: too many rows");
+    const unsigned grid = static_cast<unsigned>((rows + 127) / 128);
+    const auto* src = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+    auto* qp = reinterpret_cast<__nv_bfloat16*>(q.data_ptr());
+    auto* kp = reinterpret_cast<__nv_bfloat16*>(k.data_ptr());
+    auto* vp = reinterpret_cast<__nv_bfloat16*>(v.data_ptr());
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int nhi = static_cast<int>(nh), dpi = static_cast<int>(DP);
+    if (D == 64)
+      vision_rope_fwd_vec_kernel<64><<<grid, 128, 0, stream>>>(src, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
+                                                               qp, kp, vp, N, nhi, dpi);
+    else
+      vision_rope_fwd_vec_kernel<72><<<grid, 128, 0, stream>>>(src, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
+                                                               qp, kp, vp, N, nhi, dpi);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {q, k, v};
+  }
   const int64_t threads = N * nh * 32;
-  if (threads == 0) return {q, k, v};
   TORCH_CHECK((threads + 255) / 256 <= 0x7fffffff, "vision_rope_fwd: too many rows");
   vision_rope_fwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cosv.data_ptr<float>(), sinv.data_ptr<float>(),
@@ -510,8 +618,30 @@ torch::Tensor vision_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, 
   check_vec(sinv, N * (D / 2), at::kFloat, "vision_rope_bwd sin");
   const at::cuda::CUDAGuard guard(dq.device());
   auto dqkv = torch::empty({N, 3 * nh * D}, dq.options());
+  if (N == 0) return dqkv;
+  const bool vec = DP % 8 == 0 && reinterpret_cast<uintptr_t>(dq.data_ptr()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dk.data_ptr()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dv.data_ptr()) % 16 == 0;
+  if (vec && (D == 64 || D == 72)) {
+    const int64_t rows = N * 3 * nh;
+    TORCH_CHECK((rows + 127) / 128 <= 0x7fffffff, "vision_rope_bwd: too many rows");
+    const unsigned grid = static_cast<unsigned>((rows + 127) / 128);
+    const auto* a = reinterpret_cast<const __nv_bfloat16*>(dq.data_ptr());
+    const auto* b = reinterpret_cast<const __nv_bfloat16*>(dk.data_ptr());
+    const auto* c = reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr());
+    auto* o = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int nhi = static_cast<int>(nh), dpi = static_cast<int>(DP);
+    if (D == 64)
+      vision_rope_bwd_vec_kernel<64><<<grid, 128, 0, stream>>>(a, b, c, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
+                                                               o, N, nhi, dpi);
+    else
+      vision_rope_bwd_vec_kernel<72><<<grid, 128, 0, stream>>>(a, b, c, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
+                                                               o, N, nhi, dpi);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return dqkv;
+  }
   const int64_t threads = N * nh * 32;
-  if (threads == 0) return dqkv;
   vision_rope_bwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dk.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()), cosv.data_ptr<float>(), sinv.data_ptr<float>(),

@@ -81,7 +81,7 @@ def test_bias_gelu(approximate, rows, Fd):
 
 
 @cuda
-@pytest.mark.parametrize("N,nh,D", [(1, 16, 72), (1000, 16, 72), (300, 3, 64)])
+@pytest.mark.parametrize("N,nh,D", [(1, 16, 72), (1000, 16, 72), (300, 3, 64), (50, 4, 32)])
 def test_vision_rope_pad(N, nh, D):
     ops = _ops()
     torch.manual_seed(0)
