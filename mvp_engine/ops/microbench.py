@@ -430,7 +430,10 @@ def bench_vision(tokens: int, iters: int) -> None:
     cos, sin = ang.cos(), ang.sin()
     e = _ext_mod()
     y, mean, rstd = e.layernorm_fwd(x, w, b, 1e-6)
-    dq = torch.randn(N, nh, 128, device="cuda").bfloat16()
+    # distinct gradient tensors: aliased inputs would be served from L2 and overstate the bandwidth
+    dy = torch.randn(N, H, device="cuda").bfloat16()
+    dh = torch.randn(N, Fd, device="cuda").bfloat16()
+    dq, dk, dv = (torch.randn(N, nh, 128, device="cuda").bfloat16() for _ in range(3))
 
     def eager_rope():
         t = qkv.view(N, 3, nh, D)
@@ -448,15 +451,16 @@ def bench_vision(tokens: int, iters: int) -> None:
         # name: (ours, eager, algorithmic bytes)
         "layernorm_fwd": (lambda: e.layernorm_fwd(x, w, b, 1e-6),
                           lambda: torch.nn.functional.layer_norm(x, (H,), w, b, 1e-6), 2 * N * H * 2 + N * 8),
-        "layernorm_bwd": (lambda: e.layernorm_bwd(y, x, mean, rstd, w),
+        "layernorm_bwd": (lambda: e.layernorm_bwd(dy, x, mean, rstd, w),
                           None, 3 * N * H * 2 + N * 8),
         "bias_gelu_fwd_tanh": (lambda: e.bias_gelu_fwd(h, bf, True),
                                lambda: torch.nn.functional.gelu(h + bf, approximate="tanh"), 2 * N * Fd * 2),
-        "bias_gelu_bwd_tanh": (lambda: e.bias_gelu_bwd(h, h, bf, True), None, 3 * N * Fd * 2),
+        "bias_gelu_bwd_tanh": (lambda: e.bias_gelu_bwd(dh, h, bf, True), None, 3 * N * Fd * 2),
         "vision_rope_fwd": (lambda: e.vision_rope_fwd(qkv, nh, cos, sin, 128), eager_rope,
                             N * 3 * H * 2 + 3 * N * nh * 128 * 2 + 2 * N * (D // 2) * 4),
-        "vision_rope_bwd": (lambda: e.vision_rope_bwd(dq, dq, dq, cos, sin, D), None,
-                            3 * N * nh * 128 * 2 + N * 3 * H * 2 + 2 * N * (D // 2) * 4),
+        # reads the first D columns of each padded gradient row, writes dqkv
+        "vision_rope_bwd": (lambda: e.vision_rope_bwd(dq, dk, dv, cos, sin, D), None,
+                            3 * N * nh * D * 2 + N * 3 * H * 2 + 2 * N * (D // 2) * 4),
     }
     peak = _hbm_peak()
     for name, (ours, eager, nbytes) in cases.items():
