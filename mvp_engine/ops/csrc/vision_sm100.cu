@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(
     const __nv_bfloat16* gr = dy + static_cast<int64_t>(row) * H;
     const float mean = mean_in[row], rstd = rstd_in[row];
     float sg = 0.f, sgx = 0.f;
+#pragma unroll 4
     for (int v = lane; v < nv; v += 32) {
       float f[8], g[8], wf[8];
       vload8(xr + v * 8, f);
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(
     }
     const float mg = vwarp_sum(sg) / H, mgx = vwarp_sum(sgx) / H;
     __nv_bfloat16* dxr = dx + static_cast<int64_t>(row) * H;
+#pragma unroll 4
     for (int v = lane; v < nv; v += 32) {
       float f[8], g[8], wf[8], o[8];
       vload8(xr + v * 8, f);
