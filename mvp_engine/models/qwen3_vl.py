@@ -135,6 +135,13 @@ def _ln(x: torch.Tensor, ln: nn.LayerNorm) -> torch.Tensor:
     return ops.layer_norm(x, _as_compute(ln.weight, x), _as_compute(ln.bias, x), ln.eps)
 
 
+def _linear_residual(x: torch.Tensor, lin: nn.Linear, residual: torch.Tensor) -> torch.Tensor:
+    """``residual + (x @ W^T + b)``: GEMM without bias, then one fused bias + residual kernel on CUDA bf16."""
+    if x.is_cuda and x.dtype == torch.bfloat16 and lin.bias is not None and residual.dtype == x.dtype:
+        return ops.bias_residual(ops.linear(x, _as_compute(lin.weight, x)), _as_compute(lin.bias, x), residual)
+    return residual + _linear(x, lin)
+
+
 def _linear_gelu(x: torch.Tensor, lin: nn.Linear, approximate: str) -> torch.Tensor:
     """``gelu(x @ W^T + b)``: GEMM without bias, then one fused bias + GELU kernel on CUDA bf16."""
     if x.is_cuda and x.dtype == torch.bfloat16 and lin.bias is not None:
@@ -201,8 +208,12 @@ class Qwen3VLVisionMLP(nn.Module):
         self.linear_fc1 = nn.Linear(c.hidden_size, c.intermediate_size, bias=True)
         self.linear_fc2 = nn.Linear(c.intermediate_size, c.hidden_size, bias=True)
 
-    def forward(self, x):
-        return _linear(_linear_gelu(x, self.linear_fc1, "tanh"), self.linear_fc2)
+    def forward(self, x, residual: Optional[torch.Tensor] = None):
+        """``fc2(gelu(fc1(x)))``; with ``residual``, returns ``residual + that`` (bias and residual adds fused)."""
+        h = _linear_gelu(x, self.linear_fc1, "tanh")
+        if residual is not None:
+            return _linear_residual(h, self.linear_fc2, residual)
+        return _linear(h, self.linear_fc2)
 
 
 class Qwen3VLVisionAttention(nn.Module):
@@ -213,8 +224,11 @@ class Qwen3VLVisionAttention(nn.Module):
         self.qkv = nn.Linear(c.hidden_size, 3 * c.hidden_size, bias=True)
         self.proj = nn.Linear(c.hidden_size, c.hidden_size, bias=True)
 
-    def forward(self, x: torch.Tensor, cu: torch.Tensor, max_len: int, cos: torch.Tensor, sin: torch.Tensor):
-        """``cos`` / ``sin``: ``[N, head_dim / 2]`` fp32 of the rotary angles (both halves share them)."""
+    def forward(self, x: torch.Tensor, cu: torch.Tensor, max_len: int, cos: torch.Tensor, sin: torch.Tensor,
+                residual: Optional[torch.Tensor] = None):
+        """``cos`` / ``sin``: ``[N, head_dim / 2]`` fp32 of the rotary angles (both halves share them).
+
+        With ``residual``, returns ``residual + attention output`` (bias and residual adds fused)."""
         N = x.shape[0]
         D = self.head_dim
         qkv = _linear(x, self.qkv)
@@ -222,6 +236,8 @@ class Qwen3VLVisionAttention(nn.Module):
             # RoPE kernel writes q / k / v zero-padded to the head_dim-128 attention layout directly
             q, k, v = ops.vision_rope_pad(qkv, self.num_heads, cos, sin, 128)
             o = flash_attn_varlen(q, k, v, cu, max_len, causal=False, softmax_scale=D**-0.5)[..., :D]
+            if residual is not None:
+                return _linear_residual(o.reshape(N, -1), self.proj, residual)
             return _linear(o.reshape(N, -1), self.proj)
         q, k, v = qkv.view(N, 3, self.num_heads, D).unbind(1)
         c = torch.cat([cos, cos], -1).unsqueeze(1)
@@ -230,7 +246,8 @@ class Qwen3VLVisionAttention(nn.Module):
         q = (qf * c + _rotate_half(qf) * s).to(x.dtype)
         k = (kf * c + _rotate_half(kf) * s).to(x.dtype)
         o = vision_attention(q, k, v, cu, max_len)
-        return _linear(o.reshape(N, -1), self.proj)
+        out = _linear(o.reshape(N, -1), self.proj)
+        return out if residual is None else residual + out
 
 
 def _rotate_half(x):
@@ -252,8 +269,8 @@ class Qwen3VLVisionBlock(nn.Module):
         self.mlp = Qwen3VLVisionMLP(c)
 
     def forward(self, x, cu, max_len, cos, sin):
-        x = x + self.attn(_ln(x, self.norm1), cu, max_len, cos, sin)
-        return x + self.mlp(_ln(x, self.norm2))
+        x = self.attn(_ln(x, self.norm1), cu, max_len, cos, sin, residual=x)
+        return self.mlp(_ln(x, self.norm2), residual=x)
 
 
 class Qwen3VLVisionPatchMerger(nn.Module):

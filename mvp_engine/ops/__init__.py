@@ -42,6 +42,7 @@ __all__ = [
     "layer_norm",
     "bias_gelu",
     "vision_rope_pad",
+    "bias_residual",
 ]
 
 
@@ -650,6 +651,35 @@ def bias_gelu(x: torch.Tensor, b: torch.Tensor, approximate: str = "none") -> to
     if not _native(x) or x.dtype != torch.bfloat16:
         return F.gelu(x + b.to(x.dtype), approximate=approximate)
     return _BiasGelu.apply(x, b.to(x.dtype), approximate == "tanh")
+
+
+class _BiasResidual(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, b, x):
+        shape = y.shape
+        out = _ext.ext().bias_residual_fwd(y.reshape(-1, shape[-1]).contiguous(), b.contiguous(),
+                                           x.reshape(-1, shape[-1]).contiguous())
+        ctx.save_for_backward(b)
+        ctx.acc = grad_acc(b)
+        return out.view(shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (b,) = ctx.saved_tensors
+        kb = _acc_of(b, ctx.acc)
+        db = _ext.ext().bias_grad(dout.reshape(-1, dout.shape[-1]).contiguous(), acc=kb)
+        return dout, _param_grad(db, b, ctx.acc, kb is not None), dout
+
+
+def bias_residual(y: torch.Tensor, b: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """``x + (y + b)``: a bias-free projection's bias add and the residual add in one pass on CUDA bf16.
+
+    Each add rounds to the activation dtype as the two eager adds do; the backward passes the gradient
+    through to ``x`` and ``y`` and sums it over rows for ``b`` (into ``b``'s fp32 accumulator when present).
+    """
+    if not _native(y) or y.dtype != torch.bfloat16:
+        return x + (y + b.to(y.dtype))
+    return _BiasResidual.apply(y, b.to(y.dtype), x)
 
 
 class _VisionRope(torch.autograd.Function):

@@ -241,6 +241,47 @@ __global__ void __launch_bounds__(128) bias_gelu_bwd_kernel(const __nv_bfloat16*
   for (int i = 0; i < 8; ++i) pr[i] = acc[i];
 }
 
+// ------------------------------------------------------ bias + residual add
+// out = bf16(x + bf16(y + b)): the projection's bias add and the residual add, rounded as the two eager
+// adds round.  grid as bias_gelu_fwd_kernel.
+__global__ void __launch_bounds__(128) bias_residual_fwd_kernel(const __nv_bfloat16* __restrict__ y,
+                                                                const __nv_bfloat16* __restrict__ b,
+                                                                const __nv_bfloat16* __restrict__ x,
+                                                                __nv_bfloat16* __restrict__ out, int rows, int F) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v * 8 >= F) return;
+  float bf[8];
+  vload8(b + v * 8, bf);
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int64_t off = static_cast<int64_t>(r) * F + v * 8;
+    float f[8], g[8];
+    vload8(y + off, f);
+    vload8(x + off, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = g[i] + rbf16(f[i] + bf[i]);
+    vstore8(out + off, f);
+  }
+}
+
+// Per-row-group column sums of a bf16 matrix (the bias gradient): part[blockIdx.y, F].
+__global__ void __launch_bounds__(128) col_partial_kernel(const __nv_bfloat16* __restrict__ g,
+                                                          float* __restrict__ part, int rows, int F) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v * 8 >= F) return;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    float f[8];
+    vload8(g + static_cast<int64_t>(r) * F + v * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += f[i];
+  }
+  float* pr = part + static_cast<int64_t>(blockIdx.y) * F + v * 8;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pr[i] = acc[i];
+}
+
 // ------------------------------------------------------------- vision RoPE
 // qkv: [N, 3, nh, D] bf16; cos / sin: [N, D/2] fp32.  One warp per (token, head).
 // q_out / k_out / v_out: [N, nh, DP] bf16 with columns D..DP-1 zero.
@@ -560,6 +601,55 @@ std::vector<torch::Tensor> bias_gelu_bwd(const torch::Tensor& dy, const torch::T
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   launch_colsum(part, G, static_cast<int>(F), static_cast<int>(F), 0, db, db_acc.has_value());
   return {dx, db};
+}
+
+torch::Tensor bias_residual_fwd(const torch::Tensor& y, const torch::Tensor& b, const torch::Tensor& x) {
+  check_bf16_2d(y, "bias_residual_fwd y");
+  check_bf16_2d(x, "bias_residual_fwd x");
+  TORCH_CHECK(y.sizes() == x.sizes(), "bias_residual_fwd: y / x shapes differ");
+  const int64_t rows = y.size(0), F = y.size(1);
+  check_vec(b, F, at::kBFloat16, "bias_residual_fwd b");
+  TORCH_CHECK(F % 8 == 0 && rows <= 0x7fffffff, "bias_residual: F must be a multiple of 8");
+  const at::cuda::CUDAGuard guard(y.device());
+  auto out = torch::empty_like(y);
+  if (rows == 0) return out;
+  const dim3 grid(static_cast<unsigned>((F / 8 + 127) / 128), static_cast<unsigned>(std::min<int64_t>(rows, 65535)));
+  bias_residual_fwd_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      static_cast<int>(rows), static_cast<int>(F));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+// Column sums of g [rows, F] in fp32 (a bias gradient); with acc (fp32, F) they are added there.
+torch::Tensor bias_grad(const torch::Tensor& g, const c10::optional<torch::Tensor>& acc) {
+  check_bf16_2d(g, "bias_grad g");
+  const int64_t rows = g.size(0), F = g.size(1);
+  TORCH_CHECK(F % 8 == 0 && rows <= 0x7fffffff, "bias_grad: F must be a multiple of 8");
+  const at::cuda::CUDAGuard guard(g.device());
+  torch::Tensor db;
+  if (acc.has_value()) {
+    check_vec(*acc, F, at::kFloat, "bias_grad acc");
+    db = *acc;
+  } else {
+    db = torch::empty({F}, g.options().dtype(at::kFloat));
+  }
+  if (rows == 0) {
+    if (!acc.has_value()) db.zero_();
+    return db;
+  }
+  const int col_blocks = static_cast<int>((F / 8 + 127) / 128);
+  const int64_t want = std::max<int64_t>(1, static_cast<int64_t>(num_sms(g)) * 16 / col_blocks);
+  const int G = static_cast<int>(std::min<int64_t>({rows, want, 65535}));
+  auto part = torch::empty({G, F}, g.options().dtype(at::kFloat));
+  col_partial_kernel<<<dim3(static_cast<unsigned>(col_blocks), static_cast<unsigned>(G)), 128, 0,
+                       at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+                                                           part.data_ptr<float>(), static_cast<int>(rows),
+                                                           static_cast<int>(F));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_colsum(part, G, static_cast<int>(F), static_cast<int>(F), 0, db, acc.has_value());
+  return db;
 }
 
 // Returns (q, k, v), each [N, nh, DP] bf16 with the head columns past D zero.

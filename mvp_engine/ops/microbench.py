@@ -456,6 +456,8 @@ def bench_vision(tokens: int, iters: int) -> None:
         "bias_gelu_fwd_tanh": (lambda: e.bias_gelu_fwd(h, bf, True),
                                lambda: torch.nn.functional.gelu(h + bf, approximate="tanh"), 2 * N * Fd * 2),
         "bias_gelu_bwd_tanh": (lambda: e.bias_gelu_bwd(dh, h, bf, True), None, 3 * N * Fd * 2),
+        "bias_residual_fwd": (lambda: e.bias_residual_fwd(x, b, dy), lambda: dy + (x + b), 3 * N * H * 2),
+        "bias_grad": (lambda: e.bias_grad(dy), lambda: dy.float().sum(0), N * H * 2),
         "vision_rope_fwd": (lambda: e.vision_rope_fwd(qkv, nh, cos, sin, 128), eager_rope,
                             N * 3 * H * 2 + 3 * N * nh * 128 * 2 + 2 * N * (D // 2) * 4),
         # reads the first D columns of each padded gradient row, writes dqkv

@@ -81,6 +81,29 @@ def test_bias_gelu(approximate, rows, Fd):
 
 
 @cuda
+@pytest.mark.parametrize("rows,H", [(1, 1152), (3000, 1152), (257, 4096)])
+def test_bias_residual(rows, H):
+    ops = _ops()
+    torch.manual_seed(0)
+    y = torch.randn(rows, H, device="cuda").bfloat16().requires_grad_()
+    x = torch.randn(rows, H, device="cuda").bfloat16().requires_grad_()
+    b = torch.randn(H, device="cuda").bfloat16().requires_grad_()
+    out = ops.bias_residual(y, b, x)
+    yf, xf, bf = (t.detach().float().requires_grad_() for t in (y, x, b))
+    ref = xf + (yf + bf)
+    assert _rel_err(out, ref) < 8e-3
+    g = torch.randn(rows, H, device="cuda").bfloat16()
+    out.backward(g)
+    ref.backward(g.float())
+    assert _rel_err(x.grad, xf.grad) < 1e-2 and _rel_err(y.grad, yf.grad) < 1e-2
+    assert _rel_err(b.grad, bf.grad) < 1e-2
+    b2 = b.detach().clone().requires_grad_()
+    b2._mvp_grad_acc = torch.ones(H, device="cuda")
+    ops.bias_residual(y.detach(), b2, x.detach()).backward(g)
+    assert b2.grad is None and _rel_err(b2._mvp_grad_acc - 1, bf.grad) < 1e-2
+
+
+@cuda
 @pytest.mark.parametrize("N,nh,D", [(1, 16, 72), (1000, 16, 72), (300, 3, 64), (50, 4, 32)])
 def test_vision_rope_pad(N, nh, D):
     ops = _ops()
