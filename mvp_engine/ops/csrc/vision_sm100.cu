@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(128) col_partial_kernel(const __nv_bfloat16* _
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll 4
   for (int r = blockIdx.y; r < rows; r += gridDim.y) {
     float f[8];
     vload8(g + static_cast<int64_t>(r) * F + v * 8, f);
@@ -640,7 +641,8 @@ torch::Tensor bias_grad(const torch::Tensor& g, const c10::optional<torch::Tenso
     return db;
   }
   const int col_blocks = static_cast<int>((F / 8 + 127) / 128);
-  const int64_t want = std::max<int64_t>(1, static_cast<int64_t>(num_sms(g)) * 16 / col_blocks);
+  // few row groups: the column-sum pass over the partials is one thread per column
+  const int64_t want = std::max<int64_t>(1, static_cast<int64_t>(num_sms(g)) * 4 / col_blocks);
   const int G = static_cast<int>(std::min<int64_t>({rows, want, 65535}));
   auto part = torch::empty({G, F}, g.options().dtype(at::kFloat));
   col_partial_kernel<<<dim3(static_cast<unsigned>(col_blocks), static_cast<unsigned>(G)), 128, 0,
