@@ -4,7 +4,8 @@
 // attention kernel's layout.  bf16 in and out, fp32 math, one bf16 rounding
 // per output as PyTorch's eager ops round (transformers Qwen3VLVisionBlock /
 // Qwen3VLVisionMLP / apply_rotary_pos_emb_vision, the modules the reference's
-// qwen3_vl recipe trains: recipes/qwen3_vl/model/* builds them from HF).
+// qwen3_vl recipe trains; it patches only the patch embedding of that HF model,
+// recipes/qwen3_vl/model/qwen3_vl.py:151-171).
 //
 // Parameter gradients (LayerNorm weight / bias, GELU bias) are column sums over
 // rows: each CTA sums its rows into fp32 partials, a second kernel sums the
