@@ -4,7 +4,11 @@
 # copy of its recipes/ tree, which the wheel does not package.
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-SRC="${1:-/root/reference}"
+if [ $# -lt 1 ]; then
+    echo "usage: $0 <path to the reference source tree>" >&2
+    exit 2
+fi
+SRC="$1"
 python -m pip install --no-index --no-build-isolation --no-deps --find-links /opt/wheelhouse \
     --target "$HERE/_ref" "$SRC"
 # package data the wheel does not declare (the launcher and engine read it at run time)

@@ -285,12 +285,52 @@ class MappedLoader:
     def map(self, fn: Callable) -> "MappedLoader":
         return MappedLoader(self, fn)
 
+    def state_dict(self) -> Optional[dict]:
+        inner = getattr(self.loader, "state_dict", None)
+        return inner() if callable(inner) else None
+
+    def load_state_dict(self, state: dict) -> None:
+        inner = getattr(self.loader, "load_state_dict", None)
+        if callable(inner):
+            inner(state)
+
 
 class BatchLoader(torch.utils.data.DataLoader):
-    """torch ``DataLoader`` with ``map(fn)`` for per-batch host transforms."""
+    """torch ``DataLoader`` with ``map(fn)`` for per-batch host transforms and a resumable position.
+
+    The position is the number of batches handed out since the current pass began.  Sources are
+    seeded and the pipeline is deterministic, so a restored loader reproduces its stream by drawing
+    and dropping that many batches at the start of its next pass (exact, at the cost of re-reading
+    them)."""
+
+    _handed_out = 0
+    _fast_forward = 0
 
     def map(self, fn: Callable) -> MappedLoader:
         return MappedLoader(self, fn)
+
+    def __iter__(self):
+        source = super().__iter__()
+        skip, self._fast_forward = self._fast_forward, 0
+        self._handed_out = 0
+        return self._positioned(source, skip)
+
+    def _positioned(self, source, skip: int):
+        for _ in range(skip):
+            try:
+                next(source)
+            except StopIteration:
+                return
+            self._handed_out += 1
+        for batch in source:
+            self._handed_out += 1
+            yield batch
+
+    def state_dict(self) -> dict:
+        return {"batches_into_pass": int(self._handed_out)}
+
+    def load_state_dict(self, state: dict) -> None:
+        self._fast_forward = int(state.get("batches_into_pass", 0))
 
 
 class TorchLoader:

@@ -1,24 +1,31 @@
-"""Template-method training engine (reference: mvp_engine/engine/engine.py:50-592).
+"""Template-method training engine.
 
-Workflow::
+Public contract (the reference's, ``mvp_engine/engine/engine.py:50-592`` there): recipes
+subclass :class:`Engine`, implement ``prepare_model / prepare_optimizer /
+prepare_scheduler / prepare_dataloader`` and may override any hook below::
 
     __init__  : prepare_config -> prepare_parallel -> prepare_runtime_info
                 -> set_seed -> prepare_logger
     train()   : before_train -> do_train -> after_train
     do_train  : per micro-batch  train_pre_step -> train_exec_step
-                (forward_step -> backward_step -> optimizer_step)
-                and after each optimizer step train_post_step + save
+                (forward_step -> backward_step -> optimizer_step);
+                after each optimizer step  train_post_step -> save
 
-Subclasses implement ``prepare_model / prepare_optimizer / prepare_scheduler /
-prepare_dataloader`` exactly as in the reference.  Additions of this engine:
+How this engine runs that contract:
 
-* the process group also comes up on CPU (gloo) and always has a timeout;
+* the micro-batch stream (:meth:`_micro_batches`) is one generator that rolls
+  over epochs; the loop in :meth:`do_train` and the public single-step API
+  :meth:`train_step` stage batches through the same :meth:`_stage` helper;
 * every optimizer step is timed on the device with CUDA events
-  (``self.step_time_ms``, max over ranks), next to the reference's host
-  ``Timer``;
-* after each optimizer step the device status word written by bounded waits in
-  the native kernels is checked, so a peer that stopped responding surfaces as
-  an exception on the host instead of a hang.
+  (``self.step_time_ms``, max over ranks) next to the host ``Timer``;
+* after each optimizer step the device status word that the native kernels'
+  bounded waits write is checked, so a peer that stopped answering becomes a host
+  exception instead of a hang; a store heartbeat watchdog is polled before each
+  micro-batch;
+* checkpoint directories are committed with a completion marker and pruned only
+  after the new one is complete (:class:`~.checkpoint_store.CheckpointStore`);
+  ``resume: latest`` picks the newest complete one.  The data loader's position
+  travels in the per-rank engine state when the loader can report it.
 """
 
 from __future__ import annotations
@@ -28,14 +35,13 @@ import os
 import platform
 import random
 import secrets
-import shutil
 import socket
 import time
 from abc import ABC, abstractmethod
 from dataclasses import dataclass
 from os import PathLike
 from pathlib import Path
-from typing import Any, ClassVar, Optional, Type, Union
+from typing import Any, Callable, ClassVar, Iterator, Optional, Type, Union
 
 import numpy as np
 import torch
@@ -52,28 +58,14 @@ from ..utils.log.backend import FileBackend, TerminalBackend, WandbBackend
 from ..utils.log.timer import CudaStepTimer, Timer
 from ..utils.misc import calculate_model_size, get_device, get_git_info
 from ..utils.training import GradientAccumulationState, GradientScaler, accumulate_gradients, clip_grad_norm_
+from .checkpoint_store import COMPLETE_MARKER, CheckpointStore, latest_complete_checkpoint
 
 logging.captureWarnings(True)
 logging.basicConfig(level=os.environ.get("LOGLEVEL", "ERROR").upper())
 
+__all__ = ["COMPLETE_MARKER", "Engine", "TrainStepContext", "latest_complete_checkpoint", "set_seed"]
 
-COMPLETE_MARKER = "COMPLETE"
-
-
-def latest_complete_checkpoint(root: Union[str, PathLike]) -> Optional[str]:
-    """Newest ``<policy>_<n>`` directory under ``root`` holding the completion marker (None if none).
-
-    A checkpoint interrupted mid-save (or damaged afterwards and stripped of its marker) is skipped,
-    so an automatic restart resumes from the last checkpoint that was fully written.
-    """
-    root = Path(root)
-    if not root.is_dir():
-        return None
-    cands = [p for p in root.iterdir() if p.is_dir() and p.name.split("_")[-1].isdigit()]
-    for p in sorted(cands, key=lambda p: int(p.name.split("_")[-1]), reverse=True):
-        if (p / COMPLETE_MARKER).is_file():
-            return str(p)
-    return None
+_COMPUTE_DTYPES = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
 
 
 @dataclass
@@ -91,15 +83,24 @@ class TrainStepContext:
 
 
 def set_seed(seed: int, deterministic: bool = False) -> None:
-    """Seed python, numpy and torch (all devices); optionally force deterministic kernels."""
+    """Seed python, numpy and torch (every device); optionally ask for deterministic kernels."""
     random.seed(seed)
     np.random.seed(seed % (2**32))
     torch.manual_seed(seed)
     if torch.cuda.is_available():
         torch.cuda.manual_seed_all(seed)
     if deterministic:
-        torch.use_deterministic_algorithms(True, warn_only=True)
         os.environ.setdefault("CUBLAS_WORKSPACE_CONFIG", ":4096:8")
+        torch.use_deterministic_algorithms(True, warn_only=True)
+
+
+def _log_backend_factories(engine: "Engine") -> dict[str, Callable[[], Any]]:
+    out_dir = Path(engine.config.runtime.output_dir)
+    return {
+        "terminal": lambda: TerminalBackend(id=engine.run_id),
+        "file": lambda: FileBackend(id=engine.run_id, path=out_dir),
+        "wandb": lambda: WandbBackend(id=engine.run_id, project=engine.config.project.name, path=out_dir),
+    }
 
 
 class Engine(ABC):
@@ -124,6 +125,7 @@ class Engine(ABC):
         self.step_time_ms: float = 0.0
         self._cuda_timer = CudaStepTimer()
         self._step_timer_running = False
+        self._watchdog = None
 
     # ------------------------------------------------------------ properties
     def prepare_config(self, config: Any) -> BaseEngineConfig:
@@ -131,8 +133,9 @@ class Engine(ABC):
 
     @property
     def device(self) -> torch.device:
-        return get_device(index=get_local_rank() % max(1, torch.cuda.device_count()) if torch.cuda.is_available()
-                          else 0)
+        if not torch.cuda.is_available():
+            return get_device(index=0)
+        return get_device(index=get_local_rank() % max(1, torch.cuda.device_count()))
 
     @property
     def device_type(self) -> str:
@@ -140,14 +143,25 @@ class Engine(ABC):
 
     @property
     def dtype(self) -> torch.dtype:
-        return {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}.get(
-            self.config.optim.mixed_precision, torch.float32)
+        return _COMPUTE_DTYPES.get(self.config.optim.mixed_precision, torch.float32)
+
+    @property
+    def loop_policy(self) -> str:
+        return self.config.loop.policy
+
+    def _require_iter_policy(self, what: str, exc: type) -> None:
+        if self.loop_policy != "iter":
+            raise exc(f"Unsupported loop policy for {what}: {self.loop_policy}")
 
     @property
     def total_steps(self) -> int:
-        if self.loop_policy == "iter":
-            return self.config.loop.total_steps
-        raise NotImplementedError(f"Unsupported loop policy: {self.loop_policy}")
+        self._require_iter_policy("total_steps", NotImplementedError)
+        return self.config.loop.total_steps
+
+    @property
+    def progress(self) -> float:
+        self._require_iter_policy("progress", ValueError)
+        return self.step / self.total_steps
 
     @property
     def project_dir(self) -> Path:
@@ -158,10 +172,6 @@ class Engine(ABC):
         return self.config.runtime.run_id
 
     @property
-    def loop_policy(self) -> str:
-        return self.config.loop.policy
-
-    @property
     def _accumulate_step(self) -> int:
         return self.ga_state.micro_step
 
@@ -170,20 +180,12 @@ class Engine(ABC):
         self.ga_state.micro_step = int(value)
 
     @property
-    def progress(self) -> float:
-        if self.loop_policy == "iter":
-            return self.step / self.total_steps
-        raise ValueError(f"Unsupported loop policy: {self.loop_policy}")
-
-    @property
     def unwrapped_model(self) -> torch.nn.Module:
+        """The innermost module under DDP-style ``.module`` wrappers."""
         m = self.model
-        while True:
-            inner = getattr(m, "module", None)
-            if isinstance(inner, torch.nn.Module) and inner is not m:
-                m = inner
-                continue
-            return m
+        while isinstance(getattr(m, "module", None), torch.nn.Module) and m.module is not m:
+            m = m.module
+        return m
 
     # --------------------------------------------------------------- set-up
     def set_seed(self, seed: int, deterministic: bool = False) -> None:
@@ -194,36 +196,27 @@ class Engine(ABC):
         self.parallel_mesh = ParallelMesh.initialize(self.device.type, self.config.parallel.mesh.model_dump())
 
     def prepare_runtime_info(self) -> None:
-        git = get_git_info()
         rt = self.config.runtime
+        git = get_git_info()
         rt.git_info = f"<{git['branch']}> {git['commit_hash']}"
         rt.world_size = dist.get_world_size() if dist.is_initialized() else 1
         rt.hostname = socket.gethostname()
         rt.python_version = platform.python_version()
         rt.torch_version = str(torch.__version__)
         if not rt.run_id:
-            local = f"{self.config.project.name}_{time.strftime('%Y%m%d%H%M%S', time.localtime())}_{secrets.token_hex(2)}"
-            rt.run_id = broadcast_from_main(local)
+            stamp = time.strftime("%Y%m%d%H%M%S", time.localtime())
+            rt.run_id = broadcast_from_main(f"{self.config.project.name}_{stamp}_{secrets.token_hex(2)}")
         rt.output_dir = str(Path(self.config.project.dir) / rt.run_id)
 
     def prepare_logger(self) -> None:
-        backends = []
-        if self.config.dev_mode:
-            backends = [TerminalBackend(id=self.run_id)]
-        else:
-            for b in self.config.log.backends:
-                if b == "terminal":
-                    backends.append(TerminalBackend(id=self.run_id))
-                elif b == "file":
-                    backends.append(FileBackend(id=self.run_id, path=Path(self.config.runtime.output_dir)))
-                elif b == "wandb":
-                    backends.append(WandbBackend(id=self.run_id, project=self.config.project.name,
-                                                 path=Path(self.config.runtime.output_dir)))
-                else:
-                    raise ValueError(f"Invalid log backend: {b}")
+        factories = _log_backend_factories(self)
+        names = ["terminal"] if self.config.dev_mode else list(self.config.log.backends)
+        unknown = [n for n in names if n not in factories]
+        if unknown:
+            raise ValueError(f"Invalid log backend: {unknown[0]}")
         acc = self.config.log.accumulation_size
-        init_logger(backends, interval=self.config.log.interval,
-                    accumulation_size=acc if acc is not None else self.config.log.interval)
+        init_logger([factories[n]() for n in names], interval=self.config.log.interval,
+                    accumulation_size=self.config.log.interval if acc is None else acc)
 
     @abstractmethod
     def prepare_model(self) -> torch.nn.Module: ...
@@ -238,46 +231,53 @@ class Engine(ABC):
     def prepare_dataloader(self, workflow: str = "train") -> Any: ...
 
     # ------------------------------------------------------------ checkpoint
+    def _checkpoint_store(self) -> CheckpointStore:
+        return CheckpointStore(self.project_dir / "checkpoints", self.config.checkpoint.keep_n,
+                               is_writer=is_main_process())
+
+    def _checkpoint_tag(self) -> str:
+        counter = self.epoch if self.loop_policy == "epoch" else self.step
+        return f"{self.loop_policy}_{counter}"
+
+    def _data_state(self) -> Optional[dict]:
+        loader = getattr(self, "train_loader", None)
+        getter = getattr(loader, "state_dict", None)
+        return getter() if callable(getter) else None
+
     def save(self, force: bool = False) -> None:
-        interval = self.config.checkpoint.interval
-        if (not force and self.step % interval != 0) or self.config.dev_mode:
+        due = force or self.step % self.config.checkpoint.interval == 0
+        if self.config.dev_mode or not due:
+            return
+        store, tag = self._checkpoint_store(), self._checkpoint_tag()
+        if store.is_current(tag, self.step):
+            logger.info(f"Checkpoint {tag} already holds step {self.step}; not rewritten.")
             return
         logger.info(f"Saving checkpoint for step {self.step}...")
-        ckpt_root = self.project_dir / "checkpoints"
-        ckpt_root.mkdir(parents=True, exist_ok=True)
-        tag = f"{self.loop_policy}_{self.epoch if self.loop_policy == 'epoch' else self.step}"
-        cur = ckpt_root / tag
-        if is_main_process():
-            existing = sorted((p for p in os.listdir(ckpt_root) if p != cur.name and p.split("_")[-1].isdigit()),
-                              key=lambda p: int(p.split("_")[-1]))
-            keep_existing = self.config.checkpoint.keep_n - 1
-            for old in existing[: max(len(existing) - keep_existing, 0)]:
-                shutil.rmtree(ckpt_root / old, ignore_errors=True)
-        cur.mkdir(parents=True, exist_ok=True)
-        if dist.is_initialized():
-            dist.barrier()
-        save_checkpoint(self.parallel_mesh.device_mesh, cur, self.model, self.optimizer, scheduler=self.scheduler,
+        target = store.begin(tag)
+        save_checkpoint(self.parallel_mesh.device_mesh, target, self.model, self.optimizer, scheduler=self.scheduler,
                         scaler=self.scaler, step=self.step, epoch=self.epoch, _accumulate_step=self._accumulate_step,
-                        hf_enable=self.config.checkpoint.hf_enable)
-        if dist.is_initialized():
-            dist.barrier()
-        if is_main_process():  # written last: a checkpoint without it is incomplete and never resumed from
-            (cur / COMPLETE_MARKER).write_text(str(self.step))
+                        hf_enable=self.config.checkpoint.hf_enable, data_state=self._data_state())
+        store.commit(tag, self.step)
 
     def load(self, ckpt_path: Union[str, PathLike], restore_training_state: bool = True,
              restore_rng_state: bool = True) -> None:
-        logger.info(f"{'Loading checkpoint' if restore_training_state else 'Initializing model from'} {ckpt_path}...")
+        verb = "Loading checkpoint" if restore_training_state else "Initializing model from"
+        logger.info(f"{verb} {ckpt_path}...")
+        restore = restore_training_state
         state = load_checkpoint(self.parallel_mesh.device_mesh, ckpt_path, self.model,
-                                self.optimizer if restore_training_state else None,
-                                self.scheduler if restore_training_state else None,
-                                self.scaler if restore_training_state else None,
-                                restore_engine_state=restore_training_state, restore_rng_state=restore_rng_state,
+                                optimizer=self.optimizer if restore else None,
+                                scheduler=self.scheduler if restore else None,
+                                scaler=self.scaler if restore else None,
+                                restore_engine_state=restore, restore_rng_state=restore_rng_state,
                                 hf_enable=self.config.checkpoint.hf_enable)
         if state is None:
             return
-        self.step = state["step"]
-        self.epoch = state["epoch"]
+        self.step, self.epoch = int(state["step"]), int(state["epoch"])
         self._accumulate_step = state["_accumulate_step"]
+        data_state = state.get("data_state")
+        loader = getattr(self, "train_loader", None)
+        if data_state is not None and callable(getattr(loader, "load_state_dict", None)):
+            loader.load_state_dict(data_state)
         if hasattr(self, "timer"):
             self.timer.set_progress(self.step, self.total_steps)
 
@@ -287,83 +287,107 @@ class Engine(ABC):
         self.do_train()
         self.after_train()
 
-    def before_train(self) -> None:
-        logger.log_config(self.config.model_dump())
-        logger.info("Building DataLoader...")
+    def _build_loaders(self) -> None:
         self.train_loader = self.prepare_dataloader("train")
         self.evaluate_loader = self.prepare_dataloader("evaluate")
-        logger.info("Building Model...")
+
+    def _build_model(self) -> None:
         self.model = self.prepare_model()
         total, trainable = calculate_model_size(self.model)
         logger.info(f" - Model size: {total / 1e9:.4f} B")
         logger.info(f" - Trainable model size: {trainable / 1e9:.4f} B")
-        logger.info("Building Optimizer...")
+
+    def _build_optimizer(self) -> None:
         self.optimizer = self.prepare_optimizer()
         self.ga_state = GradientAccumulationState(self.config.optim.gradient_accumulation_steps)
-        logger.info("Building Scheduler...")
+
+    def _build_scheduler(self) -> None:
         self.scheduler = self.prepare_scheduler()
-        logger.info("Building GradientScaler...")
+
+    def _build_scaler(self) -> None:
         self.scaler = GradientScaler(enabled=self.dtype != torch.float32, dtype=self.dtype, device=self.device_type)
+
+    def _resume_source(self) -> Optional[str]:
         resume = getattr(self.config, "resume", None)
-        if resume == "latest":  # newest complete checkpoint of this project, if any
-            resume = latest_complete_checkpoint(self.project_dir / "checkpoints")
-        if resume is not None:
-            self.load(resume, restore_training_state=True, restore_rng_state=True)
+        if resume == "latest":  # the newest complete checkpoint of this run, if there is one
+            return latest_complete_checkpoint(self.project_dir / "checkpoints")
+        return resume
+
+    def before_train(self) -> None:
+        logger.log_config(self.config.model_dump())
+        for label, build in (("DataLoader", self._build_loaders), ("Model", self._build_model),
+                             ("Optimizer", self._build_optimizer), ("Scheduler", self._build_scheduler),
+                             ("GradientScaler", self._build_scaler)):
+            logger.info(f"Building {label}...")
+            build()
+        source = self._resume_source()
+        if source is not None:
+            self.load(source, restore_training_state=True, restore_rng_state=True)
         from ..distributed.watchdog import start_default_watchdog
 
         self._watchdog = start_default_watchdog()
         logger.info("Initializing Timer...")
         self.timer = Timer(total_progress=self.total_steps, window_size=self.config.log.timer_window_size)
 
+    def _micro_batches(self) -> Iterator[Any]:
+        """Endless stream of training batches; each pass over the loader is one epoch."""
+        while True:
+            empty = True
+            for batch in self.train_loader:
+                empty = False
+                yield batch
+            if empty:
+                raise RuntimeError("the training data loader produced no batches")
+            self.epoch += 1
+            logger.info(f"Starting epoch {self.epoch}...")
+
+    def _stage(self, data: Any) -> TrainStepContext:
+        """Wrap one host batch in a step context and run ``train_pre_step`` on it."""
+        ctx = TrainStepContext(data=data, step=self.step, epoch=self.epoch, micro_step=self.ga_state.micro_step)
+        prepared = self.train_pre_step(ctx)
+        if prepared is not None and prepared is not ctx:
+            ctx.data = prepared
+        return ctx
+
     def do_train(self) -> None:
-        name = type(self.unwrapped_model).__name__
-        logger.info(f"Start training: {name} / {type(self.optimizer).__name__} / {type(self.scheduler).__name__}...")
+        parts = [type(self.unwrapped_model).__name__, type(self.optimizer).__name__, type(self.scheduler).__name__]
+        logger.info(f"Start training: {' / '.join(parts)}...")
         self.model.train()
         self.timer.start()
         self.timer.set_progress(self.step)
+        stream = self._micro_batches()
         while self.progress < 1.0:
-            it = iter(self.train_loader)
-            try:
-                while self.progress < 1.0:
-                    with self.timer.scope("data_time"):
-                        data = next(it)
-                        ctx = TrainStepContext(data=data, step=self.step, epoch=self.epoch,
-                                               micro_step=self.ga_state.micro_step)
-                        prepared = self.train_pre_step(ctx)
-                        if prepared is not None and prepared is not ctx:
-                            ctx.data = prepared
-                    if getattr(self, "_watchdog", None) is not None:
-                        self._watchdog.check()  # a silent peer ends the run before the next collectives
-                    with self.timer.scope("exec_time"):
-                        self.train_exec_step(ctx)
-                    if not ctx.optimizer_step_completed:
-                        continue
-                    assert ctx.outputs is not None, "The forward step must populate ctx.outputs."
-                    self.step += 1
-                    self.timer.tick()
-                    self.train_post_step(ctx)
-                    self.save()
-            except StopIteration:
-                self.epoch += 1
-                logger.info(f"Starting epoch {self.epoch}...")
+            with self.timer.scope("data_time"):
+                ctx = self._stage(next(stream))
+            if self._watchdog is not None:
+                self._watchdog.check()  # a silent peer ends the run before the next collective
+            with self.timer.scope("exec_time"):
+                self.train_exec_step(ctx)
+            if ctx.optimizer_step_completed:
+                assert ctx.outputs is not None, "The forward step must populate ctx.outputs."
+                self.step += 1
+                self.timer.tick()
+                self.train_post_step(ctx)
+                self.save()
 
     def train_step(self, micro_batches: list[Any]) -> dict[str, Any]:
-        """One optimizer step over ``micro_batches`` (host batches as the dataloader yields them):
-        each goes through ``train_pre_step`` and ``train_exec_step``; the step's outputs are returned.
-        This is the public single-step API the training loop, benchmarks and tests share."""
-        if len(micro_batches) != int(self.config.optim.gradient_accumulation_steps):
-            raise ValueError(f"expected {self.config.optim.gradient_accumulation_steps} micro-batches, "
-                             f"got {len(micro_batches)}")
-        ctx = None
+        """One optimizer step over ``micro_batches`` (host batches, as the data loader yields them).
+
+        Each batch is staged through ``train_pre_step`` and run through ``train_exec_step``; the last
+        one must complete the optimizer step.  Returns that step's outputs.  The benchmark and the
+        tests drive training through this call."""
+        expected = int(self.config.optim.gradient_accumulation_steps)
+        if len(micro_batches) != expected:
+            raise ValueError(f"expected {expected} micro-batches, got {len(micro_batches)}")
+        contexts = []
         for data in micro_batches:
-            ctx = TrainStepContext(data=data, step=self.step, epoch=self.epoch, micro_step=self.ga_state.micro_step)
-            prepared = self.train_pre_step(ctx)
-            if prepared is not None and prepared is not ctx:
-                ctx.data = prepared
+            ctx = self._stage(data)
             self.train_exec_step(ctx)
-        assert ctx is not None and ctx.optimizer_step_completed, "the last micro-batch must complete a step"
+            contexts.append(ctx)
+        if not contexts[-1].optimizer_step_completed:
+            raise RuntimeError("the last micro-batch did not complete an optimizer step")
         self.step += 1
-        return ctx.outputs or {}
+        return contexts[-1].outputs or {}
 
     def train_pre_step(self, ctx: TrainStepContext) -> Optional[TrainStepContext]:
         return None
@@ -390,41 +414,49 @@ class Engine(ABC):
             _ext.check_status(self.device)
 
     def forward_step(self, ctx: TrainStepContext) -> None:
-        with torch.autocast(device_type=self.device_type, dtype=self.dtype, enabled=self.dtype != torch.float32):
+        mixed = self.dtype != torch.float32
+        with torch.autocast(device_type=self.device_type, dtype=self.dtype, enabled=mixed):
             ctx.outputs = self.model(ctx.data)
 
     def backward_step(self, ctx: TrainStepContext) -> None:
-        assert ctx.outputs is not None and "loss" in ctx.outputs and "logs" in ctx.outputs
+        out = ctx.outputs
+        missing = [k for k in ("loss", "logs") if out is None or k not in out]
+        assert not missing, f"the model output lacks {missing}"
         ctx.should_sync = self.ga_state.advance()
-        ctx.loss = ctx.outputs["loss"] / self.config.optim.gradient_accumulation_steps
+        ctx.loss = out["loss"] / self.config.optim.gradient_accumulation_steps
         with accumulate_gradients(self.model, sync=ctx.should_sync):
             self.scaler.scale(ctx.loss).backward()
 
-    def optimizer_step(self, ctx: TrainStepContext) -> None:
-        if not ctx.should_sync:
-            return
+    def _apply_update(self) -> None:
+        """Unscale, clip, step, advance the schedule and clear gradients."""
         self.scaler.unscale_(self.optimizer)
-        if self.config.optim.clip_grad_norm is not None:
-            clip_grad_norm_(self.model, self.config.optim.clip_grad_norm)
+        limit = self.config.optim.clip_grad_norm
+        if limit is not None:
+            clip_grad_norm_(self.model, limit)
         self.scaler.step(self.optimizer)
         self.scaler.update()
         self.scheduler.step()
         self.optimizer.zero_grad(set_to_none=True)
-        ctx.optimizer_step_completed = True
+
+    def optimizer_step(self, ctx: TrainStepContext) -> None:
+        if ctx.should_sync:
+            self._apply_update()
+            ctx.optimizer_step_completed = True
 
     def train_post_step(self, ctx: TrainStepContext) -> None:
-        logs = {"eta": self.timer.eta_string, "perf/data_time": self.timer.get_scope_time("data_time"),
-                "perf/exec_time": self.timer.get_scope_time("exec_time"),
-                "perf/step_time_device_ms": self.step_time_ms}
-        for i, lr in enumerate(self.scheduler.get_last_lr()):
-            logs[f"lr/group_{i}"] = lr
-        self.last_logs = {**ctx.outputs["logs"], **logs}
-        logger.log_metrics(self.last_logs, step=self.step, total_steps=self.total_steps)
+        logs = dict(ctx.outputs["logs"])
+        logs.update({"eta": self.timer.eta_string, "perf/data_time": self.timer.get_scope_time("data_time"),
+                     "perf/exec_time": self.timer.get_scope_time("exec_time"),
+                     "perf/step_time_device_ms": self.step_time_ms})
+        logs.update({f"lr/group_{i}": lr for i, lr in enumerate(self.scheduler.get_last_lr())})
+        self.last_logs = logs
+        logger.log_metrics(logs, step=self.step, total_steps=self.total_steps)
 
     def after_train(self) -> None:
-        if getattr(self, "_watchdog", None) is not None:
+        if self._watchdog is not None:
             self._watchdog.stop()
-        self.save(force=True and not self.config.dev_mode)
+        if not self.config.dev_mode:
+            self.save(force=True)
         logger.info("Training finished!")
         logger.destroy()
 

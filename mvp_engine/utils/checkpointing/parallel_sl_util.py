@@ -131,13 +131,18 @@ def _restore_rng(st: dict[str, Any]) -> None:
 # -------------------------------------------------------------------- save
 def save_checkpoint(mesh, cur_checkpoint_dir: Path, model: nn.Module, optimizer=None, scheduler=None, scaler=None,
                     step: int = 0, epoch: int = 0, _accumulate_step: int = 0, prefix: str = "",
-                    hf_enable: bool = False) -> None:
+                    hf_enable: bool = False, data_state: Optional[dict] = None) -> None:
+    """Write one checkpoint directory.  ``data_state`` (this rank's data-loader position, when the
+    loader reports one) is stored beside the rank's RNG state in ``engine/rank_<r>.pt``."""
     cur = Path(cur_checkpoint_dir)
     backend = infer_checkpoint_backend(mesh)
     if prefix == "":
         (cur / "engine").mkdir(parents=True, exist_ok=True)
         _barrier()
-        torch.save(_rng_state(), cur / "engine" / f"rank_{get_rank()}.pt")
+        per_rank = _rng_state()
+        if data_state is not None:
+            per_rank["data_state"] = data_state
+        torch.save(per_rank, cur / "engine" / f"rank_{get_rank()}.pt")
 
     if backend == "ddp":
         # Unsharded: every rank holds full state; rank 0 writes it.
@@ -256,11 +261,15 @@ def load_checkpoint(mesh, ckpt_path, model: nn.Module, optimizer=None, scheduler
         scheduler.load_state_dict(state["scheduler"])
     if scaler is not None and "scaler" in state:
         scaler.load_state_dict(state["scaler"])
-    if restore_rng_state:
-        rng = cur / "engine" / f"rank_{get_rank()}.pt"
-        if os.path.exists(rng):
-            _restore_rng(torch.load(rng, map_location="cpu", weights_only=False))
-    return {"step": state["step"], "epoch": state["epoch"], "_accumulate_step": state["_accumulate_step"]}
+    out = {"step": state["step"], "epoch": state["epoch"], "_accumulate_step": state["_accumulate_step"]}
+    per_rank_path = cur / "engine" / f"rank_{get_rank()}.pt"
+    if os.path.exists(per_rank_path):
+        per_rank = torch.load(per_rank_path, map_location="cpu", weights_only=False)
+        if restore_rng_state:
+            _restore_rng(per_rank)
+        if "data_state" in per_rank:
+            out["data_state"] = per_rank["data_state"]
+    return out
 
 
 def _load_model_full(base: nn.Module, sd: dict[str, torch.Tensor]) -> None:

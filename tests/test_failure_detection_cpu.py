@@ -167,3 +167,43 @@ def test_engine_resumes_from_latest_complete_checkpoint(tmp_path):
     assert "iter_4" in ckpts
     second = spawn_workers(_resume_run, 1, str(tmp_path), 6, True, timeout=300)[0]
     assert second == (4, 6)
+
+
+def _fake_ckpt(store, tag, step, *, interrupt=False):
+    path = store.begin(tag)
+    (path / "model").mkdir(exist_ok=True)
+    (path / "model" / "shard.bin").write_bytes(os.urandom(32))
+    if interrupt:
+        raise RuntimeError("killed mid-save")
+    store.commit(tag, step)
+
+
+def test_checkpoint_rewrite_interrupted_is_not_resumed(tmp_path):
+    """A directory being rewritten loses its marker first, so a crash mid-rewrite falls back to the
+    previous complete checkpoint; a save of a step that is already complete is recognised."""
+    from mvp_engine.engine.checkpoint_store import CheckpointStore, latest_complete_checkpoint
+
+    root = tmp_path / "checkpoints"
+    store = CheckpointStore(root, keep_n=3, is_writer=True, barrier=lambda: None)
+    _fake_ckpt(store, "epoch_1", 10)
+    _fake_ckpt(store, "epoch_2", 20)
+    assert store.is_current("epoch_2", 20) and not store.is_current("epoch_2", 25)
+    assert latest_complete_checkpoint(root) == str(root / "epoch_2")
+    with pytest.raises(RuntimeError):
+        _fake_ckpt(store, "epoch_2", 25, interrupt=True)  # same tag, new step, dies half way
+    assert latest_complete_checkpoint(root) == str(root / "epoch_1")
+
+
+def test_checkpoint_retention_counts_complete_only(tmp_path):
+    from mvp_engine.engine.checkpoint_store import CheckpointStore, latest_complete_checkpoint
+
+    root = tmp_path / "checkpoints"
+    store = CheckpointStore(root, keep_n=1, is_writer=True, barrier=lambda: None)
+    _fake_ckpt(store, "iter_2", 2)
+    with pytest.raises(RuntimeError):
+        _fake_ckpt(store, "iter_4", 4, interrupt=True)
+    # keep_n=1 and a failed save: the complete checkpoint survives, the partial one is not resumable
+    assert latest_complete_checkpoint(root) == str(root / "iter_2")
+    _fake_ckpt(store, "iter_6", 6)
+    names = sorted(p.name for p in root.iterdir())
+    assert names == ["iter_6"], names  # older complete one pruned after the new marker; stale partial gone
