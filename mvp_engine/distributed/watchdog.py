@@ -41,6 +41,8 @@ class HeartbeatWatchdog:
         self._beat = 0
         self._seen: dict[int, tuple[str, float]] = {}
         self._failed: set[int] = set()
+        self._last_store_ok = time.monotonic()
+        self._store_error = ""
         self._stop = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self._lock = threading.Lock()
@@ -68,9 +70,14 @@ class HeartbeatWatchdog:
         while not self._stop.is_set():
             try:
                 self._tick()
-            except Exception:  # noqa: BLE001 - a store that went away is itself a failure signal
-                with self._lock:
-                    self._failed.update(r for r in range(self.world) if r != self.rank)
+                self._last_store_ok = time.monotonic()
+            except Exception as exc:  # noqa: BLE001
+                # One failed store round trip is treated like a missed heartbeat: only a store that
+                # stays unreachable for timeout_s marks the peers as failed.
+                self._store_error = repr(exc)
+                if time.monotonic() - self._last_store_ok > self.timeout_s:
+                    with self._lock:
+                        self._failed.update(r for r in range(self.world) if r != self.rank)
             self._stop.wait(self.interval_s)
 
     def start(self) -> "HeartbeatWatchdog":
@@ -87,7 +94,7 @@ class HeartbeatWatchdog:
     def check(self) -> None:
         failed = self.failed_ranks()
         if failed:
-            raise PeerFailureError(failed)
+            raise PeerFailureError(failed, f"last store error {self._store_error}" if self._store_error else "")
 
     def stop(self) -> None:
         self._stop.set()

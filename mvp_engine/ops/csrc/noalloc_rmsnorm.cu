@@ -31,6 +31,9 @@
 //     is written by the same call first, so nothing needs zeroing between calls,
 //     but two calls whose kernels overlap on the GPU (different streams, or
 //     different host threads on one device) race on the scratch: serialise them.
+//   * An error already pending on the calling thread (from an earlier launch of
+//     the caller) is returned as kNoAllocPendingError without launching anything
+//     and without clearing it.
 //   * Returns 0 on success, or a kNoAlloc* code; the launches are asynchronous
 //     on `stream` (cudaStream_t, may be null for the legacy default stream).
 #include "noalloc_rmsnorm.h"
@@ -54,6 +57,7 @@ enum Code : int {
   kNoAllocBadArgument = 2,
   kNoAllocSetupFailed = 3,
   kNoAllocLaunchFailed = 4,
+  kNoAllocPendingError = 5,
 };
 
 // Weight-gradient partial sums: [kMaxSplits][kMaxHidden] fp32.
@@ -86,15 +90,15 @@ __global__ void dx_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloa
 
 // partials[split][c] = sum over the split's rows of dy * bf16(h * rstd); block = 256 columns.
 __global__ void dw_partial_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ h,
-                                  const float* __restrict__ rstd, float* __restrict__ partials, int rows, int H,
-                                  int rows_per_split) {
+                                  const float* __restrict__ rstd, float* __restrict__ partials, int64_t rows, int H,
+                                  int64_t rows_per_split) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const int split = blockIdx.y;
+  const int64_t split = blockIdx.y;
   if (c >= H) return;
-  const int r0 = split * rows_per_split;
-  const int r1 = min(rows, r0 + rows_per_split);
+  const int64_t r0 = split * rows_per_split;
+  const int64_t r1 = r0 + rows_per_split < rows ? r0 + rows_per_split : rows;
   float acc = 0.f;
-  for (int r = r0; r < r1; ++r) {
+  for (int64_t r = r0; r < r1; ++r) {
     const int64_t off = static_cast<int64_t>(r) * H + c;
     acc += __bfloat162float(dy[off]) * bf16r(__bfloat162float(h[off]) * rstd[r]);
   }
@@ -137,17 +141,24 @@ extern "C" __attribute__((visibility("default"))) int mvp_rmsnorm_bwd_noalloc(
     return kNoAllocBadArgument;
   if (rows < 1 || hidden < 1 || hidden % 8 != 0) return kNoAllocBadArgument;
   if (hidden > kMaxHidden) return kNoAllocTooLarge;
+  // An error left by an earlier launch of the caller is reported, not cleared: nothing is launched
+  // and the caller's own error handling still sees it.
+  if (cudaPeekAtLastError() != cudaSuccess) return kNoAllocPendingError;
   float* scratch = nullptr;
   if (int rc = scratch_for_current_device(&scratch); rc != kNoAllocOk) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t nrows = rows;  // int64 grid arithmetic: rows may be any positive int
   const int splits = rows < kMaxSplits ? rows : kMaxSplits;
-  const int rows_per_split = (rows + splits - 1) / splits;
+  const int64_t rows_per_split = (nrows + splits - 1) / splits;
   const auto* dy_b = static_cast<const __nv_bfloat16*>(dy);
   const auto* h_b = static_cast<const __nv_bfloat16*>(h);
   const auto* w_b = static_cast<const __nv_bfloat16*>(w);
-  dx_kernel<<<(rows + 7) / 8, 256, 0, s>>>(dy_b, h_b, rstd, w_b, static_cast<__nv_bfloat16*>(dx), rows, hidden);
+  const unsigned dx_blocks = static_cast<unsigned>((nrows + 7) / 8);  // <= 2^28, under the grid limit
+  dx_kernel<<<dx_blocks, 256, 0, s>>>(dy_b, h_b, rstd, w_b, static_cast<__nv_bfloat16*>(dx), rows, hidden);
+  if (cudaGetLastError() != cudaSuccess) return kNoAllocLaunchFailed;
   dim3 grid((hidden + 255) / 256, splits);
-  dw_partial_kernel<<<grid, 256, 0, s>>>(dy_b, h_b, rstd, scratch, rows, hidden, rows_per_split);
+  dw_partial_kernel<<<grid, 256, 0, s>>>(dy_b, h_b, rstd, scratch, nrows, hidden, rows_per_split);
+  if (cudaGetLastError() != cudaSuccess) return kNoAllocLaunchFailed;
   dw_reduce_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(scratch, dw, splits, hidden);
   return cudaGetLastError() == cudaSuccess ? kNoAllocOk : kNoAllocLaunchFailed;
 }

@@ -9,13 +9,14 @@
 //   dy, h:  [rows, hidden] bf16, contiguous     rstd: [rows] fp32 (forward 1/RMS)
 //   w:      [hidden] bf16                       dx:   [rows, hidden] bf16 (written)
 //   dw:     [hidden] fp32 (overwritten)         stream: cudaStream_t or null
-//   1 <= hidden <= 16384, hidden % 8 == 0, rows >= 1.
+//   1 <= hidden <= 16384, hidden % 8 == 0, 1 <= rows <= INT_MAX.
 //   Scratch: one 4 MiB file-scope device array per GPU, shared by all calls.
 //   Make the first call on each device (it looks up the scratch address)
 //   before any stream capture begins.  Calls whose kernels overlap on the GPU
 //   race on the scratch; serialise them.  Nothing needs zeroing between calls.
 //   Returns 0 on success; 1 too large (nothing launched), 2 bad argument,
-//   3 setup failed, 4 launch failed.
+//   3 setup failed, 4 launch failed, 5 an earlier CUDA error is pending on this
+//   thread (nothing launched, the error is left in place for the caller).
 #pragma once
 
 #ifdef __cplusplus

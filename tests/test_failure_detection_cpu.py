@@ -207,3 +207,50 @@ def test_checkpoint_retention_counts_complete_only(tmp_path):
     _fake_ckpt(store, "iter_6", 6)
     names = sorted(p.name for p in root.iterdir())
     assert names == ["iter_6"], names  # older complete one pruned after the new marker; stale partial gone
+
+
+class _FlakyStore:
+    """A store whose round trips fail while ``down`` is set (a transient TCPStore timeout)."""
+
+    def __init__(self):
+        self.kv, self.down = {}, False
+
+    def _guard(self):
+        if self.down:
+            raise TimeoutError("store timeout")
+
+    def set(self, k, v):
+        self._guard()
+        self.kv[k] = v.encode() if isinstance(v, str) else v
+
+    def get(self, k):
+        self._guard()
+        return self.kv[k]
+
+    def check(self, keys):
+        self._guard()
+        return all(k in self.kv for k in keys)
+
+
+def test_watchdog_survives_a_transient_store_error():
+    from mvp_engine.distributed.watchdog import HeartbeatWatchdog, PeerFailureError
+
+    store = _FlakyStore()
+    peer = HeartbeatWatchdog(store, 1, 2, interval_s=0.05, timeout_s=0.6)
+    me = HeartbeatWatchdog(store, 0, 2, interval_s=0.05, timeout_s=0.6).start()
+    peer.start()
+    try:
+        time.sleep(0.2)
+        store.down = True  # one short outage, well under the timeout
+        time.sleep(0.2)
+        store.down = False
+        time.sleep(0.3)
+        me.check()  # no peer marked failed
+        store.down = True  # an outage longer than the timeout does end the run
+        time.sleep(1.0)
+        with pytest.raises(PeerFailureError):
+            me.check()
+    finally:
+        store.down = False
+        me.stop()
+        peer.stop()
