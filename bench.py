@@ -320,7 +320,7 @@ def run_ours(args) -> None:
     if dist.is_initialized():
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t.item())
-    fl = torch.tensor([engine.mfu_kit._accumulated_model_flops], device=engine.device, dtype=torch.float64)
+    fl = torch.tensor([engine.mfu_kit.accumulated_model_flops], device=engine.device, dtype=torch.float64)
     if dist.is_initialized():
         dist.all_reduce(fl)
     flops_per_step = float(fl.item()) / args.steps  # logical FLOPs summed over ranks (reference formula)

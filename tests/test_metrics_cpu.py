@@ -79,3 +79,27 @@ def test_distributed_metric_gloo_world2():
     for r in (r0, r1):
         assert r["loss"] == pytest.approx(5.25) and r["tokens"] == 300.0 and r["peak"] == 1.0
     assert r0["mine"] == 0.0 and r1["mine"] == 1.0
+
+
+def test_mfu_kit_formula_and_peaks(monkeypatch):
+    from mvp_engine.kit import MFUKit
+
+    kit = MFUKit()
+    assert kit.normalize_device_name("NVIDIA B200") == "NVIDIA B200"
+    assert kit.normalize_device_name("NVIDIA H100 80GB HBM3") == "NVIDIA H100 SXM"
+    assert kit.normalize_device_name("Some GPU") == "Some GPU" and kit.normalize_device_name(" ") is None
+    assert kit.resolve_peak_tflops(device_type="cpu", precision="bf16", configured_device_name="b200") == \
+        ("NVIDIA B200", 2250.0)
+    assert kit.resolve_peak_tflops(device_type="cpu", precision="bf16") == (None, None)
+    kit.accumulate_microbatch(model_flops=1.0e15)
+    kit.accumulate_microbatch(model_flops=1.25e15)
+    log = kit.build_log(device_type="cpu", precision="bf16", step_time_seconds=2.0, configured_device_name="B200")
+    assert log == {"perf/mfu": pytest.approx(2.25e15 / 2.0 / 2250e12)}
+    assert kit.accumulated_model_flops == 0.0  # the window was consumed
+    assert kit.build_log(model_flops_per_step=1e12, device_type="cpu", precision="int3", step_time_seconds=1.0,
+                         configured_device_name="B200") == {}
+    monkeypatch.setenv("MVP_PEAK_TFLOPS", "1000")
+    assert kit.build_log(model_flops_per_step=1e15, device_type="cpu", precision="bf16",
+                         step_time_seconds=1.0) == {"perf/mfu": pytest.approx(1.0)}
+    with pytest.raises(ValueError):
+        kit.calculate_mfu(model_flops_per_step=1.0, step_time_seconds=0.0, device_peak_tflops=1.0, world_size=1)
