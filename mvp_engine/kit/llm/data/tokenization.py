@@ -1,4 +1,12 @@
-"""Segment tokenisation with per-segment loss flags (reference: mvp_engine/kit/llm/data/tokenization.py:14-55)."""
+"""Segment tokenisation for text samples.
+
+Public API of the reference's ``mvp_engine/kit/llm/data/tokenization.py:14-55``:
+``tokenize(segments)`` returns ``(input_ids, labels, attention_mask)`` chunks of
+at most ``max_seq_len`` tokens.  Behaviour kept: segments are tokenised without
+special tokens; a segment with ``loss=False`` gets ``ignore_index`` labels; one
+EOS token closes a non-empty sample and is supervised when the last segment is.
+Added: ``"tokens"`` segments carry ids already (synthetic and pre-tokenised data).
+"""
 
 from __future__ import annotations
 
@@ -11,9 +19,13 @@ from .types import LLMSegment
 TokenizedFields = tuple[list[int], list[int], list[int]]
 
 
-@dataclass(slots=True)
+def _windows(n: int, size: int) -> range:
+    return range(0, n, size)
+
+
+@dataclass
 class LLMTokenizationHandler:
-    """Tokenise segments, label supervised ones, append EOS, split into ``max_seq_len`` chunks."""
+    """Tokenise segments, mask unsupervised ones, close with EOS, cut into ``max_seq_len`` chunks."""
 
     tokenizer: Any
     max_seq_len: int
@@ -25,35 +37,34 @@ class LLMTokenizationHandler:
             raise ValueError("LLMTokenizationHandler.max_seq_len must be positive.")
 
     def segment_ids(self, seg: LLMSegment) -> list[int]:
-        if seg.type == "tokens":
-            return [int(t) for t in seg.value]
-        if seg.type != "text":
-            raise ValueError(f"Unsupported LLM segment type: {seg.type!r}.")
+        kind = seg.type
+        if kind == "tokens":
+            return list(map(int, seg.value))
+        if kind != "text":
+            raise ValueError(f"Unsupported LLM segment type: {kind!r}.")
         if not isinstance(seg.value, str):
             raise TypeError("LLM text segment value must be a string.")
         return list(self.tokenizer(seg.value, add_special_tokens=False)["input_ids"])
 
+    def _eos(self) -> int:
+        eos = getattr(self.tokenizer, "eos_token_id", None)
+        if eos is None:
+            raise ValueError("Tokenizer has no eos_token_id; required when add_eos=True.")
+        return int(eos)
+
     def tokenize(self, segments: Sequence[LLMSegment]) -> list[TokenizedFields]:
-        ids: list[int] = []
-        labels: list[int] = []
-        for seg in segments:
-            part = self.segment_ids(seg)
-            ids.extend(part)
-            labels.extend(part if seg.loss else [self.ignore_index] * len(part))
-        if self.add_eos and ids:
-            eos = getattr(self.tokenizer, "eos_token_id", None)
-            if eos is None:
-                raise ValueError("Tokenizer has no eos_token_id; required when add_eos=True.")
-            ids.append(int(eos))
-            labels.append(int(eos) if (segments[-1].loss if segments else True) else self.ignore_index)
-        out: list[TokenizedFields] = []
-        for s in range(0, len(ids), self.max_seq_len):
-            chunk = ids[s:s + self.max_seq_len]
-            if chunk:
-                out.append((chunk, labels[s:s + self.max_seq_len], [1] * len(chunk)))
-        return out
+        parts = [(self.segment_ids(seg), bool(seg.loss)) for seg in segments]
+        ids = [t for toks, _ in parts for t in toks]
+        labels = [t if supervised else self.ignore_index for toks, supervised in parts for t in toks]
+        if ids and self.add_eos:
+            eos = self._eos()
+            last_supervised = parts[-1][1] if parts else True
+            ids.append(eos)
+            labels.append(eos if last_supervised else self.ignore_index)
+        n = self.max_seq_len
+        return [(ids[s:s + n], labels[s:s + n], [1] * len(ids[s:s + n])) for s in _windows(len(ids), n)]
 
 
-@dataclass(slots=True)
+@dataclass
 class LLMPretrainTextTokenizationHandler(LLMTokenizationHandler):
-    """Full-token-loss pretraining tokenisation."""
+    """Pretraining: every token supervised (segments come with ``loss=True``)."""
