@@ -66,7 +66,25 @@ def _packs(n: int, seq_len: int, vocab: int, seed: int, rank: int):
     return out
 
 
+# Workloads of bench.py the reference cannot run, with the reason (printed as its `unavailable` line).
+NOT_IN_REFERENCE = {
+    "qwen3-8b-cp-ring": "the reference has no context parallelism (only a 'cp' mesh-role name, "
+                        "mvp_engine/distributed/parallel_mesh.py:15-22; no context mesh field in config/schema.py)",
+    "qwen3-8b-cp-ulysses": "the reference has no context parallelism (only a 'cp' mesh-role name, "
+                           "mvp_engine/distributed/parallel_mesh.py:15-22; no context mesh field in config/schema.py)",
+    "qwen3-32b-tp": "the reference ships no TP_MODULE_CONFIG for Qwen3 (recipes/qwen3 binds none), so its "
+                    "tensor-parallel path cannot shard this model",
+    "qwen3-vl-8b": "the reference's Qwen3-VL recipe loads weights and processor files with from_pretrained "
+                   "(recipes/qwen3_vl/engine/qwen3_vl_engine.py:166-170, kit/mllm/data) and reads a Lance dataset; "
+                   "none of them exist offline",
+}
+
+
 def run(args) -> None:
+    workload = getattr(args, "workload", "qwen3-8b-fsdp")
+    if workload in NOT_IN_REFERENCE:
+        _unavailable(f"workload {workload}: {NOT_IN_REFERENCE[workload]}")
+        return
     if not os.path.isdir(os.path.join(REF, "mvp_engine")):
         _unavailable("reference not installed: run baseline/install_reference.sh (pip --no-deps into baseline/_ref)")
         return
