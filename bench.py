@@ -238,10 +238,15 @@ def run_ours(args) -> None:
     H, F, L = cfgm.hidden_size, cfgm.intermediate_size, cfgm.num_hidden_layers
     qkv = (cfgm.num_attention_heads + 2 * cfgm.num_key_value_heads) * cfgm.head_dim
     local_tokens = args.seq_len // cp  # context ranks hold 1/cp of the row
-    # saved per token and layer (bf16): norms / residuals, qkv, q + k, attention output and the
-    # SwiGLU input (the activation itself is recomputed in the backward)
-    per_layer = local_tokens * 2 * (6 * H + qkv + (cfgm.num_attention_heads + cfgm.num_key_value_heads) *
-                                    cfgm.head_dim + 2 * F) * 1.1
+    # saved per token and layer (bf16): the two residual sums, qkv, the attention output and the SwiGLU
+    # input.  The normalised GEMM inputs, the normalised + rotated q / k and the SwiGLU activation are
+    # recomputed in the backward (single-rank, data-parallel and ring layers); the tensor-parallel and
+    # Ulysses layers keep the norm outputs and q / k as well.
+    plain = tp == 1 and wl.get("cp") != "ulysses"
+    kept = 4 * H + qkv + 2 * F
+    if not plain:
+        kept += 2 * H + (cfgm.num_attention_heads + cfgm.num_key_value_heads) * cfgm.head_dim
+    per_layer = local_tokens * 2 * kept * 1.1
     head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
     # 10 GiB of slack; the multimodal workload also keeps the vision tower's per-block checkpoint inputs,
     # the image embeddings and a block's recomputed activations, which vary with the images of a pack

@@ -107,6 +107,10 @@ class BaseBackendKwargsConfig(BaseModel):
     ddp: BaseDDPConfig = Field(default_factory=BaseDDPConfig)
     context_parallel: ContextParallelConfig = Field(default_factory=ContextParallelConfig)
     comm: CommConfig = Field(default_factory=CommConfig)
+    # native runtime: free each decoder block's full weights after use and gather them again when needed
+    # (FSDP2's reshard_after_forward).  None: keep them resident unless they would take more than a fifth
+    # of the device's memory.
+    reshard_after_forward: Optional[bool] = None
 
 
 class BaseParallelConfig(BaseModel):

@@ -69,10 +69,15 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
         shard_mesh = dp.mesh if dp.active else None
         if shard_mesh is not None and len(dp.dim_names) > 1:
             shard_mesh = parallel_mesh.device_mesh[dp.dim_names]._flatten("_".join(dp.dim_names))
-        logger.info(f"Wrapping {type(model).__name__} with native flat FSDP over {dp.world_size} rank(s)...")
+        reshard = kw.get("reshard_after_forward")
+        if reshard is None and dev.type == "cuda" and dp.world_size > 1:
+            full_bytes = sum(p.numel() for p in model.parameters()) * 2
+            reshard = full_bytes > 0.2 * torch.cuda.get_device_properties(dev).total_memory
+        logger.info(f"Wrapping {type(model).__name__} with native flat FSDP over {dp.world_size} rank(s)"
+                    f"{' (weights resharded after use)' if reshard else ''}...")
         return NativeFSDP(model, group=dp.group, device=dev, param_dtype=param_dtype,
                           comm="fused" if comm_cfg.get("fused", True) else "nccl", shard_mesh=shard_mesh,
-                          tp_group=tp.group if tp.active else None)
+                          tp_group=tp.group if tp.active else None, reshard_after_forward=bool(reshard))
 
     if not shard_active and not tp.active:
         from torch.nn.parallel import DistributedDataParallel

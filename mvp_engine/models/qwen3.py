@@ -68,22 +68,23 @@ class Qwen3Config:
         return cfg
 
 
-# Architecture presets (public HF configs), used when no local config.json exists.
+# Architecture presets (public HF configs), used when no local config.json exists.  Every Qwen3 size
+# uses 128-dim heads, which for several sizes is not hidden_size / heads.
 QWEN3_PRESETS: dict[str, dict] = {
     "Qwen/Qwen3-0.6B": dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
-                            num_key_value_heads=8, tie_word_embeddings=True, max_position_embeddings=40960),
+                            num_key_value_heads=8, head_dim=128, tie_word_embeddings=True, max_position_embeddings=40960),
     "Qwen/Qwen3-1.7B": dict(hidden_size=2048, intermediate_size=6144, num_hidden_layers=28, num_attention_heads=16,
-                            num_key_value_heads=8, tie_word_embeddings=True, max_position_embeddings=40960),
+                            num_key_value_heads=8, head_dim=128, tie_word_embeddings=True, max_position_embeddings=40960),
     "Qwen/Qwen3-4B": dict(hidden_size=2560, intermediate_size=9728, num_hidden_layers=36, num_attention_heads=32,
-                          num_key_value_heads=8, tie_word_embeddings=True, max_position_embeddings=40960),
+                          num_key_value_heads=8, head_dim=128, tie_word_embeddings=True, max_position_embeddings=40960),
     "Qwen/Qwen3-8B": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
-                          num_key_value_heads=8, max_position_embeddings=40960),
+                          num_key_value_heads=8, head_dim=128, max_position_embeddings=40960),
     "Qwen/Qwen3-8B-Base": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
-                               num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=32768),
+                               num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=32768),
     "Qwen/Qwen3-14B": dict(hidden_size=5120, intermediate_size=17408, num_hidden_layers=40, num_attention_heads=40,
-                           num_key_value_heads=8, max_position_embeddings=40960),
+                           num_key_value_heads=8, head_dim=128, max_position_embeddings=40960),
     "Qwen/Qwen3-32B": dict(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64, num_attention_heads=64,
-                           num_key_value_heads=8, max_position_embeddings=40960),
+                           num_key_value_heads=8, head_dim=128, max_position_embeddings=40960),
     # tiny configs for tests and smoke runs
     "mvp/qwen3-tiny": dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                            num_attention_heads=4, num_key_value_heads=2, head_dim=128,
@@ -175,13 +176,15 @@ class Qwen3DecoderLayer(nn.Module):
         """
         attn = self.self_attn
         tp = getattr(self, "_tp", None)  # tensor-parallel runtime (column / row-parallel shards)
+        Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
+        cp = ctx.cp
+        if tp is None and (cp is None or not cp.ulysses_fused(x, Hq, Hkv, D)):
+            return self._forward_plain(x, residual, ctx)
         if residual is None:
             hn = self.input_layernorm(x)
             h = x
         else:
             hn, h = self.input_layernorm(x, residual)
-        Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
-        cp = ctx.cp
         if tp is None and cp is not None and cp.ulysses_fused(hn, Hq, Hkv, D):
             # context parallel (Ulysses) with the all-to-alls fused into the producing kernels
             o = cp.ulysses_block(hn, self.fused_weight("qkv", hn), _as_compute(attn.q_norm.weight, hn),
@@ -213,6 +216,30 @@ class Qwen3DecoderLayer(nn.Module):
         else:  # the activation is recomputed in the backward instead of being kept
             out = ops.swiglu_linear(gu, wd)
         return out, h2
+
+
+    def _forward_plain(self, x: torch.Tensor, residual: Optional[torch.Tensor], ctx: "PackedContext"):
+        """Single-rank / data-parallel / ring-CP layer: each RMSNorm and the GEMM it feeds are one autograd
+        node that keeps the residual sum, not the normalised rows (``ops.rms_norm_linear``)."""
+        attn = self.self_attn
+        Hq, Hkv, D = attn.num_heads, attn.num_kv_heads, attn.head_dim
+        ln1, ln2 = self.input_layernorm, self.post_attention_layernorm
+        qkv, h = ops.rms_norm_linear(x, _as_compute(ln1.weight, x), self.fused_weight("qkv", x),
+                                     ln1.variance_epsilon, residual=residual)
+        wq, wk = _as_compute(attn.q_norm.weight, x), _as_compute(attn.k_norm.weight, x)
+        if ctx.cp is None and ctx.causal:  # one autograd node: all of q/k/v's gradients land in one dqkv buffer
+            o = ops.qk_norm_rope_attention(qkv, Hq, Hkv, wq, wk, ctx.position_ids, ctx.rope,
+                                           attn.q_norm.variance_epsilon, ctx.cu_seqlens, ctx.max_seqlen,
+                                           attn.scaling)
+        else:
+            q, k = ops.qk_norm_rope(qkv, Hq, Hkv, wq, wk, ctx.position_ids, ctx.rope, attn.q_norm.variance_epsilon)
+            v = qkv[:, (Hq + Hkv) * D:].view(-1, Hkv, D)
+            o = ctx.attention(q, k, v, attn.scaling)
+        o = ops.linear(o.reshape(o.shape[0], Hq * D), _as_compute(attn.o_proj.weight, x))
+        gu, h2 = ops.rms_norm_linear(o, _as_compute(ln2.weight, o), self.fused_weight("gate_up", o),
+                                     ln2.variance_epsilon, residual=h)
+        # the SwiGLU activation is recomputed in the backward instead of being kept
+        return ops.swiglu_linear(gu, _as_compute(self.mlp.down_proj.weight, gu)), h2
 
 
 @dataclass

@@ -30,6 +30,7 @@ __all__ = [
     "gemm",
     "linear",
     "rms_norm",
+    "rms_norm_linear",
     "qk_norm_rope",
     "qk_norm_rope_attention",
     "RopeCache",
@@ -177,6 +178,70 @@ class _RMSNorm(torch.autograd.Function):
         return dx, dw, (dx if ctx.has_res else None), None
 
 
+class _NormLinear(torch.autograd.Function):
+    """``(rmsnorm(x + residual) * w_norm) @ w_lin^T`` plus the sum ``h = x + residual``, keeping only
+    ``h`` and the row scales for the backward.
+
+    The normalised rows (the GEMM's input) are not held from forward to backward: the backward
+    recomputes them from ``h`` in one bandwidth-bound pass before the weight-gradient GEMM.  Decoder
+    layers use this for the input and post-attention norms; the activation memory saved lets more
+    layers skip activation checkpointing."""
+
+    @staticmethod
+    def forward(ctx, x, residual, w_norm, w_lin, eps):
+        shape = x.shape
+        H = shape[-1]
+        x2 = x.reshape(-1, H).contiguous()
+        r2 = residual.reshape(-1, H).contiguous() if residual is not None else None
+        ext = _ext.ext()
+        outs = ext.rmsnorm_fwd(x2, r2, w_norm, eps)
+        hn, rstd = outs[0], outs[1]
+        h = outs[2] if residual is not None else x2
+        y = gemm(hn, w_lin)
+        ctx.save_for_backward(h, rstd, w_norm, w_lin)
+        ctx.accs = (grad_acc(w_norm), grad_acc(w_lin))
+        ctx.has_res = residual is not None
+        ctx.shape = shape
+        ctx.eps = eps
+        return y.view(*shape[:-1], w_lin.shape[0]), h.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy, dh):
+        h, rstd, w_norm, w_lin = ctx.saved_tensors
+        acc_n, acc_l = ctx.accs
+        H = ctx.shape[-1]
+        ext = _ext.ext()
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        hn = ext.rmsnorm_fwd(h, None, w_norm, ctx.eps)[0]  # the GEMM input, recomputed
+        dw_lin = None
+        if acc_l is not None or ctx.needs_input_grad[3]:
+            dw_lin = _wgrad(dy2, hn, w_lin, acc_l)
+        del hn
+        dhn = gemm(dy2, w_lin, b_mn=True)
+        dh2 = dh.reshape(-1, H).contiguous() if dh is not None else None
+        acc = acc_n if (acc_n is not None and acc_n.is_contiguous() and acc_n.dtype == torch.float32) else None
+        outs = ext.rmsnorm_bwd(dhn, h, rstd, w_norm, dh2, True, dw_acc=acc)
+        dx = outs[0].view(ctx.shape)
+        if acc is not None:
+            dw_norm = None
+        elif acc_n is not None:
+            acc_n.add_(outs[1])
+            dw_norm = None
+        else:
+            dw_norm = outs[1].to(w_norm.dtype)
+        return dx, (dx if ctx.has_res else None), dw_norm, dw_lin, None
+
+
+def rms_norm_linear(x: torch.Tensor, w_norm: torch.Tensor, w_lin: torch.Tensor, eps: float,
+                    residual: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(linear(rmsnorm(h) * w_norm, w_lin), h)`` with ``h = x + residual`` (or ``x``), without keeping the
+    normalised rows for the backward (see :class:`_NormLinear`)."""
+    if not _native(x) or x.dtype != torch.bfloat16 or w_lin.dtype != torch.bfloat16:
+        y, h = rms_norm(x, w_norm, eps, residual=residual)
+        return linear(y, w_lin), h
+    return _NormLinear.apply(x, residual, w_norm, w_lin, float(eps))
+
+
 def _rms_norm_eager(x, w, eps):
     xf = x.float()
     var = xf.pow(2).mean(-1, keepdim=True)
@@ -293,18 +358,22 @@ class _QKNormRopeAttention(torch.autograd.Function):
         q, k, rstd = ext.qk_norm_rope_fwd(qkv, hq, hkv, wq, wk, pos, axis, cos_t, sin_t, eps)
         v = qkv[:, (hq + hkv) * D:].view(qkv.shape[0], hkv, D)
         o, lse = ext.flash_attn_fwd(q, k, v, cu, scale, causal, _ext.status_buffer(q.device).data_ptr())
-        ctx.save_for_backward(qkv, wq, wk, pos, rstd, q, k, o, lse, cu)
-        ctx.meta = (hq, hkv, cache, scale, causal)
+        # q and k (5/6 of qkv's size) are not kept: the backward recomputes them from qkv in one
+        # bandwidth-bound pass, which lets more decoder layers skip activation checkpointing.
+        ctx.save_for_backward(qkv, wq, wk, pos, rstd, o, lse, cu)
+        ctx.meta = (hq, hkv, cache, scale, causal, float(eps))
         ctx.accs = (grad_acc(wq), grad_acc(wk))
         return o
 
     @staticmethod
     def backward(ctx, do):
-        qkv, wq, wk, pos, rstd, q, k, o, lse, cu = ctx.saved_tensors
-        hq, hkv, cache, scale, causal = ctx.meta
+        qkv, wq, wk, pos, rstd, o, lse, cu = ctx.saved_tensors
+        hq, hkv, cache, scale, causal, eps = ctx.meta
         D = cache.head_dim
         T = qkv.shape[0]
         ext = _ext.ext()
+        cos_f, sin_f, axis_f = cache.tables(qkv.device)
+        q, k, _ = ext.qk_norm_rope_fwd(qkv, hq, hkv, wq, wk, pos, axis_f, cos_f, sin_f, eps)
         dqkv = torch.empty_like(qkv)
         v = qkv[:, (hq + hkv) * D:].view(T, hkv, D)
         dk_buf = torch.empty(T, hkv, D, dtype=qkv.dtype, device=qkv.device)
@@ -740,6 +809,19 @@ def peer_reduce_scatter(peer_bufs: list[int], peer_slots: list[int], my_slots: i
     peers' symmetric buffers, after every rank has published sequence number ``seq`` (bounded wait)."""
     _ext.ext().peer_reduce_scatter(peer_bufs, peer_slots, my_slots, rank, offset, shard, seq, scale, out, sumsq,
                                    _ext.status_buffer(out.device).data_ptr(), int(timeout_s * 1e9))
+
+
+def peer_gather_shards(peer_bufs: list[int], peer_flags: list[int], rank: int, offset: int, shard: int, epoch: int,
+                       out: torch.Tensor, timeout_s: float = 10.0) -> None:
+    """``out[r*shard:(r+1)*shard] = bf16 shard r`` read from rank r's symmetric buffer at element ``offset``,
+    once every rank has published ``epoch`` (bounded wait): the FSDP parameter gather by pulling."""
+    _ext.ext().peer_gather_shards(peer_bufs, peer_flags, offset, shard, epoch, out,
+                                  _ext.status_buffer(out.device).data_ptr(), int(timeout_s * 1e9))
+
+
+def publish_epoch(flag_ptr: int, epoch: int) -> None:
+    """Stream-ordered system-scope release of ``epoch`` into this rank's flag (after the kernels before it)."""
+    _ext.ext().publish_epoch(int(flag_ptr), int(epoch))
 
 
 def peer_barrier(peer_slots: list[int], my_slots: int, rank: int, seq: int, timeout_s: float = 10.0) -> None:

@@ -462,3 +462,60 @@ void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std
       p, slots.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ----------------------------------------------------------------------------
+// FSDP parameter gather (resharded units): stand-alone launch of the shard pull, and the epoch
+// publication that tells the peers this rank's shards are final for the coming step.
+namespace mvp {
+namespace comm {
+
+__global__ void __launch_bounds__(256) shard_gather_kernel(ShardGather g, int* status) {
+  __shared__ int flag;
+  shard_gather_cta(g, blockIdx.x, status, &flag);
+}
+
+__global__ void publish_epoch_kernel(unsigned long long* flag, unsigned long long epoch) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // the optimizer's shard writes (earlier kernels) before the flag
+    st_release_sys(flag, epoch);
+  }
+}
+
+}  // namespace comm
+}  // namespace mvp
+
+void peer_gather_shards(const std::vector<int64_t>& peer_bufs, const std::vector<int64_t>& peer_flags,
+                        int64_t offset, int64_t shard, int64_t epoch, torch::Tensor& out, int64_t status_ptr,
+                        int64_t timeout_ns) {
+  using namespace mvp;
+  const int world = static_cast<int>(peer_bufs.size());
+  TORCH_CHECK(world >= 1 && world <= kMaxGatherRanks && static_cast<int>(peer_flags.size()) == world,
+              "peer_gather_shards: 1..8 ranks, one flag per rank");
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.element_size() == 2 && out.numel() == world * shard,
+              "peer_gather_shards: contiguous 16-bit output of world x shard elements");
+  TORCH_CHECK((shard * 2) % 16 == 0 && (offset * 2) % 16 == 0, "peer_gather_shards: 16-byte aligned shards");
+  ShardGather g{};
+  for (int r = 0; r < world; ++r) {
+    g.src[r] = reinterpret_cast<const uint4*>(peer_bufs[r] + offset * 2);
+    g.flags[r] = reinterpret_cast<const unsigned long long*>(peer_flags[r]);
+  }
+  g.dst = reinterpret_cast<uint4*>(out.data_ptr());
+  g.n16 = shard * 2 / 16;
+  g.world = world;
+  g.epoch = static_cast<unsigned long long>(epoch);
+  g.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+  // One CTA per SM at most: the copy runs on the comm stream beside the compute kernels and needs
+  // no shared memory, so it co-resides with them; 148 x 256 threads x 8 x 16 B keeps ~4.8 MB in flight.
+  const int64_t total = g.n16 * world;
+  g.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(148, (total + 2047) / 2048)));
+  const at::cuda::CUDAGuard guard(out.device());
+  mvp::comm::shard_gather_kernel<<<g.ctas, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      g, reinterpret_cast<int*>(status_ptr));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void publish_epoch(int64_t flag_ptr, int64_t epoch) {
+  mvp::comm::publish_epoch_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<unsigned long long*>(flag_ptr), static_cast<unsigned long long>(epoch));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

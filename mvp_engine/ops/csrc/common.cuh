@@ -271,6 +271,65 @@ struct PeerPull {
   int rows;  // grid rows given to the copy (0: no copy)
 };
 
+// FSDP parameter gather by pulling: the full weights of one unit are rebuilt in this GPU's staging
+// slot from every rank's bf16 shard, read straight out of the ranks' symmetric shard buffers (rank r's
+// shard lands at r * n16).  Each rank publishes an epoch into its own flag after its optimizer step has
+// written its shard; a copy CTA waits (bounded) until every rank's epoch reaches `epoch`, so a rank
+// that runs ahead never reads a peer's shard of the previous step.  Shards do not change between
+// two optimizer steps, so nothing else needs ordering: the copy is safe at any point of the step.
+constexpr int kMaxGatherRanks = 8;
+struct ShardGather {
+  const uint4* src[kMaxGatherRanks];                 // rank r's shard of the unit (peer mapping; own: local)
+  const unsigned long long* flags[kMaxGatherRanks];  // rank r's published epoch
+  uint4* dst;                                        // the unit's full buffer in this GPU's staging slot
+  int64_t n16;                                       // 16-byte units per shard
+  int world;
+  unsigned long long epoch;
+  unsigned long long timeout_ns;
+  int ctas;  // CTAs that carry the copy (0: no copy)
+};
+
+// One copy CTA of `g`: CTA `cta` of g.ctas copies every (g.ctas)-th chunk (all threads call it).
+__device__ __forceinline__ void shard_gather_cta(const ShardGather& g, int cta, int* status, int* flag) {
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < g.world && ok; ++r) {
+      while (ld_acquire_sys(g.flags[r]) < g.epoch) {
+        if (globaltimer() - t0 > g.timeout_ns) {
+          record_status(status, kTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    *flag = ok;
+  }
+  __syncthreads();
+  if (!*flag) return;
+  constexpr int kUnroll = 8;  // 16-byte loads in flight per thread: covers the NVLink round trip
+  const int64_t total = g.n16 * g.world;
+  const int64_t stride = static_cast<int64_t>(g.ctas) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(cta) * blockDim.x + threadIdx.x; i0 < total; i0 += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < total) {
+        const int64_t r = i / g.n16;
+        v[u] = g.src[r][i - r * g.n16];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < total) g.dst[i] = v[u];
+    }
+  }
+}
+
 // Body of one copy CTA (all threads of the CTA call it; `flag` is one int of shared memory).
 __device__ __forceinline__ void peer_pull_cta(const PeerPull& j, int* status, int* flag) {
   if (threadIdx.x == 0) {

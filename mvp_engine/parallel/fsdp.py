@@ -21,15 +21,29 @@ Because shards are contiguous slices of the full layout, the parameter
 all-gather is an in-place ``all_gather_into_tensor`` into ``full`` and the
 gradient reduce-scatter reads ``grad`` as is: no copy-in / copy-out kernels.
 The optimizer writes its bf16 output straight into this rank's slice of
-``full``.  Full weights stay resident between steps (``reshard_after_forward``
-is not needed at the memory budget of a 180 GB B200), so each parameter crosses
-NVLink once per optimizer step, not twice per micro-batch.
+``full``.  By default full weights stay resident between steps, so each
+parameter crosses NVLink once per optimizer step, not twice per micro-batch;
+that is the fast mode whenever the 180 GB of a B200 hold them.
 
 Overlap.  Gradient reduce-scatter of a unit starts on a side stream as soon as
 that unit's backward finishes (a hook on the unit's inputs), only on the
 micro-batch that syncs.  Parameter all-gathers of the next step are issued per
 unit in forward order right after the optimizer step; each unit's forward
 waits only for its own gather.
+
+Resharding (``reshard_after_forward=True``, FSDP2's option of that name,
+reference: mvp_engine/distributed/fsdp2.py:82-167).  Decoder units then keep only
+this rank's bf16 slice (``wshard``) between uses; their full weights live in one
+of two staging slots (units alternate) only while the unit runs, in forward and
+again in backward.  Each unit's gather is issued one unit ahead on the comm
+stream (the next unit in forward, the previous one in backward), after an event
+that orders it behind the last kernel that read the slot, so it overlaps the
+current unit's compute.  The gather is NCCL's all-gather (``comm="nccl"``) or the
+engine's peer pull (``comm="fused"``): every rank reads the other ranks' slices
+straight out of their symmetric shard buffers.  The root unit (embeddings, final
+norm, LM head) stays resident.  Gradients accumulate in the full-size fp32 buffer
+across micro-batches and are reduce-scattered on the syncing micro-batch, as
+torch FSDP2 does when gradient sync is off between micro-batches.
 
 Checkpoints.  ``checkpoint_state_dict`` returns HF-named tensors; on more than
 one rank they are DTensors with ``Shard(0)`` placements over the shard mesh,
@@ -96,11 +110,21 @@ class FlatUnit:
     rs_event: Optional[torch.cuda.Event] = None
     rs_pending: bool = False
     views: dict[str, torch.Tensor] = field(default_factory=dict)
+    resharded: bool = False  # full weights only while the unit runs (staging slot), else wshard
+    slot: int = -1
+    wshard: Optional[torch.Tensor] = None  # this rank's bf16 slice when resharded
     rep_end: int = 0  # entries [0, rep_end) are tensor-parallel partial (summed over the tensor group)
     repl_end: int = 0  # entries [0, repl_end) are replicated over the tensor group (partial or complete)
 
     def local_range(self, rank: int) -> tuple[int, int]:
         return rank * self.shard, (rank + 1) * self.shard
+
+    def own_compute_slice(self, rank: int) -> torch.Tensor:
+        """Where this rank's bf16 weights live between steps (the optimizer writes here)."""
+        if self.resharded:
+            return self.wshard
+        lo, hi = self.local_range(rank)
+        return self.full[lo:hi]
 
 
 class _UnitBackwardHook(torch.autograd.Function):
@@ -115,6 +139,21 @@ class _UnitBackwardHook(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         ctx.owner._on_unit_backward_done(ctx.unit_index)
+        return (None, None) + grads
+
+
+class _UnitBackwardStartHook(torch.autograd.Function):
+    """Identity on the unit's outputs; its backward runs before any op of the unit's backward."""
+
+    @staticmethod
+    def forward(ctx, owner, unit_index, *xs):
+        ctx.owner = owner
+        ctx.unit_index = unit_index
+        return xs if len(xs) > 1 else xs[0]
+
+    @staticmethod
+    def backward(ctx, *grads):
+        ctx.owner._on_unit_backward_start(ctx.unit_index)
         return (None, None) + grads
 
 
@@ -142,8 +181,14 @@ class NativeFSDP(nn.Module):
     def __init__(self, model: nn.Module, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, param_dtype: Any = torch.bfloat16,
                  unit_classes: Optional[Iterable[str]] = None, comm: str = "nccl",
-                 shard_mesh: Any = None, tp_group: Optional[dist.ProcessGroup] = None) -> None:
+                 shard_mesh: Any = None, tp_group: Optional[dist.ProcessGroup] = None,
+                 reshard_after_forward: bool = False) -> None:
         super().__init__()
+        self.reshard_after_forward = bool(reshard_after_forward)
+        self._slots: list[torch.Tensor] = []
+        self._slot_owner = [-1, -1]  # unit index whose full weights each staging slot holds (-1: none)
+        self._phase = "forward"
+        self._wpeer = None  # symmetric bf16 shard buffer for the peer-pull gather
         self.module = model
         self.group = group
         self.tp_group = tp_group
@@ -246,6 +291,7 @@ class NativeFSDP(nn.Module):
             u.padded = max(quantum, int(math.ceil(off / quantum) * quantum))
             u.shard = u.padded // self.world
         self._peer = self._setup_peer_collectives()
+        self._plan_resharding()
         for u in self.units:
             self._materialise(u, {id(e): params[by_entry[id(e)]] for e in u.entries})
 
@@ -297,13 +343,66 @@ class NativeFSDP(nn.Module):
                         "using NCCL reduce-scatter", level="warning")
             return None
 
+    def _plan_resharding(self) -> None:
+        """Pick the resharded units (trainable decoder blocks), give each a staging slot (alternating in
+        forward order) and its bf16 shard; allocate two slots of the largest such unit."""
+        if not self.reshard_after_forward or self.world == 1:
+            return
+        chosen = [u for u in self.units if u.module is not None and u.trainable and "<frozen>" not in u.name]
+        if len(chosen) < 2:
+            return
+        for k, u in enumerate(chosen):
+            u.resharded, u.slot = True, k % 2
+        biggest = max(u.padded for u in chosen)
+        self._slots = [torch.zeros(biggest, dtype=self.param_dtype, device=self.device) for _ in range(2)]
+        total = sum(u.shard for u in chosen)
+        self._wshard_base = self._alloc_weight_shards(total)
+        off = 0
+        self._wshard_off: dict[int, int] = {}
+        for u in chosen:
+            u.wshard = self._wshard_base[off:off + u.shard]
+            self._wshard_off[u.index] = off
+            off += u.shard
+
+    def _alloc_weight_shards(self, total: int) -> torch.Tensor:
+        """bf16 shard storage of the resharded units: symmetric (peer-readable) memory for the pull gather."""
+        if self.comm == "fused" and self.device.type == "cuda" and 1 < self.world <= 8 and \
+                os.environ.get("MVP_FUSED_COMM", "1") != "0":
+            try:
+                import torch.distributed._symmetric_memory as symm
+
+                group = self.group if self.group is not None else dist.group.WORLD
+                buf = symm.empty(max(total, 8), dtype=self.param_dtype, device=self.device)
+                buf.zero_()
+                flags = symm.empty(8, dtype=torch.int64, device=self.device)
+                flags.zero_()
+                torch.cuda.synchronize(self.device)
+                h_buf = symm.rendezvous(buf, group)
+                h_flags = symm.rendezvous(flags, group)
+                h_flags.barrier()
+                self._wpeer = dict(buf=buf, flags=flags, handles=(h_buf, h_flags),
+                                   bufs=[int(x) for x in h_buf.buffer_ptrs],
+                                   flag_ptrs=[int(x) for x in h_flags.buffer_ptrs], epoch=0)
+                return buf[:total]
+            except Exception as exc:  # noqa: BLE001 - fall back to NCCL all-gathers, loudly
+                from ..utils.log import simple_info
+
+                simple_info(f"native FSDP: peer-pull parameter gather unavailable ({type(exc).__name__}: {exc}); "
+                            "using NCCL all-gather", level="warning")
+                self._wpeer = None
+        return torch.zeros(total, dtype=self.param_dtype, device=self.device)
+
     def _next_seq(self) -> int:
         self._seq = getattr(self, "_seq", 0) + 1
         return self._seq
 
     def _materialise(self, u: FlatUnit, src: dict[int, torch.Tensor]) -> None:
         dev = self.device
-        u.full = torch.zeros(u.padded, dtype=self.param_dtype, device=dev)
+        if u.resharded:
+            u.full = self._slots[u.slot][:u.padded]
+            u.full.zero_()
+        else:
+            u.full = torch.zeros(u.padded, dtype=self.param_dtype, device=dev)
         lo, hi = u.local_range(self.rank)
         if u.trainable:
             u.master = torch.zeros(u.shard, dtype=torch.float32, device=dev)
@@ -351,6 +450,10 @@ class NativeFSDP(nn.Module):
             u.views[e.fqns[0]] = view
         if u.module is not None:
             self._publish_fused(u)
+        if u.resharded:  # keep this rank's slice; the slot is shared with every other unit of its parity
+            with torch.no_grad():
+                u.wshard.copy_(u.full[lo:hi])
+            self._slot_owner[u.slot] = u.index
 
     def _publish_fused(self, u: FlatUnit) -> None:
         """Expose contiguous q/k/v and gate/up as single GEMM operands when laid out back to back."""
@@ -376,16 +479,56 @@ class NativeFSDP(nn.Module):
 
     # ------------------------------------------------------------ hooks
     def _install_hooks(self) -> None:
+        self._resharded_order = [u.index for u in self.units if u.resharded]
         for u in self.units[1:]:
             if u.module is None or "<frozen>" in u.name:
                 continue
             u.module.register_forward_pre_hook(self._make_pre_hook(u.index), with_kwargs=False)
+            if u.resharded:
+                u.module.register_forward_hook(self._make_post_hook(u.index))
+
+    def _make_post_hook(self, idx: int) -> Callable:
+        """Wrap a resharded unit's outputs so its backward first brings the unit's weights back."""
+
+        def hook(module, args, output):
+            if not torch.is_grad_enabled() or not self.module.training:
+                return None
+            outs = output if isinstance(output, tuple) else (output,)
+            live = [o for o in outs if isinstance(o, torch.Tensor) and o.requires_grad]
+            if not live:
+                return None
+            wrapped = _UnitBackwardStartHook.apply(self, idx, *live)
+            wrapped = wrapped if isinstance(wrapped, tuple) else (wrapped,)
+            it = iter(wrapped)
+            res = tuple(next(it) if (isinstance(o, torch.Tensor) and o.requires_grad) else o for o in outs)
+            return res if isinstance(output, tuple) else res[0]
+
+        return hook
+
+    def _neighbour(self, idx: int, step: int) -> Optional[int]:
+        order = self._resharded_order
+        k = order.index(idx) + step
+        return order[k] if 0 <= k < len(order) else None
+
+    def _on_unit_backward_start(self, idx: int) -> None:
+        self._phase = "backward"
+        self._ensure_gathered(idx)
+        self._wait_gather(idx)
+        prev = self._neighbour(idx, -1)
+        if prev is not None:
+            self._ensure_gathered(prev)  # prefetch: overlaps this unit's backward
 
     def _make_pre_hook(self, idx: int) -> Callable:
         def hook(module, args):
+            if self.units[idx].resharded:
+                self._ensure_gathered(idx)
             self._wait_gather(idx)
             for sib in self._siblings(idx):
                 self._wait_gather(sib)
+            if self.units[idx].resharded and self._phase == "forward":
+                nxt = self._neighbour(idx, +1)
+                if nxt is not None:
+                    self._ensure_gathered(nxt)  # prefetch: overlaps this unit's forward
             if not torch.is_grad_enabled() or not self.module.training:
                 return None
             tensors = [a for a in args if isinstance(a, torch.Tensor) and a.requires_grad]
@@ -413,8 +556,19 @@ class NativeFSDP(nn.Module):
             torch.cuda.current_stream(self.device).wait_event(ev)
             self.units[idx].ag_event = None
 
+    def _ensure_gathered(self, idx: int) -> None:
+        """Issue the gather of resharded unit ``idx`` into its slot unless the slot already holds it."""
+        u = self.units[idx]
+        if self._slot_owner[u.slot] == idx:
+            return
+        self._slot_owner[u.slot] = idx
+        self._gather(u)
+
     def _gather(self, u: FlatUnit) -> None:
         if self.world == 1:
+            return
+        if u.resharded:
+            self._gather_resharded(u)
             return
         lo, hi = u.local_range(self.rank)
         if self._comm_stream is not None:
@@ -432,14 +586,59 @@ class NativeFSDP(nn.Module):
             with torch.no_grad():
                 u.full.copy_(torch.cat(parts))
 
+    def _gather_resharded(self, u: FlatUnit) -> None:
+        """Full weights of ``u`` into its staging slot from every rank's bf16 shard.
+
+        On the comm stream, behind an event of the compute stream: every kernel issued so far (the last
+        reader of this slot among them) is ordered before the copy; the unit's own ops wait for
+        ``u.ag_event``."""
+        cur = torch.cuda.current_stream(self.device) if self._comm_stream is not None else None
+        # Saved tensors of the unit's earlier use (forward, for its backward) are views of this slot: the
+        # refill restores exactly those values, so the slot's version counter is kept as it was.
+        keep_version = torch.autograd._unsafe_preserve_version_counter(self._slots[u.slot])
+        if cur is None:  # CPU / gloo: synchronous
+            parts = [torch.empty(u.shard, dtype=u.full.dtype) for _ in range(self.world)]
+            dist.all_gather(parts, u.wshard.detach().clone(), group=self.group)
+            with torch.no_grad(), keep_version:
+                u.full.copy_(torch.cat(parts))
+            return
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self._comm_stream.wait_event(ev)
+        with torch.cuda.stream(self._comm_stream), torch.no_grad(), keep_version:
+            if self._wpeer is not None:
+                from .. import ops as _ops
+
+                wp = self._wpeer
+                off = self._wshard_off[u.index]
+                _ops.peer_gather_shards(wp["bufs"], wp["flag_ptrs"], self.rank, off, u.shard, wp["epoch"], u.full)
+            else:
+                dist.all_gather_into_tensor(u.full, u.wshard, group=self.group)
+            u.ag_event = torch.cuda.Event()
+            u.ag_event.record(self._comm_stream)
+
     @torch.no_grad()
     def _gather_all(self, initial: bool = False) -> None:
         for u in self.units:
             if initial and self.world > 1 and u.trainable:
                 # masters were copied from the full init; refresh this rank's slice
-                lo, hi = u.local_range(self.rank)
-                u.full[lo:hi].copy_(u.master.detach())
+                u.own_compute_slice(self.rank).copy_(u.master.detach())
+            if u.resharded:
+                continue  # gathered on first use
             self._gather(u)
+        if self._slots:
+            self._slot_owner = [-1, -1]
+            self._publish_weight_epoch()
+
+    def _publish_weight_epoch(self) -> None:
+        """Tell the peers that this rank's bf16 shards are final for the coming step (peer-pull gather)."""
+        if self._wpeer is None:
+            return
+        from .. import ops as _ops
+
+        wp = self._wpeer
+        wp["epoch"] += 1
+        _ops.publish_epoch(int(wp["flags"].data_ptr()), wp["epoch"])
 
     def _reduce_scatter(self, idx: int) -> None:
         u = self.units[idx]
@@ -496,6 +695,7 @@ class NativeFSDP(nn.Module):
         self._sync_grads = bool(requires_gradient_sync)
 
     def forward(self, *args, **kwargs):
+        self._phase = "forward"
         self._wait_gather(0)
         for sib in self._siblings(0):
             self._wait_gather(sib)
@@ -565,8 +765,7 @@ class NativeFSDP(nn.Module):
             with torch.no_grad():
                 for u in self.units:
                     if u.trainable:
-                        lo, hi = u.local_range(self.rank)
-                        u.full[lo:hi].copy_(u.master.detach())
+                        u.own_compute_slice(self.rank).copy_(u.master.detach())
             self.after_optimizer_step()
 
         if not getattr(optimizer, "_mvp_native_step", False):
@@ -593,8 +792,11 @@ class NativeFSDP(nn.Module):
         self._max_norm = None
         self._attach_grads()
         for u in self.units:
-            if u.trainable:
+            if u.trainable and not u.resharded:
                 self._gather(u)
+        if self._slots:  # the slots hold last step's weights: every resharded unit gathers again
+            self._slot_owner = [-1, -1]
+            self._publish_weight_epoch()
 
     def logical_parameter_counts(self) -> tuple[int, int]:
         total = sum(e.numel for u in self.units for e in u.entries)
@@ -661,7 +863,13 @@ class NativeFSDP(nn.Module):
             lo, hi = u.local_range(self.rank)
             if u.trainable:
                 u.master.copy_(stage[lo:hi])
-            u.full.copy_(stage.to(u.full.dtype))
+            if u.resharded:
+                u.wshard.copy_(stage[lo:hi].to(u.wshard.dtype))
+            else:
+                u.full.copy_(stage.to(u.full.dtype))
+        if self._slots:
+            self._slot_owner = [-1, -1]
+            self._publish_weight_epoch()
 
     def _full_from_value(self, v: Any, shape: torch.Size) -> torch.Tensor:
         try:

@@ -43,14 +43,14 @@ class FlatAdamW(torch.optim.Optimizer):
         g = self.param_groups[0]
         b1, b2 = g["betas"]
         for u in self.units:
-            lo, hi = u.local_range(f.rank)
-            shadow = u.full[lo:hi] if u.full.dtype == torch.bfloat16 else None
+            own = u.own_compute_slice(f.rank)
+            shadow = own if own.dtype == torch.bfloat16 else None
             ops.adamw_step_(u.master.data, u.grad_shard[: u.shard], u.exp_avg, u.exp_avg_sq, lr=float(g["lr"]), beta1=b1, beta2=b2,
                             eps=float(g["eps"]), weight_decay=float(g["weight_decay"]), step=self._step_count,
                             grad_scale=f._grad_scale, norm_sq=f._norm_sq,
                             max_norm=f._max_norm if f._max_norm is not None else 0.0, p_bf16=shadow)
             if shadow is None:
-                u.full[lo:hi].copy_(u.master.to(u.full.dtype))
+                own.copy_(u.master.to(own.dtype))
         f.after_optimizer_step()
         return loss
 

@@ -51,3 +51,50 @@ def test_fsdp_world2_matches_single_process():
     for k, v in single[1].items():
         assert torch.allclose(v, multi[0][1][k], atol=1e-4), k
         assert torch.allclose(multi[0][1][k], multi[1][1][k])
+
+
+def _train_reshard(rank, world, port, steps, reshard, ckpt):
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import build_qwen3
+    from mvp_engine.parallel.fsdp import NativeFSDP
+    from mvp_engine.parallel.optim import FlatAdamW
+
+    initialize_process_group()
+    model = build_qwen3("mvp/qwen3-tiny", seed=3, vocab_size=256, hidden_size=128, intermediate_size=256,
+                        num_attention_heads=2, num_key_value_heads=1, num_hidden_layers=5)
+    if ckpt:
+        model.gradient_checkpointing_enable({"num_layers": 3})
+    fsdp = NativeFSDP(model, group=dist.group.WORLD, device=torch.device("cpu"), param_dtype=torch.float32,
+                      reshard_after_forward=reshard)
+    assert sum(u.resharded for u in fsdp.units) == (5 if reshard else 0)
+    opt = FlatAdamW(fsdp, lr=1e-3, weight_decay=0.1)
+    g = torch.Generator().manual_seed(321)
+    losses = []
+    for _ in range(steps):
+        total = 0.0
+        for micro in range(2):  # two micro-batches per step: gradients accumulate across them
+            x = torch.randint(0, 256, (2, 48), generator=g)[rank:rank + 1]
+            fsdp.set_requires_gradient_sync(micro == 1)
+            out = fsdp(input_ids=x, labels=x)
+            loss = out["loss"].sum() / (2 * 47)
+            loss.backward()
+            total += float(loss)
+        fsdp.clip_grad_norm_(1.0)
+        opt.step()
+        losses.append(total)
+    sd = fsdp.checkpoint_state_dict(full=True)
+    return losses, {k: v.clone() for k, v in sd.items() if "layers.2" in k or "layers.4" in k}
+
+
+def test_resharded_weights_match_resident_weights():
+    """reshard_after_forward (full weights only while a block runs, gathered again for backward and for
+    recomputation) reproduces the resident run, with accumulation and activation checkpointing."""
+    for ckpt in (False, True):
+        resident = spawn_workers(_train_reshard, 2, 4, False, ckpt)
+        resharded = spawn_workers(_train_reshard, 2, 4, True, ckpt)
+        for r in range(2):
+            assert resident[r][0] == resharded[r][0], (ckpt, resident[r][0], resharded[r][0])
+            for k, v in resident[r][1].items():
+                assert torch.equal(v, resharded[r][1][k]), (ckpt, k)

@@ -130,6 +130,37 @@ def test_rmsnorm(with_res):
 
 
 @cuda
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rms_norm_linear_matches_fp32(with_res):
+    """The fused norm -> GEMM node (normalised rows recomputed in the backward) against fp32 PyTorch."""
+    ops = _ops()
+    torch.manual_seed(5)
+    T, H, N = 520, 1024, 768
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+    r = torch.randn(T, H, device="cuda").bfloat16().requires_grad_() if with_res else None
+    wn = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_()
+    wl = (0.02 * torch.randn(N, H, device="cuda")).bfloat16().requires_grad_()
+    y, h = ops.rms_norm_linear(x, wn, wl, 1e-6, residual=r)
+    gy, gh = torch.randn_like(y), torch.randn_like(h)
+    torch.autograd.backward([y, h], [gy, gh])
+
+    xf = x.detach().float().requires_grad_()
+    rf = r.detach().float().requires_grad_() if with_res else None
+    wnf = wn.detach().float().requires_grad_()
+    wlf = wl.detach().float().requires_grad_()
+    hf = xf + rf if with_res else xf
+    yf = (wnf * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6))) @ wlf.t()
+    torch.autograd.backward([yf, hf], [gy.float(), gh.float()])
+    assert _rel_err(y, yf) < 1e-2
+    assert _rel_err(h, hf) < 1e-2
+    assert _rel_err(x.grad, xf.grad) < 1e-2
+    assert _rel_err(wn.grad, wnf.grad) < 1e-2
+    assert _rel_err(wl.grad, wlf.grad) < 1e-2
+    if with_res:
+        assert _rel_err(r.grad, rf.grad) < 1e-2
+
+
+@cuda
 @pytest.mark.parametrize("mrope", [None, [24, 20, 20]])
 def test_qk_norm_rope(mrope):
     ops = _ops()

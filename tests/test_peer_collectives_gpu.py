@@ -131,3 +131,64 @@ def test_native_fsdp_peer_reduce_scatter_matches_nccl():
             assert abs(a - b) < 1e-3 * abs(b) and abs(ga - gb) < 1e-3 * abs(gb)
         for x, y in zip(sf, sn):
             assert ((x - y).norm() / (y.norm() + 1e-12)).item() < 1e-4
+
+
+def _reshard_worker(rank, world, port, comm, reshard, ckpt):
+    import os
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import build_qwen3
+    from mvp_engine.ops import _ext
+    from mvp_engine.parallel.fsdp import NativeFSDP
+    from mvp_engine.parallel.optim import FlatAdamW
+
+    initialize_process_group()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = build_qwen3("mvp/qwen3-tiny", seed=3, vocab_size=512, num_hidden_layers=4, device="meta")
+    if ckpt:
+        model.gradient_checkpointing_enable({"num_layers": 2})
+    fsdp = NativeFSDP(model, group=dist.group.WORLD, device=dev, param_dtype=torch.bfloat16, comm=comm,
+                      reshard_after_forward=reshard)
+    assert sum(u.resharded for u in fsdp.units) == (4 if reshard else 0)
+    assert (fsdp._wpeer is not None) == (reshard and comm == "fused")
+    opt = FlatAdamW(fsdp, lr=1e-3)
+    g = torch.Generator().manual_seed(11 + rank)
+    T = 1024
+    cu = torch.tensor([0, 300, T], dtype=torch.int32, device=dev)
+    losses = []
+    for _ in range(3):
+        total = 0.0
+        for micro in range(2):
+            ids = torch.randint(0, 512, (1, T), generator=g).to(dev)
+            fsdp.set_requires_gradient_sync(micro == 1)
+            out = fsdp(input_ids=ids, labels=ids, cu_seq_lens_q=cu, max_length_q=724)
+            loss = out["loss"].sum() / T
+            loss.backward()
+            total += float(loss.detach())
+        gn = fsdp.clip_grad_norm_(1.0)
+        opt.step()
+        losses.append((total, float(gn)))
+    torch.cuda.synchronize()
+    _ext.check_status(dev)
+    sd = fsdp.checkpoint_state_dict(full=True)
+    dist.barrier()
+    return losses, {k: v.float().clone() for k, v in sd.items() if "layers.3." in k}
+
+
+@two_gpus
+@pytest.mark.parametrize("ckpt", [False, True])
+def test_resharded_weights_peer_pull_matches_resident(ckpt):
+    """FSDP parameter gather by peer pull (weights resharded after each use, gathered again for backward and
+    recomputation) against NCCL all-gathers and against resident weights: same losses, norms and weights."""
+    resident = spawn_workers(_reshard_worker, 2, "nccl", False, ckpt, timeout=300)
+    pulled = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, timeout=300)
+    gathered = spawn_workers(_reshard_worker, 2, "nccl", True, ckpt, timeout=300)
+    for variant in (pulled, gathered):
+        for (lv, wv), (lr, wr) in zip(variant, resident):
+            for (a, ga), (b, gb) in zip(lv, lr):
+                assert abs(a - b) <= 1e-3 * abs(b) and abs(ga - gb) <= 1e-3 * abs(gb), (lv, lr)
+            for k, v in wr.items():
+                assert ((wv[k] - v).norm() / (v.norm() + 1e-12)).item() < 1e-4, k
