@@ -19,6 +19,7 @@ backward sees a detached alias of the weight, without the attribute.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -56,6 +57,52 @@ def _native(t: torch.Tensor) -> bool:
 
 
 # --------------------------------------------------------------------- GEMM
+class GatherJob:
+    """An FSDP shard gather waiting for a GEMM to carry it (see ``NativeFSDP``).
+
+    The next large enough :func:`gemm` on the CUDA path launches the two-SM kernel with ``copy_ctas``
+    extra CTAs that pull every rank's bf16 shard into ``slot``; ``consumed`` then becomes True.  The
+    runtime that queued the job launches the stand-alone pull instead if no GEMM took it by the time
+    the gathered weights are needed."""
+
+    def __init__(self, peer_bufs: list[int], peer_flags: list[int], offset: int, shard: int, epoch: int,
+                 slot: torch.Tensor, copy_ctas: int, min_mnk: int, timeout_s: float = 10.0) -> None:
+        self.args = (list(peer_bufs), list(peer_flags), int(offset), int(shard), int(epoch))
+        self.slot = slot
+        self.copy_ctas = int(copy_ctas)
+        self.min_mnk = int(min_mnk)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.consumed = False
+
+
+_pending_gather: Optional[GatherJob] = None
+
+
+def set_pending_gather(job: Optional[GatherJob]) -> None:
+    global _pending_gather
+    _pending_gather = job
+
+
+def pending_gather() -> Optional[GatherJob]:
+    return _pending_gather
+
+
+def _carry_pending_gather(a, a_mn, b, b_mn, out, accumulate, M: int, N: int, K: int) -> bool:
+    """Launch this GEMM with the pending gather's copy CTAs if it is large enough; True when launched."""
+    global _pending_gather
+    job = _pending_gather
+    if job is None or M < 256 or N < 256 or M * N * K < job.min_mnk or a.dtype != torch.bfloat16:
+        return False
+    if os.environ.get("MVP_GEMM_PAIR", "1") == "0":  # the carrying kernel is the two-SM one
+        return False
+    _pending_gather = None
+    bufs, flags, off, shard, epoch = job.args
+    _ext.ext().gemm_pair_gather(a, a_mn, b, b_mn, out, accumulate, _ext.status_buffer(a.device).data_ptr(), bufs,
+                                flags, off, shard, epoch, job.slot, job.copy_ctas, job.timeout_ns)
+    job.consumed = True
+    return True
+
+
 def gemm(
     a: torch.Tensor,
     b: torch.Tensor,
@@ -87,6 +134,9 @@ def gemm(
         return out
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    K = a.shape[0] if a_mn else a.shape[1]
+    if _pending_gather is not None and _carry_pending_gather(a, a_mn, b, b_mn, out, accumulate, M, N, K):
+        return out
     _ext.ext().gemm(a, a_mn, b, b_mn, out, accumulate, _ext.status_buffer(a.device).data_ptr())
     return out
 

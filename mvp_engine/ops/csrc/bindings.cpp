@@ -72,6 +72,10 @@ void peer_gather_shards(const std::vector<int64_t>& peer_bufs, const std::vector
                         int64_t offset, int64_t shard, int64_t epoch, torch::Tensor& out, int64_t status_ptr,
                         int64_t timeout_ns);
 void publish_epoch(int64_t flag_ptr, int64_t epoch);
+void gemm_pair_gather(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                      bool accumulate, int64_t status_ptr, const std::vector<int64_t>& peer_bufs,
+                      const std::vector<int64_t>& peer_flags, int64_t offset, int64_t shard, int64_t epoch,
+                      torch::Tensor& slot, int64_t copy_ctas, int64_t timeout_ns);
 void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std::vector<int64_t>& peer_slots,
                        int64_t my_slots, int64_t rank, int64_t seq, int64_t status_ptr, int64_t timeout_ns);
 void gemm_ulysses(const torch::Tensor& a, const torch::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
@@ -144,6 +148,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dv_out") = py::none(), py::arg("cu_seqlens_k") = py::none(), py::arg("pull") = py::none(),
         py::arg("dq_accum") = py::none(), py::arg("dkv_f32") = py::none(), py::arg("route") = py::none());
   m.def("peer_gather_shards", &peer_gather_shards, "FSDP parameter gather: pull every rank's bf16 shard (bounded epoch wait)");
+  m.def("gemm_pair_gather", &gemm_pair_gather, "two-SM GEMM carrying an FSDP shard pull in extra CTAs");
   m.def("publish_epoch", &publish_epoch, "system-scope release of an epoch number into a flag");
   m.def("peer_publish", &peer_publish, "publish a sequence number into every rank's signal slot");
   m.def("peer_slot_sum_f32", &peer_slot_sum_f32,

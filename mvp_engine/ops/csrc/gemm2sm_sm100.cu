@@ -74,6 +74,11 @@ struct Params {
   //    share of section 0, then of section 1, ...), row stride ldc.
   int u_world, u_rank, u_chunk, u_hd;
   int u_sec[3];
+  // FSDP parameter gather carried by this GEMM (optional, gather.ctas > 0): CTAs with
+  // blockIdx.x >= 2 * gemm_clusters pull the next unit's shards into its staging slot while the
+  // other CTAs compute this GEMM's tiles.  Nothing in the GEMM reads the gathered buffer.
+  ShardGather gather{};
+  int gemm_clusters = 0;  // clusters that compute tiles (set at launch)
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -170,9 +175,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  if (p.gather.ctas > 0 && static_cast<int>(blockIdx.x) >= 2 * p.gemm_clusters) {
+    // copy CTA (both CTAs of its cluster are copy CTAs): no barriers, no tensor memory
+    shard_gather_cta(p.gather, static_cast<int>(blockIdx.x) - 2 * p.gemm_clusters, p.status,
+                     reinterpret_cast<int*>(smem));
+    return;
+  }
   const uint32_t crank = cluster_ctarank();  // 0 = leader
   const int cluster_id = blockIdx.x >> 1;
-  const int num_clusters = gridDim.x >> 1;
+  const int num_clusters = p.gemm_clusters;
   const int num_m = (p.M + TILE - 1) / TILE;
   const int num_n = (p.N + TILE - 1) / TILE;
   const int num_tiles = num_m * num_n;
@@ -427,9 +438,12 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int n
     configured = true;
   }
   const int num_tiles = ((p.M + TILE - 1) / TILE) * ((p.N + TILE - 1) / TILE);
-  const int clusters = std::max(1, std::min(num_tiles, num_sms / 2));
+  const int copy_ctas = p.gather.ctas;  // even: copy CTAs come in clusters of two
+  const int clusters = std::max(1, std::min(num_tiles, (num_sms - copy_ctas) / 2));
+  Params q = p;
+  q.gemm_clusters = clusters;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters);
+  cfg.gridDim = dim3(2 * clusters + copy_ctas);
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
@@ -440,7 +454,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int n
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, q));
 }
 
 template <int EPI>
@@ -455,9 +469,10 @@ void dispatch(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb
 }  // namespace gemm2
 }  // namespace mvp
 
-// Same contract as gemm_sm100 (operands already validated by the caller).
-void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
-                     bool accumulate, int64_t status_ptr) {
+// Same contract as gemm_sm100 (operands already validated by the caller); `gather` (optional) is an
+// FSDP shard pull carried by extra CTAs of the launch.
+static void pair_gemm_impl(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                           bool accumulate, int64_t status_ptr, const mvp::ShardGather* gather) {
   using namespace mvp::gemm2;
   const int64_t M = a_mn ? a.size(1) : a.size(0);
   const int64_t K = a_mn ? a.size(0) : a.size(1);
@@ -489,11 +504,62 @@ void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, 
   p.dst_row0 = 0;
   p.u_world = p.u_rank = p.u_chunk = p.u_hd = 0;
   p.u_sec[0] = p.u_sec[1] = p.u_sec[2] = 0;
+  if (gather != nullptr) p.gather = *gather;
   const int sms = mvp::num_sms(a.get_device());
   const int epi = out_f32 ? (accumulate ? kAccumF32 : kStoreF32) : kStoreBf16;
   if (epi == kStoreBf16) dispatch<kStoreBf16>(a_mn, b_mn, ta, tb, p, sms, stream);
   else if (epi == kStoreF32) dispatch<kStoreF32>(a_mn, b_mn, ta, tb, p, sms, stream);
   else dispatch<kAccumF32>(a_mn, b_mn, ta, tb, p, sms, stream);
+}
+
+void gemm_sm100_pair(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                     bool accumulate, int64_t status_ptr) {
+  pair_gemm_impl(a, a_mn, b, b_mn, c, accumulate, status_ptr, nullptr);
+}
+
+// Two-SM GEMM (operands as gemm_sm100, M, N >= 256) that also carries the FSDP parameter gather of
+// another unit: `copy_ctas` (even, < SM count) extra CTAs pull peer_bufs[r] + offset (bf16 elements, one
+// shard of `shard` elements per rank, after every rank published `epoch` into peer_flags[r]) into
+// `slot` [world * shard].  The GEMM never reads `slot`; the caller orders the gathered unit's use after
+// this launch on the same stream.
+void gemm_pair_gather(const torch::Tensor& a, bool a_mn, const torch::Tensor& b, bool b_mn, torch::Tensor& c,
+                      bool accumulate, int64_t status_ptr, const std::vector<int64_t>& peer_bufs,
+                      const std::vector<int64_t>& peer_flags, int64_t offset, int64_t shard, int64_t epoch,
+                      torch::Tensor& slot, int64_t copy_ctas, int64_t timeout_ns) {
+  using namespace mvp;
+  const int world = static_cast<int>(peer_bufs.size());
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16 && a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1 &&
+                  a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0,
+              "gemm_pair_gather: bf16 operands with unit inner stride and 8-element row strides");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
+              "gemm_pair_gather: operands must be 16-byte aligned");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK(K == (b_mn ? b.size(0) : b.size(1)) && c.size(0) == M && c.size(1) == N && M >= 256 && N >= 256 && K > 0,
+              "gemm_pair_gather: shapes (M, N >= 256)");
+  TORCH_CHECK(c.scalar_type() == at::kBFloat16 || c.scalar_type() == at::kFloat, "gemm_pair_gather: bf16/fp32 out");
+  TORCH_CHECK(!accumulate || c.scalar_type() == at::kFloat, "gemm_pair_gather: accumulate needs fp32 output");
+  TORCH_CHECK(world >= 1 && world <= kMaxGatherRanks && static_cast<int>(peer_flags.size()) == world,
+              "gemm_pair_gather: 1..8 ranks, one flag per rank");
+  TORCH_CHECK(slot.is_cuda() && slot.is_contiguous() && slot.element_size() == 2 && slot.numel() == world * shard,
+              "gemm_pair_gather: contiguous 16-bit slot of world x shard elements");
+  TORCH_CHECK((shard * 2) % 16 == 0 && (offset * 2) % 16 == 0, "gemm_pair_gather: 16-byte aligned shards");
+  const int sms = num_sms(a.get_device());
+  TORCH_CHECK(copy_ctas >= 2 && copy_ctas % 2 == 0 && copy_ctas <= sms - 2, "gemm_pair_gather: even copy_ctas < SMs");
+  ShardGather g{};
+  for (int r = 0; r < world; ++r) {
+    g.src[r] = reinterpret_cast<const uint4*>(peer_bufs[r] + offset * 2);
+    g.flags[r] = reinterpret_cast<const unsigned long long*>(peer_flags[r]);
+  }
+  g.dst = reinterpret_cast<uint4*>(slot.data_ptr());
+  g.n16 = shard * 2 / 16;
+  g.world = world;
+  g.epoch = static_cast<unsigned long long>(epoch);
+  g.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+  g.ctas = static_cast<int>(copy_ctas);
+  pair_gemm_impl(a, a_mn, b, b_mn, c, accumulate, status_ptr, &g);
 }
 
 // Tensor-parallel GEMM on the two-SM kernel, bf16 out, K-major A [M, K] and B [N, K]

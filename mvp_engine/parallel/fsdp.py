@@ -189,6 +189,12 @@ class NativeFSDP(nn.Module):
         self._slot_owner = [-1, -1]  # unit index whose full weights each staging slot holds (-1: none)
         self._phase = "forward"
         self._wpeer = None  # symmetric bf16 shard buffer for the peer-pull gather
+        self._gather_job = None  # (unit index, ops.GatherJob) queued for the next large GEMM
+        # Peer-pull gathers ride in the next large GEMM (MVP_FSDP_GATHER=gemm, default) or run as a
+        # stand-alone kernel on the comm stream (=kernel); copy CTAs and the smallest carrying GEMM:
+        self._gather_in_gemm = os.environ.get("MVP_FSDP_GATHER", "gemm") == "gemm"
+        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "16"))
+        self._gather_min_mnk = int(os.environ.get("MVP_FSDP_GATHER_MIN_MNK", str(1 << 33)))
         self.module = model
         self.group = group
         self.tp_group = tp_group
@@ -551,6 +557,8 @@ class NativeFSDP(nn.Module):
 
     # --------------------------------------------------- collectives
     def _wait_gather(self, idx: int) -> None:
+        if self.units[idx].resharded:
+            self._flush_gather_job(idx)
         ev = self.units[idx].ag_event
         if ev is not None and self.device.type == "cuda":
             torch.cuda.current_stream(self.device).wait_event(ev)
@@ -602,6 +610,20 @@ class NativeFSDP(nn.Module):
             with torch.no_grad(), keep_version:
                 u.full.copy_(torch.cat(parts))
             return
+        if self._wpeer is not None and self._gather_in_gemm:
+            # Fused path: the pull rides in extra CTAs of the next large GEMM on the compute stream (the
+            # current unit's), which comes after every earlier reader of the slot and before every use
+            # of the gathered unit.  A job no GEMM took is flushed by _wait_gather.
+            from .. import ops as _ops
+
+            self._flush_gather_job()
+            wp = self._wpeer
+            job = _ops.GatherJob(wp["bufs"], wp["flag_ptrs"], self._wshard_off[u.index], u.shard, wp["epoch"],
+                                 u.full, self._gather_ctas, self._gather_min_mnk)
+            self._gather_job = (u.index, job)
+            u.ag_event = None
+            _ops.set_pending_gather(job)
+            return
         ev = torch.cuda.Event()
         ev.record(cur)
         self._comm_stream.wait_event(ev)
@@ -616,6 +638,24 @@ class NativeFSDP(nn.Module):
                 dist.all_gather_into_tensor(u.full, u.wshard, group=self.group)
             u.ag_event = torch.cuda.Event()
             u.ag_event.record(self._comm_stream)
+
+    def _flush_gather_job(self, idx: Optional[int] = None) -> None:
+        """Launch a queued GEMM-carried gather that no GEMM took (all of them, or only unit ``idx``'s) as the
+        stand-alone pull kernel on the compute stream, ahead of the gathered unit's first use."""
+        pending = getattr(self, "_gather_job", None)
+        if pending is None or (idx is not None and pending[0] != idx):
+            return
+        from .. import ops as _ops
+
+        unit_idx, job = pending
+        self._gather_job = None
+        if _ops.pending_gather() is job:
+            _ops.set_pending_gather(None)
+        if job.consumed:
+            return
+        bufs, flags, off, shard, epoch = job.args
+        with torch.no_grad(), torch.autograd._unsafe_preserve_version_counter(self._slots[self.units[unit_idx].slot]):
+            _ops.peer_gather_shards(bufs, flags, self.rank, off, shard, epoch, job.slot)
 
     @torch.no_grad()
     def _gather_all(self, initial: bool = False) -> None:

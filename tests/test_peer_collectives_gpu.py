@@ -133,10 +133,14 @@ def test_native_fsdp_peer_reduce_scatter_matches_nccl():
             assert ((x - y).norm() / (y.norm() + 1e-12)).item() < 1e-4
 
 
-def _reshard_worker(rank, world, port, comm, reshard, ckpt):
+def _reshard_worker(rank, world, port, comm, reshard, ckpt, gather="gemm"):
     import os
 
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    # gemm: every pull rides in copy CTAs of the next GEMM (threshold 0 so the tiny model's GEMMs carry
+    # it); kernel: stand-alone pull kernel on the comm stream
+    os.environ["MVP_FSDP_GATHER"] = gather
+    os.environ["MVP_FSDP_GATHER_MIN_MNK"] = "0"
     import torch.distributed as dist
 
     from mvp_engine.distributed.init import initialize_process_group
@@ -154,6 +158,17 @@ def _reshard_worker(rank, world, port, comm, reshard, ckpt):
                       reshard_after_forward=reshard)
     assert sum(u.resharded for u in fsdp.units) == (4 if reshard else 0)
     assert (fsdp._wpeer is not None) == (reshard and comm == "fused")
+    from mvp_engine import ops
+
+    carried = [0]
+    real = ops._carry_pending_gather
+
+    def counting(*a, **k):
+        launched = real(*a, **k)
+        carried[0] += int(launched)
+        return launched
+
+    ops._carry_pending_gather = counting
     opt = FlatAdamW(fsdp, lr=1e-3)
     g = torch.Generator().manual_seed(11 + rank)
     T = 1024
@@ -175,6 +190,8 @@ def _reshard_worker(rank, world, port, comm, reshard, ckpt):
     _ext.check_status(dev)
     sd = fsdp.checkpoint_state_dict(full=True)
     dist.barrier()
+    if reshard and comm == "fused" and gather == "gemm":
+        assert carried[0] > 0, "no GEMM carried a gather"
     return losses, {k: v.float().clone() for k, v in sd.items() if "layers.3." in k}
 
 
@@ -182,11 +199,13 @@ def _reshard_worker(rank, world, port, comm, reshard, ckpt):
 @pytest.mark.parametrize("ckpt", [False, True])
 def test_resharded_weights_peer_pull_matches_resident(ckpt):
     """FSDP parameter gather by peer pull (weights resharded after each use, gathered again for backward and
-    recomputation) against NCCL all-gathers and against resident weights: same losses, norms and weights."""
+    recomputation) -- carried by GEMM copy CTAs, or as a stand-alone kernel -- against NCCL all-gathers
+    and against resident weights: same losses, norms and weights."""
     resident = spawn_workers(_reshard_worker, 2, "nccl", False, ckpt, timeout=300)
-    pulled = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, timeout=300)
+    in_gemm = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, "gemm", timeout=300)
+    pulled = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, "kernel", timeout=300)
     gathered = spawn_workers(_reshard_worker, 2, "nccl", True, ckpt, timeout=300)
-    for variant in (pulled, gathered):
+    for variant in (in_gemm, pulled, gathered):
         for (lv, wv), (lr, wr) in zip(variant, resident):
             for (a, ga), (b, gb) in zip(lv, lr):
                 assert abs(a - b) <= 1e-3 * abs(b) and abs(ga - gb) <= 1e-3 * abs(gb), (lv, lr)
