@@ -59,10 +59,14 @@ class FlatAdamW(torch.optim.Optimizer):
 
     # ------------------------------------------------------- checkpoints
     def _group_meta(self, fqns: list[str]) -> dict[str, Any]:
+        """The param-group entry torch.optim.AdamW of this torch version writes (same keys, so checkpoints
+        load into either runtime), with this optimizer's hyper-parameters."""
         g = self.param_groups[0]
-        return {"lr": g["lr"], "betas": g["betas"], "eps": g["eps"], "weight_decay": g["weight_decay"],
-                "amsgrad": False, "maximize": False, "foreach": None, "capturable": False, "differentiable": False,
-                "fused": None, "initial_lr": g.get("initial_lr", g["lr"]), "params": fqns}
+        meta = {k: v for k, v in torch.optim.AdamW([torch.zeros(1)]).param_groups[0].items() if k != "params"}
+        meta.update(lr=g["lr"], betas=g["betas"], eps=g["eps"], weight_decay=g["weight_decay"], params=fqns)
+        if "initial_lr" in g:  # present once a learning-rate scheduler drives the optimizer, as in torch
+            meta["initial_lr"] = g["initial_lr"]
+        return meta
 
     def checkpoint_state_dict(self, full: bool = False) -> dict[str, Any]:
         """``{"state": {fqn: {step, exp_avg, exp_avg_sq}}, "param_groups": [...]}`` keyed by HF names."""

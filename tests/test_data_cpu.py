@@ -87,3 +87,20 @@ def test_dataloader_batches():
     loader = kit.build_dataloader(kit.build_dataset(spec), spec)
     b = next(iter(loader))
     assert b["input_ids"].shape == (2, 64) and "cu_seq_lens_q" in b and b["cu_seq_lens_q"][-1] == 128
+
+
+def test_dataloader_position_resumes_the_stream():
+    """A loader restored from ``state_dict`` continues with the batch after the last one handed out."""
+    kit = LLMDataKit()
+    spec = _spec(bs=2)
+    first = kit.build_dataloader(kit.build_dataset(spec), spec)
+    it = iter(first)
+    seen = [next(it) for _ in range(3)]
+    state = first.state_dict()
+    assert state == {"batches_into_pass": 3}
+    expected = next(it)
+    again = kit.build_dataloader(kit.build_dataset(spec), spec)
+    again.load_state_dict(state)
+    got = next(iter(again))
+    assert torch.equal(got["input_ids"], expected["input_ids"])
+    assert not torch.equal(got["input_ids"], seen[-1]["input_ids"])
