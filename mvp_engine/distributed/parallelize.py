@@ -67,7 +67,15 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
             param_dtype = "float32" if next(model.parameters()).dtype == torch.float32 else param_dtype
         dp = parallel_mesh.dp_cp  # context ranks share parameters too
         shard_mesh = dp.mesh if dp.active else None
-        if shard_mesh is not None and len(dp.dim_names) > 1:
+        replicate_group = None
+        hsdp = (not parallel_mesh.cp.active and parallel_mesh.has_dim("replicate") and parallel_mesh.has_dim("shard")
+                and parallel_mesh.dim_size("replicate") > 1 and parallel_mesh.dim_size("shard") > 1)
+        if hsdp:  # shard within each replica group, average gradient shards across the replicas
+            shard_role = parallel_mesh.role("shard")
+            replicate_group = parallel_mesh.role("replicate").group
+            shard_mesh = parallel_mesh.device_mesh[("replicate", "shard")]
+            dp = shard_role
+        elif shard_mesh is not None and len(dp.dim_names) > 1:
             shard_mesh = parallel_mesh.device_mesh[dp.dim_names]._flatten("_".join(dp.dim_names))
         reshard = kw.get("reshard_after_forward")
         if reshard is None and dev.type == "cuda" and dp.world_size > 1:
@@ -77,7 +85,8 @@ def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwa
                     f"{' (weights resharded after use)' if reshard else ''}...")
         return NativeFSDP(model, group=dp.group, device=dev, param_dtype=param_dtype,
                           comm="fused" if comm_cfg.get("fused", True) else "nccl", shard_mesh=shard_mesh,
-                          tp_group=tp.group if tp.active else None, reshard_after_forward=bool(reshard))
+                          tp_group=tp.group if tp.active else None, reshard_after_forward=bool(reshard),
+                          replicate_group=replicate_group)
 
     if not shard_active and not tp.active:
         from torch.nn.parallel import DistributedDataParallel

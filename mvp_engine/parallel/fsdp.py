@@ -182,8 +182,13 @@ class NativeFSDP(nn.Module):
                  device: Optional[torch.device] = None, param_dtype: Any = torch.bfloat16,
                  unit_classes: Optional[Iterable[str]] = None, comm: str = "nccl",
                  shard_mesh: Any = None, tp_group: Optional[dist.ProcessGroup] = None,
-                 reshard_after_forward: bool = False) -> None:
+                 reshard_after_forward: bool = False, replicate_group: Optional[dist.ProcessGroup] = None) -> None:
         super().__init__()
+        # HSDP: parameters sharded over `group`, replicated over `replicate_group`, whose ranks average the
+        # reduce-scattered gradient shards (reference: mvp_engine/distributed/parallel_mesh.py:144-164)
+        self.replicate_group = replicate_group
+        self.rep_world = (dist.get_world_size(replicate_group)
+                          if (replicate_group is not None and dist.is_initialized()) else 1)
         self.reshard_after_forward = bool(reshard_after_forward)
         self._slots: list[torch.Tensor] = []
         self._slot_owner = [-1, -1]  # unit index whose full weights each staging slot holds (-1: none)
@@ -210,7 +215,7 @@ class NativeFSDP(nn.Module):
         self._sync_grads = True
         # Gradients are averaged over the data-parallel ranks (FSDP2 / DDP semantics): the
         # reduce-scatter sums, and the 1/world factor rides in the optimizer's gradient scale.
-        self._grad_scale = 1.0 / self.world
+        self._grad_scale = 1.0 / (self.world * self.rep_world)
         self._norm_sq: Optional[torch.Tensor] = None
         self._max_norm: Optional[float] = None
         cls_names = set(unit_classes) if unit_classes else set(getattr(model, "_no_split_modules", []) or [])
@@ -703,6 +708,8 @@ class NativeFSDP(nn.Module):
                                              pe.offsets[u.index], u.shard, self._next_seq(), u.grad_shard)
                 elif self.world > 1:
                     dist.reduce_scatter_tensor(u.grad_shard, u.grad, op=dist.ReduceOp.SUM, group=self.group)
+                if self.rep_world > 1 and self.world > 1:
+                    dist.all_reduce(u.grad_shard, group=self.replicate_group)
                 u.rs_event = torch.cuda.Event()
                 u.rs_event.record(self._comm_stream)
         else:
@@ -716,8 +723,11 @@ class NativeFSDP(nn.Module):
             buf = u.grad.detach().clone()
             dist.all_reduce(buf, group=self.group)
             lo, hi = u.local_range(self.rank)
+            part = buf[lo:hi].clone()
+            if self.rep_world > 1:
+                dist.all_reduce(part, group=self.replicate_group)
             with torch.no_grad():
-                u.grad_shard.copy_(buf[lo:hi])
+                u.grad_shard.copy_(part)
 
     def finish_grad_sync(self) -> None:
         """Reduce-scatter units whose hook did not fire (root, embeddings) and wait for all."""
@@ -827,7 +837,7 @@ class NativeFSDP(nn.Module):
                 if u.grad_shard is not u.grad:
                     u.grad_shard.zero_()
             u.rs_pending = False
-        self._grad_scale = 1.0 / self.world
+        self._grad_scale = 1.0 / (self.world * self.rep_world)
         self._norm_sq = None
         self._max_norm = None
         self._attach_grads()
@@ -850,9 +860,11 @@ class NativeFSDP(nn.Module):
         return chunks[self.rank] if self.rank < len(chunks) else full.new_zeros((0,) + tuple(full.shape[1:]))
 
     def _to_dtensor(self, local: torch.Tensor, shape: torch.Size):
-        from torch.distributed.tensor import DTensor, Shard
+        from torch.distributed.tensor import DTensor, Replicate, Shard
 
-        return DTensor.from_local(local, self.shard_mesh, [Shard(0)], run_check=False, shape=shape,
+        # HSDP: a 2-D (replicate, shard) mesh, FSDP2's placements for it
+        placements = [Replicate(), Shard(0)] if self.shard_mesh.ndim == 2 else [Shard(0)]
+        return DTensor.from_local(local, self.shard_mesh, placements, run_check=False, shape=shape,
                                   stride=torch.empty(shape, device="meta").stride())
 
     @torch.no_grad()

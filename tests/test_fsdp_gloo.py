@@ -99,3 +99,50 @@ def test_resharded_weights_match_resident_weights():
                 assert abs(a - b) <= 1e-5 * abs(a), (ckpt, resident[r][0], resharded[r][0])
             for k, v in resident[r][1].items():
                 assert torch.allclose(v, resharded[r][1][k], rtol=1e-5, atol=1e-6), (ckpt, k)
+
+
+def _train_hsdp(rank, world, port, hsdp):
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.models.qwen3 import build_qwen3
+    from mvp_engine.parallel.fsdp import NativeFSDP
+    from mvp_engine.parallel.optim import FlatAdamW
+
+    initialize_process_group()
+    shard_groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
+    rep_groups = [dist.new_group([0, 2]), dist.new_group([1, 3])]
+    model = build_qwen3("mvp/qwen3-tiny", seed=4, vocab_size=256, hidden_size=128, intermediate_size=256,
+                        num_attention_heads=2, num_key_value_heads=1, num_hidden_layers=2)
+    if hsdp:
+        fsdp = NativeFSDP(model, group=shard_groups[rank // 2], device=torch.device("cpu"),
+                          param_dtype=torch.float32, replicate_group=rep_groups[rank % 2])
+        assert fsdp.world == 2 and fsdp.rep_world == 2
+    else:
+        fsdp = NativeFSDP(model, group=dist.group.WORLD, device=torch.device("cpu"), param_dtype=torch.float32)
+    opt = FlatAdamW(fsdp, lr=1e-3, weight_decay=0.1)
+    g = torch.Generator().manual_seed(77)
+    losses = []
+    for _ in range(4):
+        x = torch.randint(0, 256, (4, 40), generator=g)[rank:rank + 1]
+        loss = fsdp(input_ids=x, labels=x)["loss"].sum() / 39
+        loss.backward()
+        fsdp.clip_grad_norm_(1.0)
+        opt.step()
+        t = loss.detach().clone()
+        dist.all_reduce(t)
+        losses.append(float(t) / world)
+    full = fsdp.checkpoint_state_dict(full=True)
+    return losses, {k: v.clone() for k, v in full.items() if "layers.1." in k}
+
+
+def test_hsdp_matches_flat_sharding():
+    """Replicate x shard (2 x 2) with gradient shards averaged over the replicas equals sharding over all 4."""
+    flat = spawn_workers(_train_hsdp, 4, False, timeout=300)
+    hsdp = spawn_workers(_train_hsdp, 4, True, timeout=300)
+    for (lf, wf), (lh, wh) in zip(flat, hsdp):
+        for a, b in zip(lf, lh):
+            assert abs(a - b) <= 1e-5 * abs(a), (lf, lh)
+        for k, v in wf.items():
+            # fp32 sums in another order: Adam's m / sqrt(v) magnifies differences of near-zero gradients
+            assert ((v - wh[k]).norm() / v.norm()).item() < 1e-4, (k, ((v - wh[k]).norm() / v.norm()).item())
