@@ -115,5 +115,6 @@ def check_status(device: torch.device | int | None = None, reset: bool = True) -
     if code != 0:
         if reset:
             buf.zero_()
-        raise RuntimeError(f"mvp_engine kernel reported status {code} (bounded wait expired)")
+        what = {6: "bad argument", 7: "bounds check failed (debug build)"}.get(code, "bounded wait expired")
+        raise RuntimeError(f"mvp_engine kernel reported status {code} ({what})")
     return code

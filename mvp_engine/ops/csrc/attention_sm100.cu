@@ -178,7 +178,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, q0, kv_lo, first_hi);
   key_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, q_last, last_lo, last_hi);
   const int kv_hi = last_hi + 1;
-  const int n_blocks = kv_hi > kv_lo ? (kv_hi - kv_lo + BLK - 1) / BLK : 0;
+  // debug builds: document boundaries (cu_seqlens) that point outside the key stream skip the block
+  const bool kv_in_bounds = MVP_BOUNDS_OK(p.status, kv_hi <= kv_lo || (kv_lo >= 0 && kv_hi <= p.Tk));
+  const int n_blocks = (kv_hi > kv_lo && kv_in_bounds) ? (kv_hi - kv_lo + BLK - 1) / BLK : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -648,7 +650,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   int q_lo, q_hi0, ql_lo, q_hi;
   query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, k0, q_lo, q_hi0);
   query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, k_last, ql_lo, q_hi);
-  const int nq = q_hi > q_lo ? (q_hi - q_lo + BLK - 1) / BLK : 0;
+  const bool q_in_bounds = MVP_BOUNDS_OK(p.status, q_hi <= q_lo || (q_lo >= 0 && q_hi <= p.T));
+  const int nq = (q_hi > q_lo && q_in_bounds) ? (q_hi - q_lo + BLK - 1) / BLK : 0;
   const int n_iter = nq * rep;
 
   if (threadIdx.x == 0) {

@@ -29,6 +29,7 @@ enum StatusCode : int {
   kTimeoutDrain = 4,
   kTimeoutPeer = 5,
   kBadArgument = 6,
+  kBoundsCheck = 7,  // debug builds only: an index derived from metadata left its tensor; the access was skipped
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -44,6 +45,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
+
+// Bounds checks of the debug build (``MVP_DEBUG=1 python setup.py build_ext --inplace`` defines
+// MVP_DEBUG_BOUNDS): MVP_BOUNDS_OK(status, cond) is `cond`, and a false `cond` also records kBoundsCheck so
+// that the host raises after the step; the caller then skips the access (never a trap).  Release builds
+// compile it to `true`.
+#ifdef MVP_DEBUG_BOUNDS
+#define MVP_BOUNDS_OK(status, cond) ((cond) ? true : (::mvp::record_status((status), ::mvp::kBoundsCheck), false))
+#else
+#define MVP_BOUNDS_OK(status, cond) true
+#endif
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -27,6 +27,9 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("MVP_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
+# Debug build: device-side bounds checks on metadata-derived indices (status code 7, access skipped).
+if os.environ.get("MVP_DEBUG", "0") not in ("", "0"):
+    NVCC_FLAGS.append("-DMVP_DEBUG_BOUNDS")
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
