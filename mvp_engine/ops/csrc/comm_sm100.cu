@@ -469,9 +469,13 @@ void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std
 namespace mvp {
 namespace comm {
 
-__global__ void __launch_bounds__(256) shard_gather_kernel(ShardGather g, int* status) {
-  __shared__ int flag;
-  shard_gather_cta(g, blockIdx.x, status, &flag);
+constexpr int kGatherKernelStages = 3;
+constexpr int kGatherKernelSmem = kGatherKernelStages * kGatherChunk + 1024 + 64;
+
+__global__ void __launch_bounds__(128) shard_gather_kernel(ShardGather g, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  shard_gather_cta_bulk(g, blockIdx.x, status, smem, kGatherKernelStages);
 }
 
 __global__ void publish_epoch_kernel(unsigned long long* flag, unsigned long long epoch) {
@@ -504,12 +508,18 @@ void peer_gather_shards(const std::vector<int64_t>& peer_bufs, const std::vector
   g.world = world;
   g.epoch = static_cast<unsigned long long>(epoch);
   g.timeout_ns = static_cast<unsigned long long>(timeout_ns);
-  // One CTA per SM at most: the copy runs on the comm stream beside the compute kernels and needs
-  // no shared memory, so it co-resides with them; 148 x 256 threads x 8 x 16 B keeps ~4.8 MB in flight.
-  const int64_t total = g.n16 * world;
-  g.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(148, (total + 2047) / 2048)));
+  // Bulk copies: each CTA keeps 3 x 32 KB in flight; 32 CTAs (~3 MB outstanding) cover NVLink's
+  // bandwidth-delay product with room to spare, and leave most SMs to the compute kernels.
+  const int64_t chunks = world * ((shard * 2 + kGatherChunk - 1) / kGatherChunk);
+  g.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, chunks)));
   const at::cuda::CUDAGuard guard(out.device());
-  mvp::comm::shard_gather_kernel<<<g.ctas, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mvp::comm::shard_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        mvp::comm::kGatherKernelSmem));
+    configured = true;
+  }
+  mvp::comm::shard_gather_kernel<<<g.ctas, 128, mvp::comm::kGatherKernelSmem, at::cuda::getCurrentCUDAStream()>>>(
       g, reinterpret_cast<int*>(status_ptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

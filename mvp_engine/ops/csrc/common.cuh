@@ -341,6 +341,98 @@ __device__ __forceinline__ void shard_gather_cta(const ShardGather& g, int cta, 
   }
 }
 
+// Bulk-copy (TMA, non-tensor) variant of shard_gather_cta: one elected thread moves the CTA's chunks
+// with cp.async.bulk, peer (or local) global memory -> this CTA's shared memory -> the staging slot,
+// `stages` chunks of kGatherChunk bytes in flight at a time.  A handful of CTAs then saturates NVLink:
+// each keeps stages x 32 KB of loads outstanding instead of a few KB of register loads.  Never a
+// multicast load.  `smem` holds the stages and, after them, `stages` mbarriers.
+constexpr int kGatherChunk = 32768;
+
+__device__ __forceinline__ void bulk_load_to_smem(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(sdst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_store_from_smem(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity, uint64_t t0, uint64_t limit_ns) {
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void shard_gather_cta_bulk(const ShardGather& g, int cta, int* status, uint8_t* smem,
+                                                      int stages) {
+  __shared__ int ok_flag;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * kGatherChunk);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < g.world && ok; ++r) {
+      while (ld_acquire_sys(g.flags[r]) < g.epoch) {
+        if (globaltimer() - t0 > g.timeout_ns) {
+          record_status(status, kTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+    fence_mbarrier_init();
+    ok_flag = ok;
+  }
+  __syncthreads();
+  if (!ok_flag || threadIdx.x != 0) return;
+  const int64_t shard_bytes = g.n16 * 16;
+  const int64_t per_rank = (shard_bytes + kGatherChunk - 1) / kGatherChunk;
+  const int64_t total = per_rank * g.world;
+  const int64_t mine = total > cta ? (total - cta + g.ctas - 1) / g.ctas : 0;  // chunks cta, cta+ctas, ...
+  uint8_t* dst_base = reinterpret_cast<uint8_t*>(g.dst);
+  bool alive = true;
+  for (int64_t base = 0, batch = 0; base < mine && alive; base += stages, ++batch) {
+    const int m = static_cast<int>(mine - base < stages ? mine - base : stages);
+    if (base > 0) bulk_wait_read_all();  // the previous batch's stores no longer read the stages
+    int64_t off[8];
+    uint32_t len[8];
+    for (int s = 0; s < m; ++s) {
+      const int64_t q = cta + (base + s) * g.ctas;
+      const int64_t r = q / per_rank, j = q - r * per_rank;
+      const int64_t b0 = j * kGatherChunk;
+      len[s] = static_cast<uint32_t>(shard_bytes - b0 < kGatherChunk ? shard_bytes - b0 : kGatherChunk);
+      off[s] = r * shard_bytes + b0;
+      mbar_arrive_expect_tx(&bars[s], len[s]);
+      bulk_load_to_smem(smem + static_cast<size_t>(s) * kGatherChunk,
+                        reinterpret_cast<const uint8_t*>(g.src[r]) + b0, len[s], &bars[s]);
+    }
+    const uint64_t t0 = globaltimer();
+    for (int s = 0; s < m; ++s) {
+      if (!mbar_spin_bounded(&bars[s], static_cast<uint32_t>(batch & 1), t0, g.timeout_ns)) {
+        record_status(status, kTimeoutPeer);
+        // let the loads already issued land (bounded) before the CTA's shared memory goes away
+        const uint64_t t1 = globaltimer();
+        for (int w = s; w < m; ++w) mbar_spin_bounded(&bars[w], static_cast<uint32_t>(batch & 1), t1, 200000000ull);
+        alive = false;
+        break;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bulk_store_from_smem(dst_base + off[s], smem + static_cast<size_t>(s) * kGatherChunk, len[s]);
+      bulk_commit();
+    }
+  }
+  bulk_wait_all();
+}
+
 // Body of one copy CTA (all threads of the CTA call it; `flag` is one int of shared memory).
 __device__ __forceinline__ void peer_pull_cta(const PeerPull& j, int* status, int* flag) {
   if (threadIdx.x == 0) {

@@ -177,8 +177,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x % 32;
   if (p.gather.ctas > 0 && static_cast<int>(blockIdx.x) >= 2 * p.gemm_clusters) {
     // copy CTA (both CTAs of its cluster are copy CTAs): no barriers, no tensor memory
-    shard_gather_cta(p.gather, static_cast<int>(blockIdx.x) - 2 * p.gemm_clusters, p.status,
-                     reinterpret_cast<int*>(smem));
+    // 5 x 32 KB stages of bulk copies fit in the GEMM's shared-memory footprint (6 operand stages)
+    shard_gather_cta_bulk(p.gather, static_cast<int>(blockIdx.x) - 2 * p.gemm_clusters, p.status, smem, 5);
     return;
   }
   const uint32_t crank = cluster_ctarank();  // 0 = leader

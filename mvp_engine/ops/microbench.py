@@ -209,6 +209,96 @@ def bench_peer_rs(mbytes: int, iters: int) -> None:
     dist.destroy_process_group()
 
 
+def bench_fsdp_gather(tokens: int, iters: int, copy_ctas: int, loopback_world: int) -> None:
+    """FSDP parameter gather of one Qwen3-8B decoder unit (193 M bf16 parameters), alone and carried by
+    copy CTAs of the unit's QKV GEMM ([tokens, 4096] x [6144, 4096]^T).
+
+    With torchrun (one rank per GPU) every shard is read from its owner over NVLink; run as one process,
+    the ``loopback_world`` "ranks" are local buffers (the kernel's own cost, for ncu).  Device time per
+    call, max over ranks.  Roofline of the fused kernel: the slower of the GEMM at the measured cuBLAS
+    burst rate and the remote bytes at the measured 770 GB/s peer copy rate."""
+    import os
+
+    import torch.distributed as dist
+
+    from mvp_engine import ops
+    from mvp_engine.ops import _ext
+
+    multi = int(os.environ.get("WORLD_SIZE", "1")) > 1
+    if multi:
+        import torch.distributed._symmetric_memory as symm
+
+        from mvp_engine.distributed.init import initialize_process_group
+
+        initialize_process_group()
+        rank, world = dist.get_rank(), dist.get_world_size()
+    else:
+        rank, world = 0, loopback_world
+    dev = torch.device("cuda", torch.cuda.current_device())
+    unit = 192_937_984  # Qwen3-8B layer: qkv + o + gate_up + down
+    shard = -(-unit // (64 * world)) * 64
+    if multi:
+        buf = symm.empty(shard, dtype=torch.bfloat16, device=dev)
+        flags = symm.empty(8, dtype=torch.int64, device=dev)
+        buf.normal_()
+        flags.fill_(1)
+        torch.cuda.synchronize()
+        hb, hf = symm.rendezvous(buf, dist.group.WORLD), symm.rendezvous(flags, dist.group.WORLD)
+        hf.barrier()
+        bufs, fl = [int(x) for x in hb.buffer_ptrs], [int(x) for x in hf.buffer_ptrs]
+    else:
+        local = [torch.randn(shard, device=dev).bfloat16() for _ in range(world)]
+        flags = torch.ones(world, dtype=torch.int64, device=dev)
+        bufs, fl = [t.data_ptr() for t in local], [flags.data_ptr() + 8 * r for r in range(world)]
+    slot = torch.empty(world * shard, dtype=torch.bfloat16, device=dev)
+    x = torch.randn(tokens, 4096, device=dev).bfloat16()
+    w = torch.randn(6144, 4096, device=dev).bfloat16()
+    y = torch.empty(tokens, 6144, device=dev, dtype=torch.bfloat16)
+    st = _ext.status_buffer(dev).data_ptr()
+    ext = _ext.ext()
+
+    cases = {
+        "qkv_gemm": lambda: ext.gemm(x, False, w, False, y, False, st),
+        "gather_kernel": lambda: ext.peer_gather_shards(bufs, fl, 0, shard, 1, slot, st, 10**10),
+        "gemm_carrying_gather": lambda: ext.gemm_pair_gather(x, False, w, False, y, False, st, bufs, fl, 0, shard, 1,
+                                                             slot, copy_ctas, 10**10),
+    }
+    if multi:
+        plain = torch.empty(shard, dtype=torch.bfloat16, device=dev)
+        cases["nccl_all_gather"] = lambda: dist.all_gather_into_tensor(slot, plain)
+    res = {}
+    for name, fn in cases.items():
+        if multi:
+            dist.barrier()
+        t = _time(fn, iters)
+        if multi:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt)
+        res[name] = t
+    _ext.check_status(dev)
+    # sanity: the carried gather produced every rank's shard
+    ok = True if multi else bool(torch.equal(slot, torch.cat(local)))
+    remote = (world - 1) * shard * 2 if multi else 0
+    flops = 2.0 * tokens * 6144 * 4096
+    gemm_peak = 1666.3e12
+    roof_ms = max(flops / gemm_peak, remote / 770e9) * 1e3
+    if rank == 0:
+        print(json.dumps({
+            "kernel": "gemm2sm_kernel + shard_gather_cta_bulk", "ranks": world, "mode": "peers" if multi else "loopback",
+            "unit_mb": round(unit * 2 / 2**20, 1), "copy_ctas": copy_ctas, "tokens": tokens,
+            **{f"{k}_ms": round(v, 4) for k, v in res.items()},
+            "gather_gbs_remote": round(remote / res["gather_kernel"] / 1e6, 1) if multi else None,
+            "gather_gbs_written": round(world * shard * 2 / res["gather_kernel"] / 1e6, 1),
+            "fused_roofline_ms": round(roof_ms, 4),
+            "fused_frac_of_roofline": round(roof_ms / res["gemm_carrying_gather"], 3),
+            "fused_vs_serial": round((res["qkv_gemm"] + res["gather_kernel"]) / res["gemm_carrying_gather"], 3),
+            "gather_correct": ok}), flush=True)
+    if multi:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_tp_gemm(tokens: int, hidden: int, iters: int) -> None:
     """Tensor-parallel GEMMs with the collective fused over NVLink vs NCCL + GEMM (launch with torchrun).
 
@@ -496,7 +586,10 @@ def _hbm_peak() -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer", "vision"])
+    ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer", "vision",
+                                     "fsdp_gather"])
+    ap.add_argument("--copy-ctas", type=int, default=12, help="fsdp_gather: copy CTAs carried by the GEMM")
+    ap.add_argument("--loopback-world", type=int, default=2, help="fsdp_gather: local 'ranks' when run alone")
     ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
     ap.add_argument("--docs", default="256,4096", help="attention: document lengths U[lo, hi]")
     ap.add_argument("--hidden", type=int, default=5120, help="tp_gemm: hidden size (square weights)")
@@ -519,6 +612,8 @@ def main() -> None:
         bench_tp_gemm(args.tokens if args.tokens != 8192 else 4096, args.hidden, args.iters)
     elif args.what == "peer_rs":
         bench_peer_rs(args.mbytes, args.iters)
+    elif args.what == "fsdp_gather":
+        bench_fsdp_gather(args.tokens, args.iters, args.copy_ctas, args.loopback_world)
     elif args.what == "cp_layer":
         bench_cp_layer(args.tokens, args.iters, args.impls.split(","))
     elif args.what == "cp_attention":

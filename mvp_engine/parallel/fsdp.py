@@ -198,7 +198,7 @@ class NativeFSDP(nn.Module):
         # Peer-pull gathers ride in the next large GEMM (MVP_FSDP_GATHER=gemm, default) or run as a
         # stand-alone kernel on the comm stream (=kernel); copy CTAs and the smallest carrying GEMM:
         self._gather_in_gemm = os.environ.get("MVP_FSDP_GATHER", "gemm") == "gemm"
-        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "16"))
+        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "12"))
         self._gather_min_mnk = int(os.environ.get("MVP_FSDP_GATHER_MIN_MNK", str(1 << 33)))
         self.module = model
         self.group = group
