@@ -776,6 +776,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (kvalid) query_range(p.cu_seqlens, p.cu_seqlens_k, p.n_docs, p.causal, kc, lo_c, ke);
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
+    // LSE (warpgroup 0) or delta (warpgroup 1) of query row c of block n: loaded one block ahead, so the
+    // global-memory latency is not on the per-block critical path
+    auto row_stat = [&](int n_) -> float {
+      const int h_ = hk * rep + n_ / nq;
+      const int qi = min(q_lo + (n_ % nq) * BLK + c, p.T - 1);
+      const int64_t at = static_cast<int64_t>(h_) * p.T + qi;
+      return half == 0 ? p.lse[at] * kLog2e : p.delta[at];
+    };
+    float next_stat = n_iter > 0 ? row_stat(0) : 0.f;
     for (int n = 0; n < n_iter; ++n) {
       const int h = hk * rep + n / nq;
       const int q0 = q_lo + (n % nq) * BLK;
@@ -784,11 +793,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(stg_free, (n - 1) & 1, abort_flag, p.status, kTimeoutEpilogue));
         if (!ok) break;
       }
-      {
-        const int qi = min(q0 + c, p.T - 1);
-        if (half == 0) s_lse[c] = p.lse[static_cast<int64_t>(h) * p.T + qi] * kLog2e;
-        else s_delta[c] = p.delta[static_cast<int64_t>(h) * p.T + qi];
-      }
+      if (half == 0) s_lse[c] = next_stat;
+      else s_delta[c] = next_stat;
+      if (n + 1 < n_iter) next_stat = row_stat(n + 1);  // in flight while this block is processed
       mbar_arrive(stg_full);
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(stg_full, n & 1, abort_flag, p.status, kTimeoutEpilogue));
       if (!ok) break;
