@@ -168,23 +168,41 @@ class _SplitLinear(torch.autograd.Function):
         return hi.contiguous(), lo.contiguous()
 
     @staticmethod
+    def _product(ah, al, bh, bl, out, a_mn=False, b_mn=False):
+        """out += (ah + al) (bh + bl)^T without the lo x lo term: three bf16 tcgen05 GEMMs accumulating in fp32
+        (relative error ~2^-16, the fp32-accurate path at tensor-core speed)."""
+        ops.gemm(al, bh, a_mn=a_mn, b_mn=b_mn, out=out, accumulate=True)
+        ops.gemm(ah, bl, a_mn=a_mn, b_mn=b_mn, out=out, accumulate=True)
+        ops.gemm(ah, bh, a_mn=a_mn, b_mn=b_mn, out=out, accumulate=True)
+
+    @staticmethod
     def forward(ctx, x, w, b):
         xh, xl = _SplitLinear._split(x)
         wh, wl = _SplitLinear._split(w)
         out = torch.zeros(x.shape[0], w.shape[0], device=x.device, dtype=torch.float32)
-        ops.gemm(xl, wh, out=out, accumulate=True)
-        ops.gemm(xh, wl, out=out, accumulate=True)
-        ops.gemm(xh, wh, out=out, accumulate=True)
+        _SplitLinear._product(xh, xl, wh, wl, out)
         ctx.save_for_backward(x, w)
         ctx.has_b = b is not None
+        ctx.acc = ops.grad_acc(w)
         return out if b is None else out + b.float()
 
     @staticmethod
     def backward(ctx, g):
         x, w = ctx.saved_tensors
-        g = g.float()
-        dx = g @ w if ctx.needs_input_grad[0] else None
-        dw = g.t() @ x if ctx.needs_input_grad[1] else None
+        g = g.float().contiguous()
+        gh, gl = _SplitLinear._split(g)
+        dx = dw = None
+        if ctx.needs_input_grad[0]:  # dX = G W: W read N-major as the B operand
+            dx = torch.zeros(g.shape[0], w.shape[1], device=g.device, dtype=torch.float32)
+            wh, wl = _SplitLinear._split(w)
+            _SplitLinear._product(gh, gl, wh, wl, dx, b_mn=True)
+        if ctx.acc is not None or ctx.needs_input_grad[1]:  # dW = G^T X, added into the fp32 accumulator
+            xh, xl = _SplitLinear._split(x)
+            acc = ctx.acc if (ctx.acc is not None and ctx.acc.dtype == torch.float32 and ctx.acc.is_contiguous()
+                              and ctx.acc.shape == w.shape) else None
+            target = acc if acc is not None else torch.zeros_like(w, dtype=torch.float32)
+            _SplitLinear._product(gh, gl, xh, xl, target, a_mn=True, b_mn=True)
+            dw = None if acc is not None else target
         db = g.sum(0) if ctx.has_b and ctx.needs_input_grad[2] else None
         return dx, dw, db
 
@@ -231,14 +249,17 @@ class Qwen3VLVisionAttention(nn.Module):
         With ``residual``, returns ``residual + attention output`` (bias and residual adds fused)."""
         N = x.shape[0]
         D = self.head_dim
-        qkv = _linear(x, self.qkv)
-        if qkv.is_cuda and qkv.dtype == torch.bfloat16 and D <= 128:
-            # RoPE kernel writes q / k / v zero-padded to the head_dim-128 attention layout directly
-            q, k, v = ops.vision_rope_pad(qkv, self.num_heads, cos, sin, 128)
+        if x.is_cuda and x.dtype == torch.bfloat16 and D <= 128:
+            # GEMM without bias; the RoPE kernel adds the qkv bias and writes q / k / v zero-padded to the
+            # head_dim-128 attention layout directly
+            qkv = ops.linear(x, _as_compute(self.qkv.weight, x))
+            bias = _as_compute(self.qkv.bias, x) if self.qkv.bias is not None else None
+            q, k, v = ops.vision_rope_pad(qkv, self.num_heads, cos, sin, 128, bias=bias)
             o = flash_attn_varlen(q, k, v, cu, max_len, causal=False, softmax_scale=D**-0.5)[..., :D]
             if residual is not None:
                 return _linear_residual(o.reshape(N, -1), self.proj, residual)
             return _linear(o.reshape(N, -1), self.proj)
+        qkv = _linear(x, self.qkv)
         q, k, v = qkv.view(N, 3, self.num_heads, D).unbind(1)
         c = torch.cat([cos, cos], -1).unsqueeze(1)
         s = torch.cat([sin, sin], -1).unsqueeze(1)

@@ -803,24 +803,34 @@ def bias_residual(y: torch.Tensor, b: torch.Tensor, x: torch.Tensor) -> torch.Te
 
 class _VisionRope(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv2, nh, cos, sin, pad_to):
-        q, k, v = _ext.ext().vision_rope_fwd(qkv2, nh, cos, sin, pad_to)
-        ctx.save_for_backward(cos, sin)
+    def forward(ctx, qkv2, nh, cos, sin, pad_to, bias):
+        q, k, v = _ext.ext().vision_rope_fwd(qkv2, nh, cos, sin, pad_to, bias=bias)
+        ctx.save_for_backward(cos, sin, bias if bias is not None else torch.empty(0))
+        ctx.has_bias = bias is not None
+        ctx.acc = grad_acc(bias) if bias is not None else None
         ctx.D = qkv2.shape[1] // (3 * nh)
         return q, k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
-        cos, sin = ctx.saved_tensors
+        cos, sin, bias = ctx.saved_tensors
         dq, dk, dv = (t.contiguous() if t is not None else None for t in (dq, dk, dv))
         zero = next(t for t in (dq, dk, dv) if t is not None)
         dq, dk, dv = (t if t is not None else torch.zeros_like(zero) for t in (dq, dk, dv))
-        return _ext.ext().vision_rope_bwd(dq, dk, dv, cos, sin, ctx.D), None, None, None, None
+        dqkv = _ext.ext().vision_rope_bwd(dq, dk, dv, cos, sin, ctx.D)
+        db = None
+        if ctx.has_bias:  # the bias gradient is the column sum of the pre-rotation gradient
+            kb = _acc_of(bias, ctx.acc)
+            g32 = _ext.ext().bias_grad(dqkv, acc=kb)
+            db = _param_grad(g32, bias, ctx.acc, kb is not None)
+        return dqkv, None, None, None, None, db
 
 
 def vision_rope_pad(qkv: torch.Tensor, nh: int, cos: torch.Tensor, sin: torch.Tensor,
-                    pad_to: int = 128) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Rotate-half RoPE of the vision tower applied to q and k of a fused ``qkv`` ``[N, 3 * nh * D]``.
+                    pad_to: int = 128, bias: Optional[torch.Tensor] = None
+                    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rotate-half RoPE of the vision tower applied to q and k of a fused ``qkv`` ``[N, 3 * nh * D]``, after
+    adding the optional qkv ``bias`` ``[3 * nh * D]`` (rounded to bf16 as a separate add would round it).
 
     ``cos`` / ``sin`` are ``[N, D / 2]`` fp32 (the rotary angles' cos / sin; each is used for both halves).
     Returns ``q, k, v`` as ``[N, nh, pad_to]`` with columns ``D..pad_to-1`` zero, the layout the
@@ -830,6 +840,8 @@ def vision_rope_pad(qkv: torch.Tensor, nh: int, cos: torch.Tensor, sin: torch.Te
     N = qkv.shape[0]
     D = qkv.shape[-1] // (3 * nh)
     if not _native(qkv) or qkv.dtype != torch.bfloat16:
+        if bias is not None:
+            qkv = qkv + bias.to(qkv.dtype)
         t = qkv.view(N, 3, nh, D)
         c = torch.cat([cos, cos], -1).unsqueeze(1)
         s = torch.cat([sin, sin], -1).unsqueeze(1)
@@ -840,8 +852,10 @@ def vision_rope_pad(qkv: torch.Tensor, nh: int, cos: torch.Tensor, sin: torch.Te
             out.append((xf * c + torch.cat((-bb, a), -1) * s).to(qkv.dtype))
         out.append(t[:, 2])
         return tuple(F.pad(o, (0, pad_to - D)) for o in out)
+    if bias is not None and bias.dtype != torch.bfloat16:
+        bias = bias.to(torch.bfloat16)
     return _VisionRope.apply(qkv.reshape(N, -1).contiguous(), int(nh), cos.float().contiguous(),
-                             sin.float().contiguous(), int(pad_to))
+                             sin.float().contiguous(), int(pad_to), bias.contiguous() if bias is not None else None)
 
 
 def sumsq(x: torch.Tensor) -> torch.Tensor:

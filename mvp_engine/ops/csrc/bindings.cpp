@@ -96,7 +96,8 @@ torch::Tensor bias_gelu_fwd(const torch::Tensor& x, const torch::Tensor& b, bool
 std::vector<torch::Tensor> bias_gelu_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& b,
                                          bool tanh_form, const c10::optional<torch::Tensor>& db_acc);
 std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh, const torch::Tensor& cosv,
-                                           const torch::Tensor& sinv, int64_t DP);
+                                           const torch::Tensor& sinv, int64_t DP,
+                                           const c10::optional<torch::Tensor>& bias);
 torch::Tensor bias_residual_fwd(const torch::Tensor& y, const torch::Tensor& b, const torch::Tensor& x);
 torch::Tensor bias_grad(const torch::Tensor& g, const c10::optional<torch::Tensor>& acc);
 torch::Tensor vision_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const torch::Tensor& dv,
@@ -123,7 +124,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("db_acc") = py::none());
   m.def("bias_residual_fwd", &bias_residual_fwd, "x + (y + b), each add rounded to bf16");
   m.def("bias_grad", &bias_grad, "fp32 column sums of a bf16 matrix", py::arg("g"), py::arg("acc") = py::none());
-  m.def("vision_rope_fwd", &vision_rope_fwd, "rotate-half RoPE of q / k, q / k / v padded to DP columns");
+  m.def("vision_rope_fwd", &vision_rope_fwd, "rotate-half RoPE of q / k (+ optional qkv bias), padded to DP columns",
+        py::arg("qkv"), py::arg("nh"), py::arg("cos"), py::arg("sin"), py::arg("DP"), py::arg("bias") = py::none());
   m.def("vision_rope_bwd", &vision_rope_bwd, "inverse rotation of dq / dk, written with dv into dqkv");
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd_", &ce_bwd_);

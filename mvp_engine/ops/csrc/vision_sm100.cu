@@ -285,6 +285,8 @@ __global__ void __launch_bounds__(128) col_partial_kernel(const __nv_bfloat16* _
 }
 
 // ------------------------------------------------------------- vision RoPE
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
 // qkv: [N, 3, nh, D] bf16; cos / sin: [N, D/2] fp32.  One warp per (token, head).
 // q_out / k_out / v_out: [N, nh, DP] bf16 with columns D..DP-1 zero.
 // rotate-half: out[i] = x[i] c_i - x[i+h] s_i, out[i+h] = x[i+h] c_i + x[i] s_i (h = D/2).
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(256) vision_rope_fwd_kernel(const __nv_bfloat1
                                                               __nv_bfloat16* __restrict__ qo,
                                                               __nv_bfloat16* __restrict__ ko,
                                                               __nv_bfloat16* __restrict__ vo, int64_t N, int nh, int D,
-                                                              int DP) {
+                                                              int DP, const __nv_bfloat16* __restrict__ bias) {
   const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (wid >= N * nh) return;
@@ -303,19 +305,22 @@ __global__ void __launch_bounds__(256) vision_rope_fwd_kernel(const __nv_bfloat1
   const int h = D / 2;
   const __nv_bfloat16* src = qkv + (n * 3 * nh + hd) * D;
   const int64_t dst = wid * DP;
+  // qkv + bias (optional, [3 * nh * D]), rounded to bf16 as a separate bias add would round it
+  auto in = [&](int t, int i) {
+    const float x = __bfloat162float(src[static_cast<int64_t>(t) * nh * D + i]);
+    return bias == nullptr ? x : bf16_round(x + __bfloat162float(bias[(t * nh + hd) * D + i]));
+  };
   for (int t = 0; t < 2; ++t) {
-    const __nv_bfloat16* s = src + static_cast<int64_t>(t) * nh * D;
     __nv_bfloat16* o = (t == 0 ? qo : ko) + dst;
     for (int i = lane; i < h; i += 32) {
       const float c = cosv[n * h + i], sn = sinv[n * h + i];
-      const float a = __bfloat162float(s[i]), bb = __bfloat162float(s[i + h]);
+      const float a = in(t, i), bb = in(t, i + h);
       o[i] = __float2bfloat16_rn(a * c - bb * sn);
       o[i + h] = __float2bfloat16_rn(bb * c + a * sn);
     }
     for (int i = D + lane; i < DP; i += 32) o[i] = __float2bfloat16_rn(0.f);
   }
-  const __nv_bfloat16* sv = src + static_cast<int64_t>(2) * nh * D;
-  for (int i = lane; i < DP; i += 32) vo[dst + i] = i < D ? sv[i] : __float2bfloat16_rn(0.f);
+  for (int i = lane; i < DP; i += 32) vo[dst + i] = i < D ? __float2bfloat16_rn(in(2, i)) : __float2bfloat16_rn(0.f);
 }
 
 // Inverse rotation of dq / dk and the dv slice, written into dqkv [N, 3, nh, D]:
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(128) vision_rope_fwd_vec_kernel(const __nv_bfl
                                                                   __nv_bfloat16* __restrict__ qo,
                                                                   __nv_bfloat16* __restrict__ ko,
                                                                   __nv_bfloat16* __restrict__ vo, int64_t N, int nh,
-                                                                  int DP) {
+                                                                  int DP, const __nv_bfloat16* __restrict__ bias) {
   constexpr int h = D / 2;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= N * 3 * nh) return;
@@ -371,6 +376,12 @@ __global__ void __launch_bounds__(128) vision_rope_fwd_vec_kernel(const __nv_bfl
   for (int c = 0; c < D / 8; ++c) {
     float f[8];
     vload8(qkv + idx * D + c * 8, f);
+    if (bias != nullptr) {  // the qkv bias (row `rem` of [3 * nh, D]), rounded as a separate add would round it
+      float bf[8];
+      vload8(bias + static_cast<int64_t>(rem) * D + c * 8, bf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = bf16_round(f[i] + bf[i]);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) x[c * 8 + i] = f[i];
   }
@@ -657,7 +668,8 @@ torch::Tensor bias_grad(const torch::Tensor& g, const c10::optional<torch::Tenso
 
 // Returns (q, k, v), each [N, nh, DP] bf16 with the head columns past D zero.
 std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh, const torch::Tensor& cosv,
-                                           const torch::Tensor& sinv, int64_t DP) {
+                                           const torch::Tensor& sinv, int64_t DP,
+                                           const c10::optional<torch::Tensor>& bias) {
   check_bf16_2d(qkv, "vision_rope_fwd qkv");
   const int64_t N = qkv.size(0);
   TORCH_CHECK(nh > 0 && qkv.size(1) % (3 * nh) == 0, "vision_rope_fwd: qkv width is not 3 * nh * D");
@@ -665,6 +677,12 @@ std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh,
   TORCH_CHECK(D % 2 == 0 && D <= DP, "vision_rope_fwd: D must be even and <= DP");
   check_vec(cosv, N * (D / 2), at::kFloat, "vision_rope_fwd cos");
   check_vec(sinv, N * (D / 2), at::kFloat, "vision_rope_fwd sin");
+  const __nv_bfloat16* bp = nullptr;
+  if (bias.has_value()) {
+    check_vec(*bias, 3 * nh * D, at::kBFloat16, "vision_rope_fwd bias");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(bias->data_ptr()) % 16 == 0, "vision_rope_fwd: 16-byte aligned bias");
+    bp = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
   const at::cuda::CUDAGuard guard(qkv.device());
   auto q = torch::empty({N, nh, DP}, qkv.options());
   auto k = torch::empty_like(q);
@@ -683,10 +701,10 @@ std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh,
     const int nhi = static_cast<int>(nh), dpi = static_cast<int>(DP);
     if (D == 64)
       vision_rope_fwd_vec_kernel<64><<<grid, 128, 0, stream>>>(src, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
-                                                               qp, kp, vp, N, nhi, dpi);
+                                                               qp, kp, vp, N, nhi, dpi, bp);
     else
       vision_rope_fwd_vec_kernel<72><<<grid, 128, 0, stream>>>(src, cosv.data_ptr<float>(), sinv.data_ptr<float>(),
-                                                               qp, kp, vp, N, nhi, dpi);
+                                                               qp, kp, vp, N, nhi, dpi, bp);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return {q, k, v};
   }
@@ -696,7 +714,7 @@ std::vector<torch::Tensor> vision_rope_fwd(const torch::Tensor& qkv, int64_t nh,
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cosv.data_ptr<float>(), sinv.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(q.data_ptr()), reinterpret_cast<__nv_bfloat16*>(k.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v.data_ptr()), N, static_cast<int>(nh), static_cast<int>(D),
-      static_cast<int>(DP));
+      static_cast<int>(DP), bp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {q, k, v};
 }

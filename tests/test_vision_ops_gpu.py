@@ -133,6 +133,37 @@ def test_vision_rope_pad(N, nh, D):
 
 
 @cuda
+@pytest.mark.parametrize("D", [72, 80])
+def test_vision_rope_pad_with_fused_bias(D):
+    """qkv bias added inside the RoPE kernel: forward and both gradients against fp32 (bias + rotation)."""
+    ops = _ops()
+    torch.manual_seed(1)
+    N, nh = 777, 4
+    qkv = torch.randn(N, 3 * nh * D, device="cuda").bfloat16().requires_grad_()
+    b = (0.5 * torch.randn(3 * nh * D, device="cuda")).bfloat16().requires_grad_()
+    ang = torch.rand(N, D // 2, device="cuda") * 50
+    q, k, v = ops.vision_rope_pad(qkv, nh, ang.cos(), ang.sin(), 128, bias=b)
+    tq = qkv.detach().float().requires_grad_()
+    tb = b.detach().float().requires_grad_()
+    t = (tq + tb).view(N, 3, nh, D)
+    c = torch.cat([ang.cos(), ang.cos()], -1).unsqueeze(1)
+    s = torch.cat([ang.sin(), ang.sin()], -1).unsqueeze(1)
+
+    def rot(x):
+        a, bb = x.chunk(2, dim=-1)
+        return torch.cat((-bb, a), -1)
+
+    refs = (t[:, 0] * c + rot(t[:, 0]) * s, t[:, 1] * c + rot(t[:, 1]) * s, t[:, 2])
+    for out, ref in zip((q, k, v), refs):
+        assert _rel_err(out[..., :D], ref) < 8e-3
+    gs = [torch.randn(N, nh, 128, device="cuda").bfloat16() for _ in range(3)]
+    sum((o.float() * g.float()).sum() for o, g in zip((q, k, v), gs)).backward()
+    sum((r * g[..., :D].float()).sum() for r, g in zip(refs, gs)).backward()
+    assert _rel_err(qkv.grad, tq.grad) < 1e-2
+    assert _rel_err(b.grad, tb.grad) < 1e-2
+
+
+@cuda
 def test_vision_block_matches_eager():
     """One Qwen3-VL vision block on the native kernels against the same block in fp32 eager math."""
     from mvp_engine.models import qwen3_vl as vl
@@ -183,3 +214,23 @@ def test_qwen3_vl_vision_tower_native_matches_fp32():
         got = dict(vis.named_parameters())[name].grad
         assert got is not None, name
         assert _rel_err(got.cpu(), ref_grads[name]) < 5e-2, name
+
+
+@cuda
+def test_split_linear_fp32_accuracy_forward_backward():
+    """Patch-embed GEMM in fp32 accuracy (hi/lo bf16 splits on tcgen05): forward, dX and dW against fp64."""
+    from mvp_engine.models.qwen3_vl import linear_fp32_accurate
+
+    torch.manual_seed(21)
+    x = torch.randn(3000, 1536, device="cuda", dtype=torch.float32).requires_grad_()
+    w = (0.02 * torch.randn(1152, 1536, device="cuda")).requires_grad_()
+    b = (0.1 * torch.randn(1152, device="cuda")).requires_grad_()
+    y = linear_fp32_accurate(x, w, b)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xd, wd, bd = (t.detach().double().requires_grad_() for t in (x, w, b))
+    yd = xd @ wd.t() + bd
+    yd.backward(g.double())
+    for got, ref in ((y, yd), (x.grad, xd.grad), (w.grad, wd.grad), (b.grad, bd.grad)):
+        rel = ((got.double() - ref).norm() / ref.norm()).item()
+        assert rel < 1e-4, rel
