@@ -44,22 +44,24 @@ class MeshRole:
 
 
 def resolve_mesh_shape(mesh_cfg: Mapping[str, int], world_size: int) -> dict[str, int]:
-    """Fill the single ``-1`` entry and check the product equals ``world_size``."""
-    cfg = {k: int(v) for k, v in mesh_cfg.items()}
-    unknown = [k for k, v in cfg.items() if v == -1]
-    if len(unknown) > 1:
+    """Sizes of every mesh dimension: a ``-1`` (at most one) takes whatever the others leave of ``world_size``.
+
+    The result's product must be ``world_size``; anything else is a configuration error."""
+    sizes = {name: int(v) for name, v in mesh_cfg.items()}
+    free = [name for name, v in sizes.items() if v == -1]
+    if len(free) > 1:
         raise ValueError("Only one device mesh dimension can be inferred.")
-    known = math.prod(v for v in cfg.values() if v != -1)
-    if unknown:
-        if world_size % known:
-            raise ValueError(
-                f"Cannot infer mesh dimension {unknown[0]!r}: world_size={world_size} is not divisible by {known}."
-            )
-        cfg[unknown[0]] = world_size // known
-    total = math.prod(cfg.values()) if cfg else 1
-    if total != world_size:
-        raise ValueError(f"Device mesh shape {tuple(cfg.values())} has size {total}, but world size is {world_size}.")
-    return cfg
+    fixed = math.prod(v for v in sizes.values() if v != -1)
+    if free:
+        quotient, remainder = divmod(world_size, fixed)
+        if remainder:
+            raise ValueError(f"Cannot infer mesh dimension {free[0]!r}: world_size={world_size} is not divisible "
+                             f"by {fixed}.")
+        sizes[free[0]] = quotient
+    if math.prod(sizes.values()) != world_size:
+        raise ValueError(f"Device mesh shape {tuple(sizes.values())} has size {math.prod(sizes.values())}, "
+                         f"but world size is {world_size}.")
+    return sizes
 
 
 class ParallelMesh:
