@@ -67,6 +67,8 @@ class GatherJob:
 
     def __init__(self, peer_bufs: list[int], peer_flags: list[int], offset: int, shard: int, epoch: int,
                  slot: torch.Tensor, copy_ctas: int, min_mnk: int, timeout_s: float = 10.0) -> None:
+        """``min_mnk``: smallest GEMM (in FLOPs, 2 M N K) that may carry the copy -- one that runs about as long
+        as the copy, so the copy CTAs finish within the GEMM."""
         self.args = (list(peer_bufs), list(peer_flags), int(offset), int(shard), int(epoch))
         self.slot = slot
         self.copy_ctas = int(copy_ctas)
@@ -91,7 +93,7 @@ def _carry_pending_gather(a, a_mn, b, b_mn, out, accumulate, M: int, N: int, K: 
     """Launch this GEMM with the pending gather's copy CTAs if it is large enough; True when launched."""
     global _pending_gather
     job = _pending_gather
-    if job is None or M < 256 or N < 256 or M * N * K < job.min_mnk or a.dtype != torch.bfloat16:
+    if job is None or M < 256 or N < 256 or 2 * M * N * K < job.min_mnk or a.dtype != torch.bfloat16:
         return False
     if os.environ.get("MVP_GEMM_PAIR", "1") == "0":  # the carrying kernel is the two-SM one
         return False

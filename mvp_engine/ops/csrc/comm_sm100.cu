@@ -469,7 +469,7 @@ void peer_slot_sum_f32(const torch::Tensor& slots, torch::Tensor& out, const std
 namespace mvp {
 namespace comm {
 
-constexpr int kGatherKernelStages = 3;
+constexpr int kGatherKernelStages = 6;
 constexpr int kGatherKernelSmem = kGatherKernelStages * kGatherChunk + 1024 + 64;
 
 __global__ void __launch_bounds__(128) shard_gather_kernel(ShardGather g, int* status) {
@@ -508,8 +508,8 @@ void peer_gather_shards(const std::vector<int64_t>& peer_bufs, const std::vector
   g.world = world;
   g.epoch = static_cast<unsigned long long>(epoch);
   g.timeout_ns = static_cast<unsigned long long>(timeout_ns);
-  // Bulk copies: each CTA keeps 3 x 32 KB in flight; 32 CTAs (~3 MB outstanding) cover NVLink's
-  // bandwidth-delay product with room to spare, and leave most SMs to the compute kernels.
+  // Bulk copies: each CTA keeps up to 5 x 32 KB loads in flight; 32 CTAs (~5 MB outstanding) cover
+  // NVLink's bandwidth-delay product with room to spare.
   const int64_t chunks = world * ((shard * 2 + kGatherChunk - 1) / kGatherChunk);
   g.ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, chunks)));
   const at::cuda::CUDAGuard guard(out.device());

@@ -399,35 +399,46 @@ __device__ __forceinline__ void shard_gather_cta_bulk(const ShardGather& g, int 
   const int64_t total = per_rank * g.world;
   const int64_t mine = total > cta ? (total - cta + g.ctas - 1) / g.ctas : 0;  // chunks cta, cta+ctas, ...
   uint8_t* dst_base = reinterpret_cast<uint8_t*>(g.dst);
-  bool alive = true;
-  for (int64_t base = 0, batch = 0; base < mine && alive; base += stages, ++batch) {
-    const int m = static_cast<int>(mine - base < stages ? mine - base : stages);
-    if (base > 0) bulk_wait_read_all();  // the previous batch's stores no longer read the stages
-    int64_t off[8];
-    uint32_t len[8];
-    for (int s = 0; s < m; ++s) {
-      const int64_t q = cta + (base + s) * g.ctas;
-      const int64_t r = q / per_rank, j = q - r * per_rank;
-      const int64_t b0 = j * kGatherChunk;
-      len[s] = static_cast<uint32_t>(shard_bytes - b0 < kGatherChunk ? shard_bytes - b0 : kGatherChunk);
-      off[s] = r * shard_bytes + b0;
-      mbar_arrive_expect_tx(&bars[s], len[s]);
-      bulk_load_to_smem(smem + static_cast<size_t>(s) * kGatherChunk,
-                        reinterpret_cast<const uint8_t*>(g.src[r]) + b0, len[s], &bars[s]);
+  // Ring of `stages` chunk buffers: chunk i lives in stage i % stages.  Loads run `stages` chunks ahead;
+  // a stage is refilled as soon as the store of its previous chunk has read it, so stages - 1 loads stay in
+  // flight while each store drains (a load's round trip over NVLink is the long pole).
+  auto chunk_of = [&](int64_t i, int64_t& off, uint32_t& len) -> const uint8_t* {
+    const int64_t q = cta + i * g.ctas;
+    const int64_t r = q / per_rank, b0 = (q - r * per_rank) * kGatherChunk;
+    len = static_cast<uint32_t>(shard_bytes - b0 < kGatherChunk ? shard_bytes - b0 : kGatherChunk);
+    off = r * shard_bytes + b0;
+    return reinterpret_cast<const uint8_t*>(g.src[r]) + b0;
+  };
+  auto issue_load = [&](int64_t i) {
+    int64_t off;
+    uint32_t len;
+    const uint8_t* src = chunk_of(i, off, len);
+    const int st = static_cast<int>(i % stages);
+    mbar_arrive_expect_tx(&bars[st], len);
+    bulk_load_to_smem(smem + static_cast<size_t>(st) * kGatherChunk, src, len, &bars[st]);
+  };
+  for (int64_t i = 0; i < mine && i < stages; ++i) issue_load(i);
+  const uint64_t t0 = globaltimer();
+  for (int64_t i = 0; i < mine; ++i) {
+    const int st = static_cast<int>(i % stages);
+    const uint32_t parity = static_cast<uint32_t>((i / stages) & 1);
+    if (!mbar_spin_bounded(&bars[st], parity, t0, g.timeout_ns)) {
+      record_status(status, kTimeoutPeer);
+      // let the loads already issued land (bounded) before the CTA's shared memory goes away
+      const uint64_t t1 = globaltimer();
+      for (int64_t w = i; w < mine && w < i + stages; ++w)
+        mbar_spin_bounded(&bars[w % stages], static_cast<uint32_t>((w / stages) & 1), t1, 200000000ull);
+      break;
     }
-    const uint64_t t0 = globaltimer();
-    for (int s = 0; s < m; ++s) {
-      if (!mbar_spin_bounded(&bars[s], static_cast<uint32_t>(batch & 1), t0, g.timeout_ns)) {
-        record_status(status, kTimeoutPeer);
-        // let the loads already issued land (bounded) before the CTA's shared memory goes away
-        const uint64_t t1 = globaltimer();
-        for (int w = s; w < m; ++w) mbar_spin_bounded(&bars[w], static_cast<uint32_t>(batch & 1), t1, 200000000ull);
-        alive = false;
-        break;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      bulk_store_from_smem(dst_base + off[s], smem + static_cast<size_t>(s) * kGatherChunk, len[s]);
-      bulk_commit();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    int64_t off;
+    uint32_t len;
+    chunk_of(i, off, len);
+    bulk_store_from_smem(dst_base + off, smem + static_cast<size_t>(st) * kGatherChunk, len);
+    bulk_commit();
+    if (i + stages < mine) {
+      bulk_wait_read_all();  // this stage's store has read it: refill the stage
+      issue_load(i + stages);
     }
   }
   bulk_wait_all();

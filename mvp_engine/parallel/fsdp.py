@@ -198,8 +198,11 @@ class NativeFSDP(nn.Module):
         # Peer-pull gathers ride in the next large GEMM (MVP_FSDP_GATHER=gemm, default) or run as a
         # stand-alone kernel on the comm stream (=kernel); copy CTAs and the smallest carrying GEMM:
         self._gather_in_gemm = os.environ.get("MVP_FSDP_GATHER", "gemm") == "gemm"
-        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "12"))
-        self._gather_min_mnk = int(os.environ.get("MVP_FSDP_GATHER_MIN_MNK", str(1 << 33)))
+        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "16"))
+        # a GEMM carries the gather when it runs at least about as long as the remote bytes take over NVLink:
+        # FLOPs >= remote bytes x 1500 (about 1.4 PFLOP/s over 0.9 of 770 GB/s, halved); MVP_FSDP_GATHER_MIN_MNK overrides the bound
+        self._gather_flops_per_byte = 1500.0
+        self._gather_min_mnk_env = os.environ.get("MVP_FSDP_GATHER_MIN_MNK")
         self.module = model
         self.group = group
         self.tp_group = tp_group
@@ -623,8 +626,11 @@ class NativeFSDP(nn.Module):
 
             self._flush_gather_job()
             wp = self._wpeer
+            remote = (self.world - 1) * u.shard * u.full.element_size()
+            min_flops = (int(self._gather_min_mnk_env) if self._gather_min_mnk_env is not None
+                         else int(remote * self._gather_flops_per_byte))
             job = _ops.GatherJob(wp["bufs"], wp["flag_ptrs"], self._wshard_off[u.index], u.shard, wp["epoch"],
-                                 u.full, self._gather_ctas, self._gather_min_mnk)
+                                 u.full, self._gather_ctas, min_flops)
             self._gather_job = (u.index, job)
             u.ag_event = None
             _ops.set_pending_gather(job)
