@@ -299,6 +299,56 @@ def bench_fsdp_gather(tokens: int, iters: int, copy_ctas: int, loopback_world: i
         dist.destroy_process_group()
 
 
+def bench_comm_loopback(tokens: int, hidden: int, mbytes: int, iters: int) -> None:
+    """The fused-collective kernels in one process, every "peer" a local buffer and every ready flag
+    published before launch (no wait can depend on another process): the kernels' own cost, for ncu.
+
+    * ``rs_pull_kernel``: pull reduce-scatter of an fp32 gradient unit of ``mbytes`` over two local "ranks";
+    * ``gemm_pair_tp`` column: [tokens, hidden] x [hidden, hidden]^T with per-256-row-slice readiness waits
+      (two slices, already published);
+    * ``gemm_pair_tp`` row: the same GEMM with its output rows routed to two destination buffers."""
+    from mvp_engine.ops import _ext
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ext = _ext.ext()
+    st = _ext.status_buffer(dev).data_ptr()
+    world = 2
+    n = (mbytes << 20) // 4 // (64 * world) * (64 * world)
+    shard = n // world
+    bufs = [torch.randn(n, device=dev) for _ in range(world)]
+    slots = [torch.zeros(8, dtype=torch.int64, device=dev) for _ in range(world)]
+    slots[0][1] = 1 << 60  # the other "rank" has published every sequence number already
+    out = torch.empty(shard, device=dev)
+    seq = [0]
+
+    def rs():
+        seq[0] += 1
+        ext.peer_reduce_scatter([b.data_ptr() for b in bufs], [sl.data_ptr() for sl in slots], slots[0].data_ptr(),
+                                0, 0, shard, seq[0], 1.0, out, None, st, 10**10)
+
+    x = torch.randn(tokens, hidden, device=dev).bfloat16()
+    w = torch.randn(hidden, hidden, device=dev).bfloat16()
+    y = torch.empty(tokens, hidden, device=dev, dtype=torch.bfloat16)
+    ready = torch.full((8,), 1 << 60, dtype=torch.int64, device=dev)
+    half = tokens // world
+    routed = [torch.empty(half, hidden, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+
+    def col():
+        ext.gemm_pair_tp(x, w, False, y, hidden, ready.data_ptr(), 1, half, 0, [], 0, 0, st, 10**10)
+
+    def row():
+        ext.gemm_pair_tp(x, w, False, None, hidden, 0, 0, 0, 0, [t.data_ptr() for t in routed], half, 0, st, 10**10)
+
+    res = {name: _time(fn, iters) for name, fn in (("rs_pull", rs), ("tp_column", col), ("tp_row_routed", row))}
+    _ext.check_status(dev)
+    ok = bool(torch.allclose(out, bufs[0][:shard] + bufs[1][:shard], atol=1e-5))
+    print(json.dumps({"mode": "loopback", "unit_mb": round(n * 4 / 2**20, 1), "tokens": tokens, "hidden": hidden,
+                      **{k + "_ms": round(v, 4) for k, v in res.items()},
+                      "rs_pull_gbs_read": round(n * 4 / res["rs_pull"] / 1e6, 1),
+                      "tp_tflops": round(2.0 * tokens * hidden * hidden / res["tp_column"] / 1e9, 1),
+                      "rs_correct": ok}), flush=True)
+
+
 def bench_tp_gemm(tokens: int, hidden: int, iters: int) -> None:
     """Tensor-parallel GEMMs with the collective fused over NVLink vs NCCL + GEMM (launch with torchrun).
 
@@ -587,7 +637,7 @@ def _hbm_peak() -> float:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer", "vision",
-                                     "fsdp_gather"])
+                                     "fsdp_gather", "comm_loopback"])
     ap.add_argument("--copy-ctas", type=int, default=12, help="fsdp_gather: copy CTAs carried by the GEMM")
     ap.add_argument("--loopback-world", type=int, default=2, help="fsdp_gather: local 'ranks' when run alone")
     ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
@@ -612,6 +662,8 @@ def main() -> None:
         bench_tp_gemm(args.tokens if args.tokens != 8192 else 4096, args.hidden, args.iters)
     elif args.what == "peer_rs":
         bench_peer_rs(args.mbytes, args.iters)
+    elif args.what == "comm_loopback":
+        bench_comm_loopback(args.tokens, args.hidden, args.mbytes, args.iters)
     elif args.what == "fsdp_gather":
         bench_fsdp_gather(args.tokens, args.iters, args.copy_ctas, args.loopback_world)
     elif args.what == "cp_layer":
