@@ -254,3 +254,58 @@ def test_watchdog_survives_a_transient_store_error():
         store.down = False
         me.stop()
         peer.stop()
+
+
+class _Crash(RuntimeError):
+    pass
+
+
+def _continuity_run(rank, world, port, out_dir, steps, resume, crash_at=None):
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = Path(__file__).resolve().parent.parent / "recipes" / "qwen3"
+    import_recipe_modules(root)
+    over = [f"loop.total_steps={steps}", "checkpoint.interval=2", "checkpoint.keep_n=5", "log.backends=[terminal]",
+            "model.pretrained_model_name_or_path=mvp/qwen3-tiny", "model.config_overrides.vocab_size=512",
+            "model.config_overrides.num_hidden_layers=2", "optim.mixed_precision=fp32",
+            "data.train_path=synthetic://text?vocab=512&min_len=16&max_len=96", "data.max_seq_len=128",
+            "optim.global_batch_size=2", "model.gradient_checkpointing.enabled=false"]
+    if resume:
+        over.append("resume=latest")
+    cfg = load_smoke_test_config(root, "synthetic_8b", output_dir=Path(out_dir), run_id="cont",
+                                 config_overrides=tuple(over))
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    losses = {}
+    real_post = eng.train_post_step
+
+    def record(ctx):
+        real_post(ctx)
+        losses[eng.step] = float(eng.last_logs["train/loss"])
+        if crash_at is not None and eng.step == crash_at:
+            raise _Crash  # the process "dies" after this step's update, before its checkpoint
+
+    eng.train_post_step = record
+    eng.before_train()
+    try:
+        eng.do_train()
+    except _Crash:
+        return losses
+    eng.after_train()
+    return losses
+
+
+def test_resume_continues_the_loss_curve(tmp_path):
+    """A run that dies during step 3 of 4 resumes from its step-2 checkpoint: steps 3 and 4 reproduce the
+    uninterrupted run (model, optimizer, scheduler, RNG and the data loader's position all come back)."""
+    from mvp_engine.testing import spawn_workers
+
+    straight = spawn_workers(_continuity_run, 1, str(tmp_path / "a"), 4, False, timeout=600)[0]
+    first = spawn_workers(_continuity_run, 1, str(tmp_path / "b"), 4, False, 3, timeout=600)[0]  # dies in step 3
+    resumed = spawn_workers(_continuity_run, 1, str(tmp_path / "b"), 4, True, timeout=600)[0]
+    assert sorted(resumed) == [3, 4], resumed
+    for step in (1, 2):
+        assert abs(first[step] - straight[step]) < 1e-6, (first, straight)
+    for step in (3, 4):
+        assert abs(resumed[step] - straight[step]) < 1e-5 * abs(straight[step]), (resumed, straight)
