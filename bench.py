@@ -387,6 +387,7 @@ def run_ours(args) -> None:
                 "d2h_bytes_per_step": 8 * 2 + 4 * 1,
                 "api": f"recipes.{recipe} {EngineClass.__name__}.train_step(host micro-batches)"},
         "gpu_launches": int(launches),
+        "peak_mem_gib": round(torch.cuda.max_memory_allocated(engine.device) / 2**30, 1),
         "loss_last": round(losses[-1], 4) if losses else None,
         "impl": "ours",
     }
