@@ -25,6 +25,7 @@ KERNELS_PER_CALL = {
     "peer_publish": 1, "peer_slot_sum_f32": 1, "gemm_ulysses": 1,
     "layernorm_fwd": 1, "layernorm_bwd": 3, "bias_gelu_fwd": 1, "bias_gelu_bwd": 2, "vision_rope_fwd": 1,
     "vision_rope_bwd": 1, "bias_residual_fwd": 1, "bias_grad": 2,
+    "peer_gather_shards": 1, "publish_epoch": 1, "gemm_pair_gather": 1,
 }
 launch_count = 0
 counting = False
