@@ -421,7 +421,10 @@ class Qwen3ForCausalLM(nn.Module):
                 raise NotImplementedError("logits under sequence parallelism: pass labels for the loss")
             return {"logits": ops.linear(h, w).view(*input_ids.shape, -1)}
         flat_labels = (shift_labels if shift_labels is not None else _shift_labels(labels)).reshape(-1)[local]
-        loss = ops.fused_linear_cross_entropy(h, w, flat_labels, self.loss_chunk_size)
+        # the training loop may promise the loss's per-token gradient (``loss_grad_hint``): the LM head then
+        # finishes its backward inside the forward, without recomputing the logits (not under TP)
+        hint = getattr(self, "loss_grad_hint", None) if tp is None else None
+        loss = ops.fused_linear_cross_entropy(h, w, flat_labels, self.loss_chunk_size, grad_hint=hint)
         return {"loss": loss, "logits": None}
 
     # ------------------------------------------------------------------ flops

@@ -595,25 +595,59 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, anchor: Optional[torch.Tensor]
 
 # ------------------------------------------------- fused linear cross-entropy
 class _LinearCE(torch.autograd.Function):
+    """Chunked LM head + token cross-entropy.
+
+    Without ``grad_hint`` the forward keeps only the row LSEs and the backward recomputes each logits
+    chunk.  With ``grad_hint = c`` the caller promises that the loss's gradient will be ``c`` for every
+    token (the token-normalised loss with a fixed divisor and no loss guard): the forward then finishes
+    each chunk's backward while its logits are still at hand -- softmax minus one-hot in place, the input
+    gradient GEMM into a saved ``dh`` and the weight gradient straight into its accumulator -- so the
+    logits GEMM runs once instead of twice.  The backward only rescales ``dh`` rows by ``g / c`` (exact
+    for any per-token ``g``; the weight gradient needs the promise)."""
+
     @staticmethod
-    def forward(ctx, h, w, labels, chunk):
+    def forward(ctx, h, w, labels, chunk, grad_hint):
         T = h.shape[0]
+        ext = _ext.ext()
         losses = torch.empty(T, dtype=torch.float32, device=h.device)
         lses = torch.empty(T, dtype=torch.float32, device=h.device)
+        ctx.chunk = chunk
+        ctx.acc = grad_acc(w)
+        ctx.hint = grad_hint
+        early = grad_hint is not None
+        if early:
+            dh = torch.empty_like(h)
+            g_hint = torch.full((T,), float(grad_hint), dtype=torch.float32, device=h.device)
+            want_dw = ctx.acc is None and ctx.needs_input_grad[1]
+            dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device) if want_dw else None
+            target = ctx.acc if ctx.acc is not None else dw
+            ctx.w_dtype = w.dtype
         for s in range(0, T, chunk):
             e = min(T, s + chunk)
             logits = gemm(h[s:e], w)
-            loss, lse = _ext.ext().ce_fwd(logits, labels[s:e])
+            loss, lse = ext.ce_fwd(logits, labels[s:e])
             losses[s:e] = loss
             lses[s:e] = lse
+            if early:
+                ext.ce_bwd_(logits, labels[s:e], lse, g_hint[s:e])
+                gemm(logits, w, b_mn=True, out=dh[s:e])
+                if target is not None:
+                    gemm(logits, h[s:e], a_mn=True, b_mn=True, out=target, accumulate=True)
             del logits
-        ctx.save_for_backward(h, w, labels, lses)
-        ctx.chunk = chunk
-        ctx.acc = grad_acc(w)
+        if early:
+            ctx.save_for_backward(dh, dw if dw is not None else torch.empty(0, device=h.device))
+        else:
+            ctx.save_for_backward(h, w, labels, lses)
         return losses
 
     @staticmethod
     def backward(ctx, g):
+        if ctx.hint is not None:
+            dh, dw = ctx.saved_tensors
+            ratio = (g.float() / ctx.hint).reshape(-1, 1) if g.numel() > 1 else g.float().reshape(1, 1) / ctx.hint
+            dx = (dh.float() * ratio).to(dh.dtype)
+            w_grad = dw.to(ctx.w_dtype) if dw.numel() else None
+            return dx, w_grad, None, None, None
         h, w, labels, lses = ctx.saved_tensors
         chunk = ctx.chunk
         g = g.float()
@@ -634,21 +668,25 @@ class _LinearCE(torch.autograd.Function):
             if target is not None:
                 gemm(logits, h[s:e], a_mn=True, b_mn=True, out=target, accumulate=True)
             del logits
-        return dh, (dw.to(w.dtype) if dw is not None else None), None, None
+        return dh, (dw.to(w.dtype) if dw is not None else None), None, None, None
 
 
 def fused_linear_cross_entropy(
-    h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, chunk_size: int = 4096
+    h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, chunk_size: int = 4096,
+    grad_hint: Optional[float] = None,
 ) -> torch.Tensor:
     """Per-token CE of ``h @ w.T`` against ``labels`` (ignore index -100), chunked so the
-    full ``[T, V]`` logits never exist; the backward recomputes each logits chunk."""
+    full ``[T, V]`` logits never exist; the backward recomputes each logits chunk, unless ``grad_hint``
+    (the promised, uniform per-token gradient of the loss) lets the forward finish the backward of each
+    chunk right away (see :class:`_LinearCE`)."""
     if not _native(h):
         out = []
         for s in range(0, h.shape[0], chunk_size):
             lg = F.linear(h[s : s + chunk_size], w.to(h.dtype))
             out.append(F.cross_entropy(lg.float(), labels[s : s + chunk_size], ignore_index=-100, reduction="none"))
         return torch.cat(out) if out else h.new_zeros(0, dtype=torch.float32)
-    return _LinearCE.apply(h.contiguous(), w, labels.contiguous(), int(chunk_size))
+    hint = None if grad_hint is None or not torch.is_grad_enabled() else float(grad_hint)
+    return _LinearCE.apply(h.contiguous(), w, labels.contiguous(), int(chunk_size), hint)
 
 
 # ------------------------------------------------------------ optimizer ops

@@ -142,8 +142,21 @@ class Qwen3Engine(Engine):
 
     _MODEL_KEYS = ("input_ids", "labels", "shift_labels", "position_ids", "cu_seq_lens_q", "max_length_q")
 
+    def _loss_grad_hint(self):
+        """The per-token gradient the loss will receive, when it is fixed in advance: the token loss is
+        backpropagated as ``sum / divisor`` and nothing can change that factor (no loss-spike guard, no fp16
+        loss scaling).  The model's LM head then runs its backward in the forward (one logits GEMM, not two)."""
+        d = self.config
+        if d.optim.loss_spike_skip_multiplier is not None or self.dtype == torch.float16:
+            return None
+        divisor = int(d.data.batch_size) * int(d.data.max_seq_len) * int(d.optim.gradient_accumulation_steps)
+        return float(torch.tensor(1.0, dtype=torch.float32) / divisor)  # the fp32 value autograd will pass
+
     def forward_step(self, ctx: TrainStepContext) -> None:
         data = ctx.data
+        model = self.unwrapped_model
+        if hasattr(model, "loss_chunk_size"):
+            model.loss_grad_hint = self._loss_grad_hint()
         with torch.autocast(device_type=self.device_type, dtype=self.dtype,
                             enabled=self.dtype != torch.float32 and self.device_type == "cuda"):
             outputs = self.model(**{k: data[k] for k in self._MODEL_KEYS if k in data})

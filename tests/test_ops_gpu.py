@@ -277,6 +277,39 @@ def test_fused_linear_ce():
 
 
 @cuda
+def test_fused_linear_ce_backward_in_forward():
+    """With the loss gradient promised up front, the LM head's backward runs inside the forward: same loss and
+    gradients as the fp32 reference; input gradients also follow a non-uniform per-token gradient."""
+    ops = _ops()
+    torch.manual_seed(9)
+    T, H, V = 600, 256, 5000
+    div = 1000.0
+    hint = float(torch.tensor(1.0, dtype=torch.float32) / div)
+    h = (0.5 * torch.randn(T, H, device="cuda")).bfloat16().requires_grad_()
+    w = (0.05 * torch.randn(V, H, device="cuda")).bfloat16().requires_grad_()
+    labels = torch.randint(0, V, (T,), device="cuda")
+    labels[::7] = -100
+    loss = ops.fused_linear_cross_entropy(h, w, labels, chunk_size=256, grad_hint=hint)
+    (loss.sum() / div).backward()
+    hf = h.detach().float().requires_grad_()
+    wf = w.detach().float().requires_grad_()
+    lf = torch.nn.functional.cross_entropy(hf @ wf.t(), labels, ignore_index=-100, reduction="none")
+    (lf.sum() / div).backward()
+    assert _rel_err(loss, lf) < 1e-2
+    assert _rel_err(h.grad, hf.grad) < 2e-2
+    assert _rel_err(w.grad, wf.grad) < 2e-2
+    # per-token weights: the input gradient rows are rescaled exactly
+    h2 = h.detach().clone().requires_grad_()
+    weights = torch.rand(T, device="cuda")
+    loss2 = ops.fused_linear_cross_entropy(h2, w.detach(), labels, chunk_size=256, grad_hint=hint)
+    (loss2 * weights).sum().div(div).backward()
+    hf2 = h.detach().float().requires_grad_()
+    lf2 = torch.nn.functional.cross_entropy(hf2 @ wf.detach().t(), labels, ignore_index=-100, reduction="none")
+    (lf2 * weights).sum().div(div).backward()
+    assert _rel_err(h2.grad, hf2.grad) < 2e-2
+
+
+@cuda
 def test_adamw_matches_torch():
     ops = _ops()
     torch.manual_seed(8)
