@@ -131,22 +131,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for half of the softmax exponentials so that they do not all queue on the MUFU
-// unit (the method FlashAttention-4 describes for Blackwell: Cody-Waite range reduction plus a short
-// polynomial).  x = j + f with j = round(x) (added to the exponent bits) and f in [-0.5, 0.5];
-// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3, coefficients fitted for this kernel (Lawson-weighted least squares on
-// Chebyshev nodes), maximum relative error 7.5e-5 -- far below the bf16 rounding of P that follows.
-// x < -125 (masked keys: -inf) gives exactly 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float xc = fmaxf(x, -125.f);
-  const float t = xc + 12582912.f;  // 1.5 * 2^23: the integer part lands in the low mantissa bits
-  const int j = __float_as_int(t) - 0x4B400000;
-  const float f = xc - (t - 12582912.f);
-  const float poly = fmaf(fmaf(fmaf(0.0551716648f, f, 0.2426111251f), f, 0.6932609677f), f, 0.9999280572f);
-  const float r = __int_as_float(__float_as_int(poly) + (j << 23));
-  return x < -125.f ? 0.f : r;
-}
-
 // D[tmem] (+)= A[tmem] * B[smem]: tcgen05.mma with the A operand (P) read from tensor memory.
 __device__ __forceinline__ void mma_p_tmem(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -411,7 +395,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           const float e0 = ex2_approx(fmaf(s[c * 32 + 2 * t], p.scale_log2, neg_m));
-          const float e1 = ex2_poly(fmaf(s[c * 32 + 2 * t + 1], p.scale_log2, neg_m));  // FMA pipe
+          const float e1 = ex2_approx(fmaf(s[c * 32 + 2 * t + 1], p.scale_log2, neg_m));
           rs8[(2 * t) & 7] += e0;
           rs8[(2 * t + 1) & 7] += e1;
           pk[t] = pack_bf16x2(e0, e1);
@@ -832,8 +816,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int r = col0 + t;
-            const float xe = fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[r]);
-            const float pe = (t & 1) ? ex2_poly(xe) : ex2_approx(xe);  // odd columns on the FMA pipe
+            const float pe = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[r]));
             pv[t] = pe;
             ds[t] = pe * (__uint_as_float(dr[t]) - s_delta[r]) * p.scale;
           }

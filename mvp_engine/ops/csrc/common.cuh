@@ -361,6 +361,9 @@ __device__ __forceinline__ void bulk_store_from_smem(void* gdst, const void* ssr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_one_pending() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity, uint64_t t0, uint64_t limit_ns) {
@@ -436,9 +439,11 @@ __device__ __forceinline__ void shard_gather_cta_bulk(const ShardGather& g, int 
     chunk_of(i, off, len);
     bulk_store_from_smem(dst_base + off, smem + static_cast<size_t>(st) * kGatherChunk, len);
     bulk_commit();
-    if (i + stages < mine) {
-      bulk_wait_read_all();  // this stage's store has read it: refill the stage
-      issue_load(i + stages);
+    // Refill the stage of the previous chunk once its store has read it (the store just issued may still
+    // be reading): stores overlap each other and stages - 1 loads stay in flight.
+    if (i > 0 && i - 1 + stages < mine) {
+      bulk_wait_read_one_pending();
+      issue_load(i - 1 + stages);
     }
   }
   bulk_wait_all();

@@ -638,7 +638,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attention", "peer_rs", "tp_gemm", "cp_attention", "cp_layer", "vision",
                                      "fsdp_gather", "comm_loopback"])
-    ap.add_argument("--copy-ctas", type=int, default=12, help="fsdp_gather: copy CTAs carried by the GEMM")
+    ap.add_argument("--copy-ctas", type=int, default=24, help="fsdp_gather: copy CTAs carried by the GEMM")
     ap.add_argument("--loopback-world", type=int, default=2, help="fsdp_gather: local 'ranks' when run alone")
     ap.add_argument("--impls", default="ring,ring_fused,ulysses", help="cp_attention: cases to time")
     ap.add_argument("--docs", default="256,4096", help="attention: document lengths U[lo, hi]")

@@ -198,7 +198,7 @@ class NativeFSDP(nn.Module):
         # Peer-pull gathers ride in the next large GEMM (MVP_FSDP_GATHER=gemm, default) or run as a
         # stand-alone kernel on the comm stream (=kernel); copy CTAs and the smallest carrying GEMM:
         self._gather_in_gemm = os.environ.get("MVP_FSDP_GATHER", "gemm") == "gemm"
-        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "16"))
+        self._gather_ctas = int(os.environ.get("MVP_FSDP_GATHER_CTAS", "24"))
         # a GEMM carries the gather when it runs at least about as long as the remote bytes take over NVLink:
         # FLOPs >= remote bytes x 1500 (about 1.4 PFLOP/s over 0.9 of 770 GB/s, halved); MVP_FSDP_GATHER_MIN_MNK overrides the bound
         self._gather_flops_per_byte = 1500.0
