@@ -248,7 +248,8 @@ def run_ours(args) -> None:
         kept += 2 * H + (cfgm.num_attention_heads + cfgm.num_key_value_heads) * cfgm.head_dim
     per_layer = local_tokens * 2 * kept * 1.1
     head_ws = 4096 * cfgm.vocab_size * 2 * 2 + args.seq_len * H * 16
-    # 7 GiB of slack (the one-GPU headline peaked at 160.7 of 178 GiB with 3 layers recomputed); the multimodal workload also keeps the vision tower's per-block checkpoint inputs,
+    # 7 GiB of slack (the one-GPU headline peaked at 160.7 of 178 GiB with 3 layers recomputed); the
+    # multimodal workload also keeps the vision tower's per-block checkpoint inputs,
     # the image embeddings and a block's recomputed activations, which vary with the images of a pack
     budget = free - head_ws - (7 << 30) - int(wl.get("reserve_gb", 0)) * (1 << 30)
     keep = max(0, min(L, int(budget // per_layer)))
