@@ -20,6 +20,7 @@
 // The bound (timeout_ns) is a launch argument: 10 s in training, far above
 // the millisecond skew between ranks that run the same unit order.
 #include <cuda_runtime.h>
+#include <cstdlib>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -193,10 +194,18 @@ void peer_reduce_scatter(const std::vector<int64_t>& peer_bufs, const std::vecto
   p.scale = static_cast<float>(scale);
   p.out = out.data_ptr<float>();
   p.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
-  // Two CTAs per SM keep ~10 MB of loads in flight (enough for NVLink); they need no shared memory
-  // and few registers, so they co-reside with the persistent GEMM / attention CTAs of the backward.
+  // CTAs per SM (MVP_RS_CTAS_PER_SM, default 2): two keep ~10 MB of loads in flight, enough for NVLink.
+  // The kernel runs beside the backward's GEMM / attention CTAs, and at 126 registers per thread two of its
+  // CTAs fill an SM's register file, so fewer CTAs trade reduce-scatter speed for co-residency.
+  static const int per_sm = [] {
+    const char* env = std::getenv("MVP_RS_CTAS_PER_SM");
+    const int v = env != nullptr ? std::atoi(env) : 2;
+    return v < 1 ? 1 : (v > 4 ? 4 : v);
+  }();
   const int64_t n4 = shard / 4;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(2 * 148, (n4 + 1023) / 1024)));
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  const int blocks =
+      static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(per_sm) * sms, (n4 + 1023) / 1024)));
   rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
