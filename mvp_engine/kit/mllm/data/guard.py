@@ -1,4 +1,7 @@
-"""Multimodal data guards (reference: mvp_engine/kit/mllm/data/guard.py:30-452)."""
+"""Multimodal data guards: the LLM guards' rule tables plus image checks, and the text-only batch guard.
+
+Public names and drop reasons of the reference's ``mvp_engine/kit/mllm/data/guard.py:30-452``.
+"""
 
 from __future__ import annotations
 
@@ -6,46 +9,59 @@ from typing import Any, Mapping, Sequence
 
 import torch
 
-from ...llm.data.guard import CheckResult, LLMGuard
+from ...llm.data.guard import CheckResult, LLMGuard, Rule, _bad_vector
 from .sample import MLLMSample
 
 
 class MLLMGuard(LLMGuard):
-    pass
+    """Rule-table guard (see :class:`~mvp_engine.kit.llm.data.guard.LLMGuard`) for multimodal items."""
 
 
 class MLLMRawRowGuard(MLLMGuard):
+    """Raw rows: dicts whose ``images`` (if any) is a list, accepted by the schema handler."""
+
     def __init__(self, assemble_context: Any = None, *, schema_handler=None, verbose: bool = True) -> None:
         super().__init__(assemble_context, verbose=verbose)
         self.schema_handler = schema_handler
 
+    def rules(self) -> Sequence[Rule]:
+        return (("raw.not_dict", lambda row: not isinstance(row, dict)),
+                ("raw.invalid_images", lambda row: row.get("images") is not None
+                 and not isinstance(row["images"], (list, tuple))))
+
     def check(self, sample: Any) -> CheckResult:
-        if not isinstance(sample, dict):
-            return CheckResult(False, "raw.not_dict")
-        imgs = sample.get("images")
-        if imgs is not None and not isinstance(imgs, (list, tuple)):
-            return CheckResult(False, "raw.invalid_images")
-        if self.schema_handler is not None:
-            reason = self.schema_handler.check_row(sample)
-            if reason is not None:
-                return CheckResult(False, reason)
-        return CheckResult(True)
+        verdict = super().check(sample)
+        if not verdict.is_valid or self.schema_handler is None:
+            return verdict
+        reason = self.schema_handler.check_row(sample)  # the handler names its own reason
+        return CheckResult(reason is None, reason)
+
+
+def _mllm_unsupervised(sample: MLLMSample) -> bool:
+    ignore = sample.spec.tokenization_handler.ignore_index
+    return all(lab == ignore for lab in sample.labels)
 
 
 class MLLMSampleGuard(MLLMGuard):
-    def check(self, sample: Any) -> CheckResult:
-        if not isinstance(sample, MLLMSample):
-            return CheckResult(False, "sample.invalid_type")
-        sample.tokenize()
-        if sample.token_length <= 0:
-            return CheckResult(False, "sample.empty_tokens")
-        ign = sample.spec.tokenization_handler.ignore_index
-        if all(lab == ign for lab in sample.labels):
-            return CheckResult(False, "sample.no_supervised_tokens")
-        return CheckResult(True)
+    """Tokenised samples: non-empty, with at least one supervised label."""
+
+    def rules(self) -> Sequence[Rule]:
+        return (("sample.invalid_type", lambda s: not isinstance(s, MLLMSample)),
+                ("sample.empty_tokens", lambda s: s.tokenize().token_length <= 0),
+                ("sample.no_supervised_tokens", _mllm_unsupervised))
+
+
+def _image_tokens_disagree(item: dict, image_token_id: int, merge_size: int) -> bool:
+    """The number of image placeholder tokens differs from the merged patch count of the images."""
+    placeholders = int(item["input_ids"].eq(image_token_id).sum())
+    merged = int(item["image_grid_thw"].prod(-1).sum()) // merge_size ** 2
+    return placeholders != merged
 
 
 class MLLMModelInputGuard(MLLMGuard):
+    """Collated multimodal inputs: 1-D non-empty tensors, image placeholders matching the images'
+    merged patches, some supervised label after the shift."""
+
     def __init__(self, assemble_context: Any = None, *, ignore_index: int = -100, image_token_id: int | None = None,
                  merge_size: int = 2, verbose: bool = True) -> None:
         super().__init__(assemble_context, verbose=verbose)
@@ -53,22 +69,16 @@ class MLLMModelInputGuard(MLLMGuard):
         self.image_token_id = image_token_id
         self.merge_size = merge_size
 
-    def check(self, sample: Any) -> CheckResult:
-        if not isinstance(sample, dict) or sample.get("__empty__"):
-            return CheckResult(False, "model_input.empty")
-        for key in ("input_ids", "attention_mask", "labels", "pack_segment_ids"):
-            v = sample.get(key)
-            if not isinstance(v, torch.Tensor) or v.ndim != 1 or v.numel() == 0:
-                return CheckResult(False, f"model_input.invalid_{key}")
-        if self.image_token_id is not None and "image_grid_thw" in sample:
-            n_tok = int((sample["input_ids"] == self.image_token_id).sum())
-            n_feat = int(sample["image_grid_thw"].prod(-1).sum()) // self.merge_size ** 2
-            if n_tok != n_feat:
-                return CheckResult(False, "model_input.image_token_mismatch")
-        shifted = torch.nn.functional.pad(sample["labels"], (0, 1), value=self.ignore_index)[1:]
-        if not bool(shifted.ne(self.ignore_index).any()):
-            return CheckResult(False, "model_input.no_supervised_tokens")
-        return CheckResult(True)
+    def rules(self) -> Sequence[Rule]:
+        vectors = ("input_ids", "attention_mask", "labels", "pack_segment_ids")
+        token_id = self.image_token_id
+        return (
+            ("model_input.empty", lambda x: not isinstance(x, dict) or bool(x.get("__empty__"))),
+            *((f"model_input.invalid_{k}", _bad_vector(k)) for k in vectors),
+            ("model_input.image_token_mismatch", lambda x: token_id is not None and "image_grid_thw" in x
+             and _image_tokens_disagree(x, token_id, self.merge_size)),
+            ("model_input.no_supervised_tokens", lambda x: not bool(x["labels"][1:].ne(self.ignore_index).any())),
+        )
 
 
 class MLLMTextOnlyBatchGuard:
