@@ -298,12 +298,24 @@ __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
   }
   const bool lo = lane < 16;
   const __nv_bfloat16* row = a.qkv + static_cast<int64_t>(t) * a.ld_qkv + lane * 4;
-#pragma unroll 4
-  for (int hd = 0; hd < heads; ++hd) {
+  // Heads in groups of kGroup: every load of a group is issued before the group's first store (the
+  // compiler cannot move a load above a store to a possibly aliasing output), so kGroup row loads are in
+  // flight per warp instead of one.
+  constexpr int kGroup = 8;
+  for (int h0 = 0; h0 < heads; h0 += kGroup) {
+    uint2 raw[kGroup];
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j)
+      raw[j] = h0 + j < heads ? *reinterpret_cast<const uint2*>(row + static_cast<int64_t>(h0 + j) * D)
+                              : make_uint2(0u, 0u);
+#pragma unroll
+  for (int j = 0; j < kGroup; ++j) {
+    const int hd = h0 + j;
+    if (hd >= heads) break;
     const bool is_q = hd < a.Hq;
     float x[4];
     {
-      const uint2 u = *reinterpret_cast<const uint2*>(row + static_cast<int64_t>(hd) * D);
+      const uint2 u = raw[j];
       const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
       const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
       x[0] = p0.x; x[1] = p0.y; x[2] = p1.x; x[3] = p1.y;
@@ -325,6 +337,7 @@ __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
     u.x = pack_bf16x2(o[0], o[1]);
     u.y = pack_bf16x2(o[2], o[3]);
     *reinterpret_cast<uint2*>(dst + lane * 4) = u;
+  }
   }
 }
 
@@ -384,19 +397,38 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
     }
     int owner = 0, lrow = 0;
     if (a.route.dst[0] != nullptr) ulysses_home(a.route, t, owner, lrow);
-#pragma unroll 4
-    for (int hd = 0; hd < heads; ++hd) {
+    // Heads in groups of kGroup, all loads of a group (gradient, input row, row scale) before its first
+    // store: the stores may alias the inputs as far as the compiler knows, so without this each head would
+    // wait for its own loads.
+    constexpr int kGroup = 8;
+    for (int h0 = 0; h0 < heads; h0 += kGroup) {
+      float gs[kGroup][4], xs[kGroup][4], rs[kGroup];
+#pragma unroll
+      for (int j = 0; j < kGroup; ++j) {
+        const int hd = min(h0 + j, heads - 1);  // a repeated head past the end is loaded but not used
+        const bool is_q = hd < a.Hq;
+        load_bf16x4(is_q ? a.dq + (static_cast<int64_t>(t) * a.Hq + hd) * D + lane * 4
+                         : a.dk + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D + lane * 4, gs[j]);
+        load_bf16x4(a.qkv + static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(hd) * D + lane * 4, xs[j]);
+        rs[j] = a.rstd[static_cast<int64_t>(t) * heads + hd];
+      }
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j) {
+      const int hd = h0 + j;
+      if (hd >= heads) break;
       const bool is_q = hd < a.Hq;
       float g[4], x[4];
-      load_bf16x4(is_q ? a.dq + (static_cast<int64_t>(t) * a.Hq + hd) * D + lane * 4
-                       : a.dk + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D + lane * 4, g);
-      load_bf16x4(a.qkv + static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(hd) * D + lane * 4, x);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        g[i] = gs[j][i];
+        x[i] = xs[j][i];
+      }
       float gp[4], dy[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) gp[i] = __shfl_xor_sync(0xffffffffu, g[i], 16);
 #pragma unroll
       for (int i = 0; i < 4; ++i) dy[i] = lo ? (g[i] * c[i] + gp[i] * sn[i]) : (g[i] * c[i] - gp[i] * sn[i]);
-      const float rstd = a.rstd[static_cast<int64_t>(t) * heads + hd];
+      const float rstd = rs[j];
       float dot = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) dot += dy[i] * (is_q ? wq[i] : wk[i]) * x[i] * rstd;
@@ -417,6 +449,7 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
       u.x = pack_bf16x2(dx[0], dx[1]);
       u.y = pack_bf16x2(dx[2], dx[3]);
       *reinterpret_cast<uint2*>(dst) = u;
+    }
     }
   }
 #pragma unroll
