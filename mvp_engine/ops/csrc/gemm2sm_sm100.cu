@@ -79,7 +79,55 @@ struct Params {
   // other CTAs compute this GEMM's tiles.  Nothing in the GEMM reads the gathered buffer.
   ShardGather gather{};
   int gemm_clusters = 0;  // clusters that compute tiles (set at launch)
+  // Work split (set at launch): tiles [0, dp_tiles) are whole-tile units, tile t on cluster
+  // t % gemm_clusters; the k-blocks of tiles [dp_tiles, tiles) are spread evenly over clusters
+  // 0 .. sk_clusters-1 (stream-K tail; only for the fp32 accumulate epilogue, whose split tiles are
+  // summed with vector reductions).  sk_clusters == 0: every tile is a whole-tile unit.
+  int dp_tiles = 0;
+  int sk_clusters = 0;
 };
+
+// The units of work of one cluster, in the order all three roles walk them: its whole tiles first,
+// then its contiguous share of the tail's (tile, k-block) iterations, cut at tile boundaries.
+struct WorkList {
+  int clusters, dp_tiles, num_kb;
+  int t;                 // next whole tile
+  long long it, it_end;  // next / end tail iteration
+  __device__ WorkList(const Params& p, int cluster, int num_kb_)
+      : clusters(p.gemm_clusters), dp_tiles(p.dp_tiles), num_kb(num_kb_), t(cluster), it(0), it_end(0) {
+    if (cluster < p.sk_clusters) {
+      const int num_m = (p.M + TILE - 1) / TILE, num_n = (p.N + TILE - 1) / TILE;
+      const long long total = static_cast<long long>(num_m * num_n - p.dp_tiles) * num_kb;
+      it = total * cluster / p.sk_clusters;
+      it_end = total * (cluster + 1) / p.sk_clusters;
+    }
+  }
+  // Next unit: tile index and k-block range [kb0, kb1); false when the cluster is done.
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (t < dp_tiles) {
+      tile = t;
+      kb0 = 0;
+      kb1 = num_kb;
+      t += clusters;
+      return true;
+    }
+    if (it < it_end) {
+      tile = dp_tiles + static_cast<int>(it / num_kb);
+      kb0 = static_cast<int>(it % num_kb);
+      kb1 = static_cast<int>(min(static_cast<long long>(num_kb), kb0 + (it_end - it)));
+      it += kb1 - kb0;
+      return true;
+    }
+    return false;
+  }
+};
+
+// Fire-and-forget fp32 x4 reduction into global memory (split tiles of the accumulate epilogue).
+__device__ __forceinline__ void red_add_f32x4(float* addr, float4 v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -183,10 +231,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   const uint32_t crank = cluster_ctarank();  // 0 = leader
   const int cluster_id = blockIdx.x >> 1;
-  const int num_clusters = p.gemm_clusters;
   const int num_m = (p.M + TILE - 1) / TILE;
   const int num_n = (p.N + TILE - 1) / TILE;
-  const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -224,7 +270,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued_mask = 0, issued_phase = 0;
       uint32_t ready = 0;  // A row slices already seen published
       bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      WorkList work(p, cluster_id, num_kb);
+      int t, kb0, kb1;
+      while (ok && work.next(t, kb0, kb1)) {
         int tm, tn;
         tile_coords(t, num_m, num_n, p.group_m, tm, tn);
         tm = (tm + p.a_first_row / TILE) % num_m;
@@ -247,7 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ready |= 1u << j;
           }
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, abort_flag, p.status, kTimeoutProducer)) {
             ok = false;
             break;
@@ -293,13 +341,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+      WorkList work(p, cluster_id, num_kb);
+      int t, kb0, kb1;
+      for (; ok && work.next(t, kb0, kb1); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.status, kTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * TILE;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag, p.status, kTimeoutMma)) {
             ok = false;
             break;
@@ -314,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             else adesc = make_smem_desc_sw128(a_base + k * 2048, 64 * BK * 2, 1024);
             if constexpr (!B_MN) bdesc = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
             else bdesc = make_smem_desc_sw128(b_base + k * 2048, 64 * BK * 2, 1024);
-            mma_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit_pair(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -334,10 +384,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row_in_tile = crank * HALF + sub * 32 + lane;
     const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     int local = 0;
-    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
+    WorkList work(p, cluster_id, num_kb);
+    int t, kb0, kb1;
+    for (; work.next(t, kb0, kb1); ++local) {
       int tm, tn;
       tile_coords(t, num_m, num_n, p.group_m, tm, tn);
       tm = (tm + p.a_first_row / TILE) % num_m;
+      // a tile split over several units is summed with reductions; a whole tile is read, added, written
+      const bool split = kb0 != 0 || kb1 != num_kb;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!__all_sync(0xffffffffu,
@@ -385,7 +439,9 @@ __global__ void __launch_bounds__(THREADS, 1)
               dst[v] = q;
             }
           } else {
-            for (int j = 0; j < 32 && n + j < p.N; ++j) C[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+#pragma unroll
+            for (int j = 0; j < 32; ++j)  // constant indices keep r[] in registers
+              if (n + j < p.N) C[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
           }
         } else {
           float* C = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
@@ -396,6 +452,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               float4 q = make_float4(__uint_as_float(r[4 * v + 0]), __uint_as_float(r[4 * v + 1]),
                                      __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
               if constexpr (EPI == kAccumF32) {
+                if (split) {
+                  red_add_f32x4(reinterpret_cast<float*>(dst + v), q);
+                  continue;
+                }
                 const float4 o = dst[v];
                 q.x += o.x;
                 q.y += o.y;
@@ -405,9 +465,17 @@ __global__ void __launch_bounds__(THREADS, 1)
               dst[v] = q;
             }
           } else {
-            for (int j = 0; j < 32 && n + j < p.N; ++j) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (n + j >= p.N) continue;
               float val = __uint_as_float(r[j]);
-              if constexpr (EPI == kAccumF32) val += C[j];
+              if constexpr (EPI == kAccumF32) {
+                if (split) {
+                  atomicAdd(C + j, val);
+                  continue;
+                }
+                val += C[j];
+              }
               C[j] = val;
             }
           }
@@ -429,6 +497,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+constexpr int kMinSkBlocks = 8;  // smallest stream-K piece, in k-blocks of BK
+
+// Stream-K tail for the accumulate epilogue; MVP_GEMM_STREAMK=0 turns it off (whole tiles only).
+inline bool stream_k_enabled() {
+  static const bool on = [] {
+    const char* env = std::getenv("MVP_GEMM_STREAMK");
+    return env == nullptr || env[0] != '0';
+  }();
+  return on;
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int num_sms, cudaStream_t stream) {
   auto kern = gemm2sm_kernel<A_MN, B_MN, EPI>;
@@ -438,10 +517,29 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int n
     configured = true;
   }
   const int num_tiles = ((p.M + TILE - 1) / TILE) * ((p.N + TILE - 1) / TILE);
+  const int num_kb = (p.K + BK - 1) / BK;
   const int copy_ctas = p.gather.ctas;  // even: copy CTAs come in clusters of two
-  const int clusters = std::max(1, std::min(num_tiles, (num_sms - copy_ctas) / 2));
+  const int max_clusters = std::max(1, (num_sms - copy_ctas) / 2);
+  int clusters = std::min(num_tiles, max_clusters);
+  int dp_tiles = num_tiles, sk_clusters = 0;
+  if (EPI == kAccumF32 && stream_k_enabled()) {
+    // The last, partial wave of whole tiles would leave clusters idle: spread its k-blocks over
+    // all clusters instead (pieces of at least kMinSkBlocks), when that wave is at most 7/8 full.
+    const int tail = num_tiles % max_clusters;
+    if (tail > 0 && 8 * tail <= 7 * max_clusters) {
+      const long long tail_blocks = static_cast<long long>(tail) * num_kb;
+      const int sk = static_cast<int>(std::min<long long>(max_clusters, tail_blocks / kMinSkBlocks));
+      if (sk > tail) {
+        dp_tiles = num_tiles - tail;
+        sk_clusters = sk;
+        clusters = std::max(std::min(dp_tiles, max_clusters), sk);
+      }
+    }
+  }
   Params q = p;
   q.gemm_clusters = clusters;
+  q.dp_tiles = dp_tiles;
+  q.sk_clusters = sk_clusters;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters + copy_ctas);
   cfg.blockDim = dim3(THREADS);

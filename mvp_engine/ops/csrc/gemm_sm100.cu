@@ -287,7 +287,9 @@ __global__ void __launch_bounds__(Config<BN, BM>::THREADS, 1)
               dst[v] = q;
             }
           } else {
-            for (int j = 0; j < 32 && n + j < p.N; ++j) C[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+#pragma unroll
+            for (int j = 0; j < 32; ++j)  // constant indices keep r[] in registers
+              if (n + j < p.N) C[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
           }
         } else {
           float* C = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + n;
@@ -307,7 +309,9 @@ __global__ void __launch_bounds__(Config<BN, BM>::THREADS, 1)
               dst[v] = q;
             }
           } else {
-            for (int j = 0; j < 32 && n + j < p.N; ++j) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (n + j >= p.N) continue;
               float val = __uint_as_float(r[j]);
               if constexpr (EPI == kAccumF32) val += C[j];
               C[j] = val;

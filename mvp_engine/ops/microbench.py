@@ -60,12 +60,17 @@ def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
         x = torch.randn(M, K, device="cuda").bfloat16()
         w = torch.randn(N, K, device="cuda").bfloat16()
         dy = torch.randn(M, N, device="cuda").bfloat16()
+        acc = torch.zeros(N, K, device="cuda")  # fp32 weight-gradient accumulator (training path)
         flops = 2.0 * M * N * K
         cases = {
             "fwd": (lambda: ops.gemm(x, w), lambda: torch.matmul(x, w.t())),
             "dgrad": (lambda: ops.gemm(dy, w, b_mn=True), lambda: torch.matmul(dy, w)),
             "wgrad": (
                 lambda: ops.gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32),
+                lambda: torch.matmul(dy.t(), x),
+            ),
+            "wgrad_acc": (
+                lambda: ops.gemm(dy, x, a_mn=True, b_mn=True, out=acc, accumulate=True),
                 lambda: torch.matmul(dy.t(), x),
             ),
         }
@@ -88,7 +93,7 @@ def bench_gemm(shapes: dict[str, tuple[int, int, int]], iters: int) -> None:
                 ),
                 flush=True,
             )
-        del x, w, dy
+        del x, w, dy, acc
         torch.cuda.empty_cache()
 
 

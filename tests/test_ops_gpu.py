@@ -66,6 +66,40 @@ def test_gemm_majors(shape, majors):
 
 
 @cuda
+@pytest.mark.parametrize(
+    "shape",
+    [
+        (6144, 4096, 8192),  # QKV weight gradient: 384 tiles, a 14-tile last wave split over k
+        (4096, 4096, 1000),  # 256 tiles, ragged k (16 blocks, the last one partial)
+        (768, 1024, 4096),   # 12 tiles, fewer than the clusters: every tile split
+        (1000, 776, 2048),   # ragged M / N edges in split tiles (scalar reduction path)
+    ],
+)
+def test_gemm_accumulate_split_k_tail(shape):
+    """Weight-gradient GEMM into an fp32 accumulator (dW += dY^T X, both operands MN-major), where the
+    k-blocks of the last, partial wave of tiles are spread over all clusters and added by reductions:
+    two accumulations in a row onto a non-zero buffer must equal the fp32 product twice plus the
+    starting values."""
+    ops = _ops()
+    M, N, K = shape
+    torch.manual_seed(3)
+    dy = torch.randn(K, M, device="cuda").bfloat16()  # [tokens, out features]
+    x = torch.randn(K, N, device="cuda").bfloat16()   # [tokens, in features]
+    ref = dy.float().t() @ x.float()
+    start = torch.randn(M, N, device="cuda")
+    acc = start.clone()
+    ops.gemm(dy, x, a_mn=True, b_mn=True, out=acc, accumulate=True)
+    torch.cuda.synchronize()
+    assert _rel_err(acc - start, ref) < 1e-5, shape
+    ops.gemm(dy, x, a_mn=True, b_mn=True, out=acc, accumulate=True)
+    torch.cuda.synchronize()
+    assert _rel_err(acc - start, 2 * ref) < 1e-5, shape
+    from mvp_engine.ops import _ext
+
+    _ext.check_status()
+
+
+@cuda
 def test_gemm_strided_views():
     ops = _ops()
     torch.manual_seed(1)
