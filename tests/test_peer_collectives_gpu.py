@@ -85,10 +85,19 @@ def test_peer_reduce_scatter_two_gpus():
             assert err < 1e-5 and ssq_rel < 1e-4
 
 
+# Two runs compared after AdamW steps must add the same numbers in the same order: Adam's first update
+# is about lr * sign(g), so a last-bit difference in a near-zero gradient becomes an lr-sized weight
+# difference.  The weight-gradient GEMM's split-k tail adds its pieces in no fixed order, so the strict
+# comparisons run it on whole tiles only (MVP_GEMM_STREAMK=0); one reshard variant keeps it on and is
+# compared with a tolerance that allows for the order.
+_SPLIT_TOL = 5e-3
+
+
 def _fsdp_worker(rank, world, port, comm):
     import os
 
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["MVP_GEMM_STREAMK"] = "0"
     import torch.distributed as dist
 
     from mvp_engine.distributed.init import initialize_process_group
@@ -133,10 +142,11 @@ def test_native_fsdp_peer_reduce_scatter_matches_nccl():
             assert ((x - y).norm() / (y.norm() + 1e-12)).item() < 1e-4
 
 
-def _reshard_worker(rank, world, port, comm, reshard, ckpt, gather="gemm"):
+def _reshard_worker(rank, world, port, comm, reshard, ckpt, gather="gemm", split_k=False):
     import os
 
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["MVP_GEMM_STREAMK"] = "1" if split_k else "0"
     # gemm: every pull rides in copy CTAs of the next GEMM (threshold 0 so the tiny model's GEMMs carry
     # it); kernel: stand-alone pull kernel on the comm stream
     os.environ["MVP_FSDP_GATHER"] = gather
@@ -205,9 +215,11 @@ def test_resharded_weights_peer_pull_matches_resident(ckpt):
     in_gemm = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, "gemm", timeout=300)
     pulled = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, "kernel", timeout=300)
     gathered = spawn_workers(_reshard_worker, 2, "nccl", True, ckpt, timeout=300)
-    for variant in (in_gemm, pulled, gathered):
+    # gathers carried by GEMMs whose weight gradients use the split-k tail (the production setting)
+    in_gemm_split = spawn_workers(_reshard_worker, 2, "fused", True, ckpt, "gemm", True, timeout=300)
+    for variant, tol in ((in_gemm, 1e-4), (pulled, 1e-4), (gathered, 1e-4), (in_gemm_split, _SPLIT_TOL)):
         for (lv, wv), (lr, wr) in zip(variant, resident):
             for (a, ga), (b, gb) in zip(lv, lr):
                 assert abs(a - b) <= 1e-3 * abs(b) and abs(ga - gb) <= 1e-3 * abs(gb), (lv, lr)
             for k, v in wr.items():
-                assert ((wv[k] - v).norm() / (v.norm() + 1e-12)).item() < 1e-4, k
+                assert ((wv[k] - v).norm() / (v.norm() + 1e-12)).item() < tol, k
