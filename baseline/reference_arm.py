@@ -109,6 +109,9 @@ def run(args) -> None:
     import torch
     import torch.distributed as dist
 
+    if not torch.cuda.is_available():
+        _unavailable("no CUDA device: the reference trains with flash_attention_2, which runs on CUDA only")
+        return
     try:
         import flash_attn  # noqa: F401
     except ImportError:

@@ -424,6 +424,10 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
     else:
+        import torch
+
+        if not torch.cuda.is_available():
+            raise SystemExit("bench.py times B200 kernels: no CUDA device is visible")
         run_ours(args)
 
 
