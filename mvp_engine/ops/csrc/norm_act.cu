@@ -309,35 +309,35 @@ __global__ void qk_norm_rope_fwd_kernel(QKRopeArgs a) {
       raw[j] = h0 + j < heads ? *reinterpret_cast<const uint2*>(row + static_cast<int64_t>(h0 + j) * D)
                               : make_uint2(0u, 0u);
 #pragma unroll
-  for (int j = 0; j < kGroup; ++j) {
-    const int hd = h0 + j;
-    if (hd >= heads) break;
-    const bool is_q = hd < a.Hq;
-    float x[4];
-    {
-      const uint2 u = raw[j];
-      const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-      x[0] = p0.x; x[1] = p0.y; x[2] = p1.x; x[3] = p1.y;
+    for (int j = 0; j < kGroup; ++j) {
+      const int hd = h0 + j;
+      if (hd >= heads) break;
+      const bool is_q = hd < a.Hq;
+      float x[4];
+      {
+        const uint2 u = raw[j];
+        const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        x[0] = p0.x; x[1] = p0.y; x[2] = p1.x; x[3] = p1.y;
+      }
+      float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+      ss = warp_sum(ss);
+      const float rstd = rsqrtf(ss / D + a.eps);
+      if (lane == 0) a.rstd[static_cast<int64_t>(t) * heads + hd] = rstd;
+      float y[4], partner[4], o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = bf16r((is_q ? wq[i] : wk[i]) * bf16r(x[i] * rstd));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = lo ? (y[i] * c[i] - partner[i] * sn[i]) : (y[i] * c[i] + partner[i] * sn[i]);
+      __nv_bfloat16* dst = is_q ? a.q_out + (static_cast<int64_t>(t) * a.Hq + hd) * D
+                                : a.k_out + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D;
+      uint2 u;
+      u.x = pack_bf16x2(o[0], o[1]);
+      u.y = pack_bf16x2(o[2], o[3]);
+      *reinterpret_cast<uint2*>(dst + lane * 4) = u;
     }
-    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / D + a.eps);
-    if (lane == 0) a.rstd[static_cast<int64_t>(t) * heads + hd] = rstd;
-    float y[4], partner[4], o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) y[i] = bf16r((is_q ? wq[i] : wk[i]) * bf16r(x[i] * rstd));
-#pragma unroll
-    for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = lo ? (y[i] * c[i] - partner[i] * sn[i]) : (y[i] * c[i] + partner[i] * sn[i]);
-    __nv_bfloat16* dst = is_q ? a.q_out + (static_cast<int64_t>(t) * a.Hq + hd) * D
-                              : a.k_out + (static_cast<int64_t>(t) * a.Hkv + (hd - a.Hq)) * D;
-    uint2 u;
-    u.x = pack_bf16x2(o[0], o[1]);
-    u.y = pack_bf16x2(o[2], o[3]);
-    *reinterpret_cast<uint2*>(dst + lane * 4) = u;
-  }
   }
 }
 
@@ -413,43 +413,43 @@ __global__ void qk_norm_rope_bwd_kernel(QKRopeBwdArgs a) {
         rs[j] = a.rstd[static_cast<int64_t>(t) * heads + hd];
       }
 #pragma unroll
-    for (int j = 0; j < kGroup; ++j) {
-      const int hd = h0 + j;
-      if (hd >= heads) break;
-      const bool is_q = hd < a.Hq;
-      float g[4], x[4];
+      for (int j = 0; j < kGroup; ++j) {
+        const int hd = h0 + j;
+        if (hd >= heads) break;
+        const bool is_q = hd < a.Hq;
+        float g[4], x[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        g[i] = gs[j][i];
-        x[i] = xs[j][i];
+        for (int i = 0; i < 4; ++i) {
+          g[i] = gs[j][i];
+          x[i] = xs[j][i];
+        }
+        float gp[4], dy[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gp[i] = __shfl_xor_sync(0xffffffffu, g[i], 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dy[i] = lo ? (g[i] * c[i] + gp[i] * sn[i]) : (g[i] * c[i] - gp[i] * sn[i]);
+        const float rstd = rs[j];
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dot += dy[i] * (is_q ? wq[i] : wk[i]) * x[i] * rstd;
+        dot = warp_sum(dot) / D;
+        float dx[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dx[i] = rstd * ((is_q ? wq[i] : wk[i]) * dy[i] - x[i] * rstd * dot);
+          const float xh = bf16r(x[i] * rstd);
+          if (is_q) accq[i] += dy[i] * xh;
+          else acck[i] += dy[i] * xh;
+        }
+        __nv_bfloat16* dst = a.dqkv + static_cast<int64_t>(t) * a.ld_dqkv + static_cast<int64_t>(hd) * D + lane * 4;
+        if (a.route.dst[0] != nullptr)  // Ulysses: back to the token's rank, global head columns
+          dst = reinterpret_cast<__nv_bfloat16*>(a.route.dst[owner]) + static_cast<int64_t>(lrow) * a.route.ld +
+                (is_q ? a.route.col0 + hd * D : a.route.col0_k + (hd - a.Hq) * D) + lane * 4;
+        uint2 u;
+        u.x = pack_bf16x2(dx[0], dx[1]);
+        u.y = pack_bf16x2(dx[2], dx[3]);
+        *reinterpret_cast<uint2*>(dst) = u;
       }
-      float gp[4], dy[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) gp[i] = __shfl_xor_sync(0xffffffffu, g[i], 16);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) dy[i] = lo ? (g[i] * c[i] + gp[i] * sn[i]) : (g[i] * c[i] - gp[i] * sn[i]);
-      const float rstd = rs[j];
-      float dot = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) dot += dy[i] * (is_q ? wq[i] : wk[i]) * x[i] * rstd;
-      dot = warp_sum(dot) / D;
-      float dx[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        dx[i] = rstd * ((is_q ? wq[i] : wk[i]) * dy[i] - x[i] * rstd * dot);
-        const float xh = bf16r(x[i] * rstd);
-        if (is_q) accq[i] += dy[i] * xh;
-        else acck[i] += dy[i] * xh;
-      }
-      __nv_bfloat16* dst = a.dqkv + static_cast<int64_t>(t) * a.ld_dqkv + static_cast<int64_t>(hd) * D + lane * 4;
-      if (a.route.dst[0] != nullptr)  // Ulysses: back to the token's rank, global head columns
-        dst = reinterpret_cast<__nv_bfloat16*>(a.route.dst[owner]) + static_cast<int64_t>(lrow) * a.route.ld +
-              (is_q ? a.route.col0 + hd * D : a.route.col0_k + (hd - a.Hq) * D) + lane * 4;
-      uint2 u;
-      u.x = pack_bf16x2(dx[0], dx[1]);
-      u.y = pack_bf16x2(dx[2], dx[3]);
-      *reinterpret_cast<uint2*>(dst) = u;
-    }
     }
   }
 #pragma unroll
