@@ -80,4 +80,13 @@ def init_logger(backends: List, interval: int = 20, accumulation_size: Optional[
     return logger
 
 
-__all__ = ["Logger", "LogLevel", "logger", "init_logger", "get_logger", "simple_info", "parse_log_level"]
+def __getattr__(name: str):
+    # the backend base class for custom backends, imported on first use (the backends import this module)
+    if name == "Backend":
+        from .backend.backend import Backend
+
+        return Backend
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
+
+__all__ = ["Backend", "Logger", "LogLevel", "logger", "init_logger", "get_logger", "simple_info", "parse_log_level"]
