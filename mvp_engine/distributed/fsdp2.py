@@ -46,6 +46,9 @@ def _class_hook(model: nn.Module, name: str) -> Optional[Callable[[nn.Module], N
 
 
 def parallelize_model_with_fsdp2(model: nn.Module, backend_kwargs: Optional[dict] = None) -> nn.Module:
+    from ..patches import apply_all_patches
+
+    apply_all_patches()  # recomputed FSDP2 modules must cast their inputs (whatever the entry point)
     kw = dict(backend_kwargs or {})
     targets = set(getattr(model, "_no_split_modules", []) or []) | set(kw.pop("target_classes", []) or [])
     hp_classes = set(kw.pop("high_precision_modules", []) or [])

@@ -4,7 +4,7 @@
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Literal, Optional, Union
+from typing import Dict, List, Literal, Optional, TypedDict, Union
 
 import torch
 import torch.distributed as dist
@@ -81,12 +81,20 @@ class Metric:
         return total
 
 
+class MetricEntry(TypedDict):
+    """One named metric of a :class:`MetricAggregator`: its buffer, emission interval and update count."""
+
+    metric: Metric
+    interval: int
+    update_count: int
+
+
 class MetricAggregator:
     """Named metrics with an emission interval: a metric is reported every ``interval`` updates."""
 
     def __init__(self, dist_group: Optional[dist.ProcessGroup] = None, default_interval: int = 20,
                  default_accumulation_size: int = 20) -> None:
-        self._metrics: Dict[str, dict] = {}
+        self._metrics: Dict[str, MetricEntry] = {}
         self._group = dist_group
         self._interval = int(default_interval)
         self._acc = int(default_accumulation_size)
@@ -95,13 +103,13 @@ class MetricAggregator:
             distributed: Optional[bool] = None, support_nan: bool = True) -> None:
         if name in self._metrics:
             return
-        self._metrics[name] = {
-            "metric": Metric(accumulation_size or self._acc,
-                             bool(distributed) if distributed is not None else self._group is not None,
-                             support_nan, self._group),
-            "interval": int(interval or self._interval),
-            "count": 0,
-        }
+        self._metrics[name] = MetricEntry(
+            metric=Metric(accumulation_size or self._acc,
+                          bool(distributed) if distributed is not None else self._group is not None,
+                          support_nan, self._group),
+            interval=int(interval or self._interval),
+            update_count=0,
+        )
 
     def __contains__(self, name: str) -> bool:
         return name in self._metrics
@@ -112,7 +120,7 @@ class MetricAggregator:
                 self.add(name)
             entry = self._metrics[name]
             entry["metric"].update(value)
-            entry["count"] += 1
+            entry["update_count"] += 1
 
     def collect(self, metric_names: Optional[List[str]] = None,
                 accumulate: Literal["mean", "sum"] = "mean") -> Dict[str, Union[float, str]]:
@@ -125,7 +133,7 @@ class MetricAggregator:
         out: Dict[str, Union[float, str]] = {}
         for name in names:
             entry = self._metrics.get(name)
-            if entry is None or entry["count"] % entry["interval"] != 0:
+            if entry is None or entry["update_count"] % entry["interval"] != 0:
                 continue
             m = entry["metric"]
             out[name] = m.mean() if accumulate == "mean" else m.sum()
