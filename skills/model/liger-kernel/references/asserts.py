@@ -18,11 +18,15 @@ def test_engine_structure(engine_class):
     apply = src.find(".apply(")
     assert apply >= 0, "LigerKernelKit.apply must be called"
     assert build < 0 or apply < build, "swap kernels before the model is built"
-    assert "cross_entropy" not in src.split(".apply(", 1)[1].split(")", 1)[0] or "exclude" in src, (
-        "do not swap the cross-entropy: the token-normalised loss needs per-token losses")
+    call = src.split(".apply(", 1)[1].split(")", 1)[0]
+    assert "excluded_modules=()" not in call.replace(" ", ""), (
+        "keep the loss kernels excluded: the token-normalised loss needs per-token losses")
 
 
-def check_report(report):
-    """``LigerKernelKit.apply(...)`` result: nothing excluded was applied."""
-    applied = {name.rsplit(".", 1)[-1] for name in report.applied}
-    assert not applied & set(report.excluded), f"excluded kernels were applied: {applied & set(report.excluded)}"
+def check_report(report, excluded=("cross_entropy", "fused_linear_cross_entropy")):
+    """``LigerKernelKit.apply(...)`` result: no excluded kernel was switched on, and on the custom route
+    every enabled kernel rebound exactly one symbol."""
+    enabled = {name for name, on in (report.applied or {}).items() if on}
+    assert not enabled & set(excluded), f"excluded kernels were applied: {sorted(enabled & set(excluded))}"
+    if report.route == "custom":
+        assert len(report.patched) == len(enabled), (report.patched, enabled)

@@ -151,8 +151,14 @@ def test_liger_report_check():
     from mvp_engine.kit.model.liger import LigerKernelKit, LigerPatch
 
     mod = _template("model/liger-kernel")
-    report = LigerKernelKit().apply(custom_patches=[LigerPatch("json", "dumps", json.dumps)])
+    patches = {"rms_norm": LigerPatch("json", "dumps", json.dumps),  # rebinding to itself: harmless
+               "cross_entropy": LigerPatch("json", "loads", None)}      # excluded by default: not applied
+    report = LigerKernelKit().apply(model_family="custom", custom_patches=patches)
+    assert report.route == "custom" and report.patched == ("json.dumps",) and json.loads("1") == 1
     mod.check_report(report)
+    assert LigerKernelKit().apply(model_family="qwen3").route == "official"
+    with pytest.raises(ValueError, match="custom_patches"):
+        LigerKernelKit().apply(model_family="llama")
 
 
 # ------------------------------------------------------------------ runtime hooks on real CPU runs
