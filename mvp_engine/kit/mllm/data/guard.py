@@ -38,7 +38,7 @@ class MLLMRawRowGuard(MLLMGuard):
 
 
 def _mllm_unsupervised(sample: MLLMSample) -> bool:
-    ignore = sample.spec.tokenization_handler.ignore_index
+    ignore = sample.tokenization_handler.ignore_index
     return all(lab == ignore for lab in sample.labels)
 
 

@@ -14,7 +14,7 @@ from typing import Any, Sequence
 
 import torch
 
-from .types import MLLMMediaSlot
+from .types import MLLMMediaSlot, MLLMSegment
 
 
 def empty_model_sample() -> dict[str, Any]:
@@ -75,13 +75,28 @@ class MLLMMediaHandler:
     def tokenizer(self) -> Any:
         return getattr(self.processor, "tokenizer", self.processor)
 
-    def render(self, slots: Sequence[MLLMMediaSlot]) -> dict[str, RenderedMedia]:
+    def render_slots(self, slots: Sequence[MLLMMediaSlot]) -> dict[str, RenderedMedia]:
+        """Placeholder text of every media slot, by media id."""
         out = {}
         for s in slots:
             h = self.handlers.get(s.media_type)
             if h is None:
                 raise ValueError(f"No media handler for type {s.media_type!r}")
             out[s.media_id] = h.render(s, processor=self.processor, tokenizer=self.tokenizer)
+        return out
+
+    def render(self, segments: Sequence[MLLMSegment], media_slots: Sequence[MLLMMediaSlot]) -> list[MLLMSegment]:
+        """The segments with every media segment's value (a media id) replaced by its placeholder text;
+        media segments keep their media type (the tokenizer never supervises them)."""
+        text = self.render_slots(media_slots)
+        out = []
+        for seg in segments:
+            if seg.type in ("text", "tokens"):
+                out.append(seg)
+            elif seg.value in text:
+                out.append(MLLMSegment(seg.type, False, text[seg.value].text))
+            else:
+                raise ValueError(f"media segment {seg.value!r} has no slot")
         return out
 
     def load(self, sample: Any, media_slots: Sequence[MLLMMediaSlot]) -> dict[str, Any]:

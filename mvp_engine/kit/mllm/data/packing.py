@@ -93,8 +93,8 @@ class MLLMPackingAssembler(Assembler):
     def load_state_dict(self, state: dict[str, object], sample_spec=None) -> None:
         if sample_spec is None:
             raise ValueError("MLLMPackingAssembler.load_state_dict needs the sample spec to rebuild samples")
-        self.open = [[MLLMSample(r, sample_spec) for r in p] for p in state.get("open", [])]
-        self.pending = [MLLMSample(r, sample_spec) for r in state.get("pending", [])]
+        self.open = [[MLLMSample.from_row(r, sample_spec=sample_spec) for r in p] for p in state.get("open", [])]
+        self.pending = [MLLMSample.from_row(r, sample_spec=sample_spec) for r in state.get("pending", [])]
         if "rng" in state:
             self.rng.setstate(state["rng"])
 

@@ -24,10 +24,16 @@ _MEDIA_MARK = "\x00MEDIA{}\x00"
 
 class QwenVLChatSchemaHandler(MLLMSchemaHandler):
     def __init__(self, processor: Any, *, thinking_mode: bool | None | Literal["non-empty"] = True,
-                 image_field: str = "images") -> None:
+                 image_placeholders: tuple[str, ...] | None = None, image_field: str = "images") -> None:
+        """``image_placeholders``: extra strings in message text that stand for the next image (besides
+        ``<image>``, the processor's image token and that token wrapped in the vision start / end tokens)."""
         self.processor = processor
         self.image_field = image_field
         self._text = QwenChatSchemaHandler(getattr(processor, "tokenizer", processor), thinking_mode=thinking_mode)
+        token = getattr(processor, "image_token", "<|image_pad|>")
+        marks = (*(image_placeholders or ()), f"<|vision_start|>{token}<|vision_end|>", IMAGE_PLACEHOLDER, token)
+        # longest first, so a wrapped token is taken whole before its inner token could match
+        self._placeholder_re = re.compile("|".join(re.escape(m) for m in sorted(set(marks), key=len, reverse=True)))
 
     def check_row(self, row: Mapping[str, Any]) -> str | None:
         reason = self._text.check_row(row)
@@ -67,7 +73,7 @@ class QwenVLChatSchemaHandler(MLLMSchemaHandler):
                     else:
                         parts.append(str(item))
                 content = "".join(parts)
-            content = re.sub(re.escape(IMAGE_PLACEHOLDER), lambda _: _MEDIA_MARK.format(next(counter)), content)
+            content = self._placeholder_re.sub(lambda _: _MEDIA_MARK.format(next(counter)), content)
             msgs.append({**m, "content": content})
         text_segs, meta = self._text.normalize({"messages": msgs})
         segs: list[MLLMSegment] = []

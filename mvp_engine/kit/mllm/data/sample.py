@@ -15,12 +15,22 @@ from .spec import MLLMSampleSpec
 class MLLMSample:
     """One row: lazily normalised -> rendered -> tokenised; media loaded on demand."""
 
-    __slots__ = ("_raw", "spec", "segments", "media_slots", "metadata", "_input_ids", "_labels", "_attention_mask",
-                 "media")
+    __slots__ = ("_raw", "schema_handler", "media_handler", "tokenization_handler", "segments", "media_slots",
+                 "metadata", "_input_ids", "_labels", "_attention_mask", "media")
 
-    def __init__(self, raw: Mapping[str, Any], spec: MLLMSampleSpec) -> None:
+    def __init__(self, raw: Mapping[str, Any], spec: Optional[MLLMSampleSpec] = None, *, schema_handler: Any = None,
+                 media_handler: Any = None, tokenization_handler: Any = None) -> None:
+        """The three handlers, given directly (the reference's form) or through an ``MLLMSampleSpec``."""
+        if spec is not None:
+            schema_handler = schema_handler or spec.schema_handler
+            media_handler = media_handler or spec.media_handler
+            tokenization_handler = tokenization_handler or spec.tokenization_handler
+        if schema_handler is None or media_handler is None or tokenization_handler is None:
+            raise ValueError("MLLMSample needs schema_handler, media_handler and tokenization_handler")
         object.__setattr__(self, "_raw", dict(raw))
-        object.__setattr__(self, "spec", spec)
+        object.__setattr__(self, "schema_handler", schema_handler)
+        object.__setattr__(self, "media_handler", media_handler)
+        object.__setattr__(self, "tokenization_handler", tokenization_handler)
         for k in ("segments", "media_slots", "_input_ids", "_labels", "_attention_mask", "media"):
             object.__setattr__(self, k, None)
         object.__setattr__(self, "metadata", {})
@@ -45,9 +55,8 @@ class MLLMSample:
         if self._input_ids is not None:
             return self
         try:
-            segs, slots, meta = self.spec.schema_handler.normalize(self._raw)
-            rendered = self.spec.media_handler.render(slots)
-            ids, labels, am = self.spec.tokenization_handler.tokenize(segs, rendered)
+            segs, slots, meta = self.schema_handler.normalize(self._raw)
+            ids, labels, am = self.tokenization_handler.tokenize(self.media_handler.render(segs, slots))
             self.segments, self.media_slots, self.metadata = segs, slots, meta
             self._input_ids, self._labels, self._attention_mask = ids, labels, am
         except Exception as exc:
@@ -74,7 +83,7 @@ class MLLMSample:
     def load_media(self) -> "MLLMSample":
         if self.media is None:
             self.tokenize()
-            self.media = self.spec.media_handler.load(self, self.media_slots or []) if self.media_slots else {}
+            self.media = self.media_handler.load(self, self.media_slots or []) if self.media_slots else {}
         return self
 
     def to_model_inputs(self) -> dict[str, Any]:
@@ -116,5 +125,5 @@ class MLLMPack(list):
                "labels": torch.cat([p["labels"] for p in parts]), "pack_segment_ids": seg,
                "source_sample_num": len(parts)}
         if load_media and self:
-            out.update(self[0].spec.media_handler.merge_pack(parts))
+            out.update(self[0].media_handler.merge_pack(parts))
         return out

@@ -30,20 +30,19 @@ class MLLMTokenizationHandler:
         enc = self.tokenizer(text, add_special_tokens=False)
         return list(enc["input_ids"])
 
-    def tokenize(self, segments: Sequence[MLLMSegment], rendered: dict[str, Any]) -> tuple[list[int], list[int], list[int]]:
+    def tokenize(self, rendered_segments: Sequence[MLLMSegment]) -> tuple[list[int], list[int], list[int]]:
+        """``(input_ids, labels, attention_mask)`` of segments whose media values are already rendered to
+        placeholder text (``MLLMMediaHandler.render``)."""
         ids: list[int] = []
         labels: list[int] = []
         media_end = 0
-        for seg in segments:
-            if seg.type == "text":
-                part = self._encode(seg.value)
-                sup = seg.loss
-            elif seg.type == "tokens":
+        for seg in rendered_segments:
+            if seg.type == "tokens":
                 part = [int(t) for t in seg.value]
                 sup = seg.loss
-            else:
-                part = self._encode(rendered[seg.value].text)
-                sup = False
+            else:  # text, or a media segment's placeholder text (never supervised)
+                part = self._encode(seg.value)
+                sup = seg.loss and seg.type == "text"
             ids += part
             labels += part if sup else [self.ignore_index] * len(part)
             if seg.type not in ("text", "tokens"):

@@ -18,7 +18,8 @@ import importlib
 import subprocess
 import sys
 from pathlib import Path
-from typing import Optional, Sequence
+from collections.abc import Mapping
+from typing import Optional, Sequence, Union
 
 PROJECT_ROOT = Path(__file__).resolve().parent.parent
 RECIPES_ROOT = PROJECT_ROOT / "recipes"
@@ -74,6 +75,16 @@ def import_recipe_modules(recipe_dir: Path) -> None:
         importlib.import_module(".".join(f.relative_to(root).with_suffix("").parts))
 
 
+def _plain_dict(config) -> dict:
+    """An OmegaConf / mapping-like config as nested plain dicts."""
+    try:
+        from omegaconf import OmegaConf
+
+        return OmegaConf.to_container(config, resolve=True)
+    except ImportError:
+        return {k: _plain_dict(v) if hasattr(v, "keys") else v for k, v in config.items()}
+
+
 def run(config: dict) -> object:
     """Build the configured engine and dispatch its workflow; returns the engine."""
     from .engine import ENGINE_REGISTRY
@@ -92,9 +103,17 @@ def run(config: dict) -> object:
     return engine
 
 
-def main(argv: Optional[Sequence[str]] = None) -> None:
-    from .config.loader import compose_config
+def main(config: Optional[Union[Mapping, Sequence[str]]] = None) -> None:
+    """Launcher entry.  ``config`` is either an already composed config (a mapping, as the reference's
+    Hydra-decorated ``main(config)`` receives it; it is merged over ``config/default.yaml``) or the
+    command-line arguments (``--config <yaml>`` plus dotlist overrides; ``None`` = ``sys.argv``)."""
+    from .config.loader import compose_config, deep_merge, load_yaml
 
+    if isinstance(config, Mapping) or hasattr(config, "keys"):
+        composed = config if isinstance(config, dict) else _plain_dict(config)
+        run(deep_merge(load_yaml(Path(__file__).parent / "config" / "default.yaml"), composed))
+        return
+    argv = config
     parser = argparse.ArgumentParser(description="mvp_engine launcher")
     parser.add_argument("--config", required=True, help="Path to YAML config file")
     args, overrides = parser.parse_known_args(argv)

@@ -12,7 +12,11 @@ from .backend import Backend
 
 
 class WandbBackend(Backend):
-    def __init__(self, id: str, project: str, path: Union[str, Path], main_process_only: bool = True) -> None:
+    def __init__(self, id: str, project: str, entity: Optional[str] = None, config: Optional[Mapping] = None,
+                 path: Optional[Union[str, Path]] = None, main_process_only: bool = True) -> None:
+        """``entity`` / ``config`` go to ``wandb.init`` (an OmegaConf config is converted to plain dicts).
+        Nothing is started on non-main ranks, without ``wandb``, or without credentials / a ``WANDB_MODE``
+        (no interactive login)."""
         self.run = None
         if main_process_only and not is_main_process():
             return
@@ -22,8 +26,17 @@ class WandbBackend(Backend):
             import wandb  # type: ignore
         except Exception:
             return
-        Path(path).mkdir(parents=True, exist_ok=True)
-        self.run = wandb.init(project=project, name=id, id=id, dir=str(path), resume="allow")
+        if config is not None and not isinstance(config, dict):
+            try:
+                from omegaconf import OmegaConf
+
+                config = OmegaConf.to_container(config, resolve=True)
+            except ImportError:
+                config = dict(config)
+        if path is not None:
+            Path(path).mkdir(parents=True, exist_ok=True)
+        self.run = wandb.init(project=project, entity=entity, name=id, id=id, config=config,
+                              dir=str(path) if path is not None else None, resume="allow")
 
     def log_config(self, config: dict) -> None:
         if self.run is not None:

@@ -52,3 +52,31 @@ def test_collate_and_text_only_guard():
     out = guard(text_only)
     assert out["pixel_values"].shape[0] == 4 and out["input_ids"].shape[1] >= b["input_ids"].shape[1]
     assert int(out["pack_segment_ids"].max()) == int(b["pack_segment_ids"].max()) + 1
+
+
+def test_chat_row_through_the_handler_interfaces():
+    """The handler contract step by step (schema -> media render -> tokenise, as the reference defines
+    it): every image placeholder form in message text takes the next image slot, media segments render to
+    unsupervised placeholder tokens, and MLLMSample accepts the handlers directly."""
+    from mvp_engine.kit.mllm import MLLMSample, QwenVLChatSchemaHandler
+    from mvp_engine.kit.mllm.data.types import MLLMSegment
+
+    proc = MLLMDataKit().build_processor("synthetic", image_max_pixels=256 * 256)
+    schema = QwenVLChatSchemaHandler(proc, thinking_mode=None, image_placeholders=("[IMG]",))
+    media = QwenVLMediaHandler(proc)
+    tok = QwenVLTokenizationHandler(proc.tokenizer, max_seq_len=4096)
+    row = {"messages": [{"role": "user", "content": "<image> and [IMG]: compare"},
+                        {"role": "assistant", "content": "the first is larger"}],
+           "images": [{"height": 64, "width": 64}, {"height": 128, "width": 96}]}
+    segs, slots, _ = schema.normalize(row)
+    assert [s.value for s in segs if s.type == "image"] == ["image_0", "image_1"] and len(slots) == 2
+    rendered = media.render(segs, slots)
+    assert all(isinstance(s, MLLMSegment) for s in rendered)
+    assert all(s.type == "image" and not s.loss and "<|image_pad|>" in s.value for s in rendered if s.type == "image")
+    ids, labels, mask = tok.tokenize(rendered)
+    image_id = proc.tokenizer.convert_tokens_to_ids("<|image_pad|>")
+    pad_positions = [i for i, t in enumerate(ids) if t == image_id]
+    assert pad_positions and all(labels[i] == -100 for i in pad_positions) and len(mask) == len(ids)
+    assert any(lab != -100 for lab in labels)  # the assistant reply is supervised
+    sample = MLLMSample(row, schema_handler=schema, media_handler=media, tokenization_handler=tok)
+    assert sample.input_ids == ids and sample.labels == labels
