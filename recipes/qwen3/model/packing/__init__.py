@@ -1,3 +1,3 @@
-from .prepare import prepare_packed_model_inputs
+from .prepare import build_packed_fa2_varlen_kwargs, build_packed_text_position_ids, prepare_packed_model_inputs
 
-__all__ = ["prepare_packed_model_inputs"]
+__all__ = ["build_packed_fa2_varlen_kwargs", "build_packed_text_position_ids", "prepare_packed_model_inputs"]

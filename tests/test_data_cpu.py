@@ -104,3 +104,23 @@ def test_dataloader_position_resumes_the_stream():
     got = next(iter(again))
     assert torch.equal(got["input_ids"], expected["input_ids"])
     assert not torch.equal(got["input_ids"], seen[-1]["input_ids"])
+
+
+def test_qwen3_recipe_packing_helpers_match_a_direct_construction():
+    """Positions restart per document (0 on padding); cu_seqlens list every document of every row, the
+    padding suffix being one more; malformed padding is rejected."""
+    import pytest
+    import torch
+
+    from recipes.qwen3.model.packing import build_packed_fa2_varlen_kwargs, build_packed_text_position_ids
+
+    seg = torch.tensor([[1, 1, 1, 2, 2, 0, 0], [1, 2, 2, 2, 3, 3, 3]])
+    pos = build_packed_text_position_ids(torch.zeros_like(seg), seg)
+    assert pos.tolist() == [[0, 1, 2, 0, 1, 0, 0], [0, 0, 1, 2, 0, 1, 2]]
+    kw = build_packed_fa2_varlen_kwargs(seg)
+    assert kw["cu_seq_lens_q"].tolist() == [0, 3, 5, 7, 8, 11, 14] and kw["cu_seq_lens_q"].dtype == torch.int32
+    assert kw["max_length_q"] == kw["max_length_k"] == 3 and kw["cu_seq_lens_k"] is kw["cu_seq_lens_q"]
+    with pytest.raises(ValueError):
+        build_packed_fa2_varlen_kwargs(torch.tensor([[1, 0, 1]]))
+    with pytest.raises(ValueError):
+        build_packed_fa2_varlen_kwargs(torch.tensor([1, 1]))

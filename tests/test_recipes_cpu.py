@@ -189,3 +189,40 @@ def test_magic_transformer_trains_and_generates():
                       timeout=600)[0]
     assert 5.0 < r["logs"]["train/loss"] < 8.0
     assert "embed.weight" in r["changed"] and tuple(r["generated"]) == (1, 7)
+
+
+def test_minimal_vlm_preprocessing_entry_points(tmp_path):
+    """The recipe's row preprocessing with the reference's arguments: image decoding from bytes / path /
+    record, pixel conversion, and a chat row with an ``<image>`` placeholder -> supervised-reply tokens
+    plus as many image tokens as merged patches."""
+    import io
+
+    from PIL import Image
+
+    from mvp_engine.kit.mllm import MLLMDataKit
+    from recipes.minimal_vlm.dataset.preprocess import (convert_images_to_pixel_values, process_image,
+                                                        process_sample)
+
+    img = Image.new("RGB", (40, 30), (200, 10, 10))
+    buf = io.BytesIO()
+    img.save(buf, format="PNG")
+    png = buf.getvalue()
+    (tmp_path / "a.png").write_bytes(png)
+    for src in (png, {"bytes": png}, {"path": "a.png"}, img):
+        out = process_image(src, image_root=tmp_path)
+        assert out.size == (40, 30) and out.mode == "RGB"
+    with pytest.raises(FileNotFoundError):
+        process_image("missing.png", image_root=tmp_path)
+
+    proc = MLLMDataKit().build_processor("synthetic", image_max_pixels=256 * 256)
+    conv = convert_images_to_pixel_values({"images": [png], "adjusted_image_size": [[64, 64]]}, processor=proc)
+    assert conv["image_grid_thw"].tolist() == [[1, 4, 4]] and conv["pixel_values"].shape[0] == 16
+
+    row = {"messages": [{"role": "user", "content": "<image> what colour?"},
+                        {"role": "assistant", "content": "red"}],
+           "images": [{"bytes": png}], "image_sizes": [[64, 64]]}
+    s = process_sample(row, processor=proc, max_length=512)
+    image_id = proc.tokenizer.convert_tokens_to_ids("<|image_pad|>")
+    n_img = int((s["input_ids"] == image_id).sum())
+    assert n_img == int(s["image_grid_thw"].prod(-1).sum()) // 4 > 0  # smart-resized within the pixel bounds
+    assert int((s["labels"] != -100).sum()) > 0 and bool((s["labels"][s["input_ids"] == image_id] == -100).all())
