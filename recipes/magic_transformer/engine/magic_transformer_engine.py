@@ -9,6 +9,8 @@ mean next-token cross-entropy; logs loss and token accuracy.  The shared plumbin
 
 from __future__ import annotations
 
+from typing import TypedDict
+
 import torch
 import torch.nn.functional as F
 
@@ -18,6 +20,13 @@ from mvp_engine.engine.map_style import MapStyleEngine
 from ..configs.schema import MagicTransformerConfig
 from ..dataset import InfiniteDistributedSampler, build_dataset
 from ..model import build_magic_transformer_model
+
+
+class TrainBatch(TypedDict):
+    """A training batch on the device: token ids and next-token labels, both ``[B, T]``."""
+
+    input_ids: torch.Tensor
+    labels: torch.Tensor
 
 
 @ENGINE_REGISTRY.register()

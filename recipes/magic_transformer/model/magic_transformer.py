@@ -97,8 +97,9 @@ class GQAttention(nn.Module):
         self.out_proj = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.d_model, bias=False)
         self.drop = nn.Dropout(cfg.dropout)
 
-    def forward(self, x, cos, sin, ext_kv=None):
-        """Causal GQA; returns ``(out, (k_unrotated, v))`` for reuse by the next layer."""
+    def forward(self, x, cos, sin, mask=None, ext_kv=None):
+        """GQA, causal unless ``mask`` (boolean keep-mask or additive float mask, broadcastable to
+        ``[B, H, T, T]``) is given; returns ``(out, (k_unrotated, v))`` for reuse by the next layer."""
         B, T, _ = x.shape
         q = self.q_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
         if ext_kv is None:
@@ -109,7 +110,7 @@ class GQAttention(nn.Module):
         rep = self.n_heads // self.n_kv_heads
         kr = rotate(k, cos, sin).repeat_interleave(rep, dim=1)
         vr = v.repeat_interleave(rep, dim=1)
-        o = F.scaled_dot_product_attention(rotate(q, cos, sin), kr, vr, is_causal=True,
+        o = F.scaled_dot_product_attention(rotate(q, cos, sin), kr, vr, attn_mask=mask, is_causal=mask is None,
                                            dropout_p=self.drop.p if self.training else 0.0)
         return self.out_proj(o.transpose(1, 2).reshape(B, T, -1)), (k, v)
 
@@ -180,7 +181,7 @@ class TransformerBlock(nn.Module):
             cos, sin = rope_tables(top, self.cfg.head_dim, self.cfg.rope_base)
         else:
             cos, sin = rope[0][:k], rope[1][:k]
-        out, kv = self.attn(sel, cos, sin, ext_kv)
+        out, kv = self.attn(sel, cos, sin, ext_kv=ext_kv)
         if self.training:
             with torch.no_grad():
                 d = self.cfg.router_ema_decay

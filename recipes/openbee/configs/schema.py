@@ -5,7 +5,17 @@ from __future__ import annotations
 
 from pydantic import Field
 
-from recipes.qwen3_vl.configs.schema import Qwen3VLConfig, Qwen3VLDataConfig
+from recipes.qwen3_vl.configs.schema import (Qwen3VLCompileConfig, Qwen3VLConfig, Qwen3VLDataConfig,
+                                             Qwen3VLGradientCheckpointingConfig, Qwen3VLLoopConfig,
+                                             Qwen3VLModelConfig, Qwen3VLOptimConfig)
+
+# The reference spells out every section for OpenBee; here the sections are the Qwen3-VL ones under the
+# reference's class names, so code that imports them by name keeps working.
+OpenBeeGradientCheckpointingConfig = Qwen3VLGradientCheckpointingConfig
+OpenBeeCompileConfig = Qwen3VLCompileConfig
+OpenBeeModelConfig = Qwen3VLModelConfig
+OpenBeeOptimConfig = Qwen3VLOptimConfig
+OpenBeeLoopConfig = Qwen3VLLoopConfig
 
 
 class OpenBeeDataConfig(Qwen3VLDataConfig):

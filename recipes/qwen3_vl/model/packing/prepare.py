@@ -43,4 +43,12 @@ def prepare_packed_model_inputs(batch: dict[str, Any], *, model_config: Any, vis
     return out
 
 
-__all__ = ["build_packed_varlen_kwargs", "prepare_packed_model_inputs"]
+def build_packed_fa2_varlen_kwargs(pack_segment_ids: torch.Tensor) -> dict[str, Any]:
+    """The reference's name for the varlen arguments of ``[B, T]`` segment ids (validated; see the Qwen3
+    recipe's helper of the same name)."""
+    from recipes.qwen3.model.packing.prepare import build_packed_fa2_varlen_kwargs as build
+
+    return build(pack_segment_ids)
+
+
+__all__ = ["build_packed_fa2_varlen_kwargs", "build_packed_varlen_kwargs", "prepare_packed_model_inputs"]

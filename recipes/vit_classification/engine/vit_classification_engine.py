@@ -10,6 +10,8 @@ compute weights stay fp32.  The shared plumbing is :class:`~mvp_engine.engine.ma
 
 from __future__ import annotations
 
+from typing import TypedDict
+
 import torch
 
 from mvp_engine.distributed.utils import is_main_process
@@ -23,6 +25,13 @@ from ..dataset import InfiniteDistributedSampler, build_dataset
 from ..model import build_vit_model
 
 _FP32_POLICY = {"param_dtype": "float32", "reduce_dtype": "float32", "output_dtype": "float32"}
+
+
+class TrainBatch(TypedDict):
+    """A training batch on the device: images ``[B, 3, H, W]`` and class labels ``[B]``."""
+
+    pixel_values: torch.Tensor
+    labels: torch.Tensor
 
 
 @ENGINE_REGISTRY.register()
