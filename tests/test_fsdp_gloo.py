@@ -98,10 +98,12 @@ def test_resharded_weights_match_resident_weights():
             for a, b in zip(resident[r][0], resharded[r][0]):
                 assert abs(a - b) <= 1e-5 * abs(a), (ckpt, resident[r][0], resharded[r][0])
             for k, v in resident[r][1].items():
-                # CPU float sums are not bitwise reproducible across runs; Adam's m / sqrt(v) magnifies the
-                # last-bit differences of near-zero gradients, so compare the whole tensor
+                # CPU float sums are not bitwise reproducible across runs, and Adam's first updates are about
+                # lr * sign(g): a last-bit difference in a near-zero gradient moves that weight by up to 2 lr.
+                # So the whole tensor is compared, with a bound (2e-3) far below what one stale or wrong
+                # gather would cause (one step's update is a few percent of these weights' norm)
                 rel = ((v - resharded[r][1][k]).norm() / v.norm()).item()
-                assert rel < 1e-4, (ckpt, k, rel)
+                assert rel < 2e-3, (ckpt, k, rel)
 
 
 def _train_hsdp(rank, world, port, hsdp):
@@ -147,5 +149,6 @@ def test_hsdp_matches_flat_sharding():
         for a, b in zip(lf, lh):
             assert abs(a - b) <= 1e-5 * abs(a), (lf, lh)
         for k, v in wf.items():
-            # fp32 sums in another order: Adam's m / sqrt(v) magnifies differences of near-zero gradients
-            assert ((v - wh[k]).norm() / v.norm()).item() < 1e-4, (k, ((v - wh[k]).norm() / v.norm()).item())
+            # fp32 sums in another order; Adam turns last-bit differences of near-zero gradients into
+            # lr-sized weight differences (see the resharding test for the bound)
+            assert ((v - wh[k]).norm() / v.norm()).item() < 2e-3, (k, ((v - wh[k]).norm() / v.norm()).item())
