@@ -20,6 +20,11 @@
 //               arrive, releasing ring slots and publishing accumulators in both.
 //   warps 2..5  epilogue of this CTA's 128 rows; releases the accumulator by
 //               arriving on the leader's barrier.
+// Work: whole 256 x 256 tiles, tile t on cluster t % clusters.  For the fp32
+// accumulate epilogue (weight gradients) a last, partial wave of tiles is instead
+// cut along k and its k-blocks spread evenly over all clusters (WorkList); the
+// pieces of a cut tile are added with vector reductions, whole tiles with a
+// read-add-write.
 // Every wait is bounded; every thread of both CTAs reaches the final cluster
 // barrier, after which both MMA warps free the tensor memory.
 #include <cuda.h>
