@@ -44,3 +44,36 @@ def test_file_backend_lines_and_windows(tmp_path):
     summary = mod.summarize(tmp_path, window=1)
     assert summary["metrics"]["train/loss"]["count"] == 2 and summary["health"]["finished"]
     assert summary["health"]["messages"] == {"WARN": 1} and summary["run"]["engine"] == "Qwen3Engine"
+
+
+def test_timer_windows_eta_and_scopes(monkeypatch):
+    """Timer arithmetic on a fake clock: per-unit tick times over a window, ETA from the remaining
+    progress, named scopes, and the h:mm:ss formatting."""
+    from mvp_engine.utils.log import timer as timer_mod
+
+    now = [100.0]
+    monkeypatch.setattr(timer_mod.time, "perf_counter", lambda: now[0])
+    t = timer_mod.Timer(total_progress=10, window_size=2).start()
+    for dt in (1.0, 3.0, 5.0):
+        now[0] += dt
+        t.tick()
+    assert t.progress == 3 and t.progress_time == 4.0 and t.progress_time_latest == 5.0  # window of 2
+    assert t.eta == 4.0 * 7 and t.eta_string == "00:00:28"
+    with t.scope("data_time"):
+        now[0] += 0.5
+    t.record_scope("data_time", 1.5)
+    assert t.get_scope_time("data_time") == 1.0 and t.get_scope_time_latest("data_time") == 1.5
+    assert timer_mod.format_time(2 * 86400 + 3661) == "2d 01:01:01"
+
+
+def test_cuda_step_timer_falls_back_to_host_time_on_cpu(monkeypatch):
+    from mvp_engine.utils.log import timer as timer_mod
+
+    if timer_mod.torch.cuda.is_available():
+        return  # device timing is covered by the GPU runs
+    now = [5.0]
+    monkeypatch.setattr(timer_mod.time, "perf_counter", lambda: now[0])
+    st = timer_mod.CudaStepTimer()
+    st.start()
+    now[0] += 0.25
+    assert st.stop() == 250.0 and timer_mod.CudaStepTimer.max_over_ranks(7.0) == 7.0
