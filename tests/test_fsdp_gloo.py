@@ -1,5 +1,6 @@
 """Native flat FSDP on gloo ranks (CPU): world 2 must reproduce the single-process run."""
 
+import pytest
 import torch
 
 from mvp_engine.testing import spawn_workers
@@ -106,7 +107,7 @@ def test_resharded_weights_match_resident_weights():
                 assert rel < 2e-3, (ckpt, k, rel)
 
 
-def _train_hsdp(rank, world, port, hsdp):
+def _train_hsdp(rank, world, port, hsdp, reshard=False):
     import torch.distributed as dist
 
     from mvp_engine.distributed.init import initialize_process_group
@@ -121,7 +122,8 @@ def _train_hsdp(rank, world, port, hsdp):
                         num_attention_heads=2, num_key_value_heads=1, num_hidden_layers=2)
     if hsdp:
         fsdp = NativeFSDP(model, group=shard_groups[rank // 2], device=torch.device("cpu"),
-                          param_dtype=torch.float32, replicate_group=rep_groups[rank % 2])
+                          param_dtype=torch.float32, replicate_group=rep_groups[rank % 2],
+                          reshard_after_forward=reshard)
         assert fsdp.world == 2 and fsdp.rep_world == 2
     else:
         fsdp = NativeFSDP(model, group=dist.group.WORLD, device=torch.device("cpu"), param_dtype=torch.float32)
@@ -141,10 +143,12 @@ def _train_hsdp(rank, world, port, hsdp):
     return losses, {k: v.clone() for k, v in full.items() if "layers.1." in k}
 
 
-def test_hsdp_matches_flat_sharding():
-    """Replicate x shard (2 x 2) with gradient shards averaged over the replicas equals sharding over all 4."""
+@pytest.mark.parametrize("reshard", [False, True])
+def test_hsdp_matches_flat_sharding(reshard):
+    """Replicate x shard (2 x 2) with gradient shards averaged over the replicas equals sharding over all 4,
+    with resident weights and with weights resharded after each use (gathered within the shard group)."""
     flat = spawn_workers(_train_hsdp, 4, False, timeout=300)
-    hsdp = spawn_workers(_train_hsdp, 4, True, timeout=300)
+    hsdp = spawn_workers(_train_hsdp, 4, True, reshard, timeout=300)
     for (lf, wf), (lh, wh) in zip(flat, hsdp):
         for a, b in zip(lf, lh):
             assert abs(a - b) <= 1e-5 * abs(a), (lf, lh)
