@@ -64,7 +64,7 @@ def test_context_parallel_attention_matches_full(impl, world):
     torch.testing.assert_close(dv, vv.grad, atol=2e-5, rtol=1e-4)
 
 
-def _cp_model_step(rank, world, port, impl):
+def _cp_model_step(rank, world, port, impl, reshard=False):
     import torch.distributed as dist
 
     from mvp_engine.distributed.init import initialize_process_group
@@ -88,7 +88,9 @@ def _cp_model_step(rank, world, port, impl):
     if world > 1:
         model._mvp_cp = ContextParallel(group, impl=impl)
         batch = model._mvp_cp.shard_batch(batch)
-    fsdp = NativeFSDP(model, group=group, device=torch.device("cpu"), param_dtype=torch.float32)
+    fsdp = NativeFSDP(model, group=group, device=torch.device("cpu"), param_dtype=torch.float32,
+                      reshard_after_forward=reshard and world > 1)
+    assert sum(u.resharded for u in fsdp.units) == (2 if reshard and world > 1 else 0)
     keys = ("input_ids", "labels", "shift_labels", "position_ids", "cu_seq_lens_q", "max_length_q")
     out = fsdp(**{k: batch[k] for k in keys if k in batch})
     loss_sum = out["loss"].sum()
@@ -102,10 +104,13 @@ def _cp_model_step(rank, world, port, impl):
     return float(total), float(gn)
 
 
+@pytest.mark.parametrize("reshard", [False, True])
 @pytest.mark.parametrize("impl", ["ring", "ulysses"])
-def test_context_parallel_model_step_matches_single_process(impl):
+def test_context_parallel_model_step_matches_single_process(impl, reshard):
+    """Context-parallel ranks (sharing the parameters, resident or resharded after each use) reproduce the
+    single-process loss and gradient norm."""
     single = spawn_workers(_cp_model_step, 1, impl, timeout=300)[0]
-    multi = spawn_workers(_cp_model_step, 2, impl, timeout=300)
+    multi = spawn_workers(_cp_model_step, 2, impl, reshard, timeout=300)
     for loss, gn in multi:
         assert abs(loss - single[0]) < 1e-4 * abs(single[0]), (loss, single)
         # gradients are averaged over the 2 ranks: the norm of the mean is half the summed norm
