@@ -6,7 +6,7 @@ import torch
 from mvp_engine.testing import spawn_workers
 
 
-def _train(rank, world, port, tp_size, sp, steps):
+def _train(rank, world, port, tp_size, sp, steps, dp_rows=None, reshard=False):
     import torch.distributed as dist
 
     from mvp_engine.distributed.init import initialize_process_group
@@ -28,9 +28,10 @@ def _train(rank, world, port, tp_size, sp, steps):
         tp_group = tp_groups[rank // tp_size]
         dp_group = dp_groups[rank % tp_size] if world // tp_size > 1 else None
         apply_native_tensor_parallel(model, group=tp_group, sequence_parallel=sp)
-    dp = world // tp_size
+    dp = dp_rows or world // tp_size
     fsdp = NativeFSDP(model, group=dp_group, device=torch.device("cpu"), param_dtype=torch.float32,
-                      tp_group=tp_group)
+                      tp_group=tp_group, reshard_after_forward=reshard)
+    assert sum(u.resharded for u in fsdp.units) == (2 if reshard else 0)
     opt = FlatAdamW(fsdp, lr=1e-2, weight_decay=0.0)
     g = torch.Generator().manual_seed(9)
     T = 64
@@ -63,20 +64,17 @@ def _train(rank, world, port, tp_size, sp, steps):
     return losses, norms
 
 
-@pytest.mark.parametrize("world,tp,sp", [(2, 2, True), (2, 2, False), (4, 2, True)])
-def test_tensor_parallel_matches_single_process(world, tp, sp):
+@pytest.mark.parametrize("world,tp,sp,reshard", [(2, 2, True, False), (2, 2, False, False), (4, 2, True, False),
+                                                (4, 2, True, True)])
+def test_tensor_parallel_matches_single_process(world, tp, sp, reshard):
+    """Tensor (+ sequence) parallel ranks, with data parallelism over the tensor groups when world > tp and
+    optionally resharded weights, reproduce one process that sees the data-parallel rows as micro-batches
+    of the same optimizer step: losses and gradient norms over three AdamW steps."""
     dp = world // tp
-    single = spawn_workers(_train, 1, 1, False, 3, timeout=300)[0]
-    if dp > 1:
-        # the single process sees the dp rows as two micro-batches of one optimizer step
-        pass
-    multi = spawn_workers(_train, world, tp, sp, 3, timeout=300)
-    if dp == 1:
-        for losses, norms in multi:
-            for a, b in zip(losses, single[0]):
-                assert abs(a - b) < 2e-4 * abs(b), (losses, single[0])
-            for a, b in zip(norms, single[1]):
-                assert abs(a - b) < 2e-3 * abs(b), (norms, single[1])
-    else:
-        for losses, _ in multi:
-            assert losses == pytest.approx(multi[0][0], rel=1e-6)
+    single = spawn_workers(_train, 1, 1, False, 3, dp, timeout=300)[0]
+    multi = spawn_workers(_train, world, tp, sp, 3, None, reshard, timeout=300)
+    for losses, norms in multi:
+        for a, b in zip(losses, single[0]):
+            assert abs(a - b) < 2e-4 * abs(b), (losses, single[0])
+        for a, b in zip(norms, single[1]):
+            assert abs(a - b) < 2e-3 * abs(b), (norms, single[1])
