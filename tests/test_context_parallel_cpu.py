@@ -115,3 +115,53 @@ def test_context_parallel_model_step_matches_single_process(impl, reshard):
         assert abs(loss - single[0]) < 1e-4 * abs(single[0]), (loss, single)
         # gradients are averaged over the 2 ranks: the norm of the mean is half the summed norm
         assert abs(2 * gn - single[1]) < 2e-4 * single[1], (gn, single)
+
+
+def _cp_tp_step(rank, world, port, impl, tp, cp, sp):
+    """One forward + backward of a tiny Qwen3 through the public wrapping (mesh -> parallelize_model ->
+    host-side batch cut), on a context x tensor mesh."""
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.distributed.parallel_mesh import ParallelMesh
+    from mvp_engine.distributed.parallelize import parallelize_model
+    from mvp_engine.kit.llm.data.collator import varlen_metadata
+    from mvp_engine.models.qwen3 import build_qwen3
+    from mvp_engine.parallel.context import maybe_shard_batch
+
+    if world > 1:
+        initialize_process_group()
+    mesh = ParallelMesh.initialize("cpu", {"replicate": 1, "shard": 1, "context": cp, "tensor": tp})
+    model = build_qwen3("mvp/qwen3-tiny", seed=3, vocab_size=256, hidden_size=64, intermediate_size=128,
+                        num_attention_heads=8, num_key_value_heads=4, num_hidden_layers=2, head_dim=16)
+    g = torch.Generator().manual_seed(11)
+    T = 64
+    ids = torch.randint(0, 256, (1, T), generator=g)
+    seg = torch.tensor([[1] * 20 + [2] * 30 + [3] * 14])
+    cu, mx, pos = varlen_metadata(seg)
+    batch = {"input_ids": ids, "labels": ids.clone(), "pack_segment_ids": seg, "cu_seq_lens_q": cu,
+             "max_length_q": mx, "position_ids": pos}
+    wrapped = parallelize_model(model, parallel_mesh=mesh, device=torch.device("cpu"),
+                                backend_kwargs={"impl": "native", "sequence_parallel": sp,
+                                                "context_parallel": {"impl": impl}, "comm": {"fused": False}})
+    batch = maybe_shard_batch(model, batch)
+    keys = ("input_ids", "labels", "shift_labels", "position_ids", "cu_seq_lens_q", "max_length_q")
+    loss = wrapped(**{k: batch[k] for k in keys if k in batch})["loss"].sum()
+    loss.backward()
+    total = loss.detach().clone()
+    if world > 1:
+        dist.all_reduce(total, group=mesh.dp_cp.group)  # context ranks hold different tokens
+        if sp:
+            dist.all_reduce(total, group=mesh.tp.group)  # and so do sequence-parallel tensor ranks
+    return float(total), float(wrapped.clip_grad_norm_(1e9))
+
+
+@pytest.mark.parametrize("sp", [False, True])
+@pytest.mark.parametrize("impl", ["ring", "ulysses"])
+def test_context_parallel_composes_with_tensor_parallel(impl, sp):
+    """context 2 x tensor 2 (with and without sequence parallelism) against one process: the same loss, and
+    the gradient norm of the average over the two context ranks (half the one-process norm)."""
+    single = spawn_workers(_cp_tp_step, 1, impl, 1, 1, False, timeout=300)[0]
+    for loss, gn in spawn_workers(_cp_tp_step, 4, impl, 2, 2, sp, timeout=300):
+        assert abs(loss - single[0]) < 1e-4 * abs(single[0]), (loss, single)
+        assert abs(2 * gn - single[1]) < 2e-4 * single[1], (gn, single)
