@@ -78,3 +78,46 @@ def test_tensor_parallel_matches_single_process(world, tp, sp, reshard):
             assert abs(a - b) < 2e-4 * abs(b), (losses, single[0])
         for a, b in zip(norms, single[1]):
             assert abs(a - b) < 2e-3 * abs(b), (norms, single[1])
+
+
+def _hsdp_tp_step(rank, world, port, rep, shard, tp, sp, reshard):
+    """One forward + backward through the public wrapping on a replicate x shard x tensor mesh; every
+    data-parallel rank feeds the same row, so the averaged gradient is the one-process gradient."""
+    import torch.distributed as dist
+
+    from mvp_engine.distributed.init import initialize_process_group
+    from mvp_engine.distributed.parallel_mesh import ParallelMesh
+    from mvp_engine.distributed.parallelize import parallelize_model
+    from mvp_engine.kit.llm.data.collator import varlen_metadata
+    from mvp_engine.models.qwen3 import build_qwen3
+
+    if world > 1:
+        initialize_process_group()
+    mesh = ParallelMesh.initialize("cpu", {"replicate": rep, "shard": shard, "context": 1, "tensor": tp})
+    model = build_qwen3("mvp/qwen3-tiny", seed=3, vocab_size=256, hidden_size=64, intermediate_size=128,
+                        num_attention_heads=8, num_key_value_heads=4, num_hidden_layers=2, head_dim=16)
+    g = torch.Generator().manual_seed(11)
+    T = 64
+    ids = torch.randint(0, 256, (1, T), generator=g)
+    seg = torch.tensor([[1] * 20 + [2] * 30 + [3] * 14])
+    cu, mx, pos = varlen_metadata(seg)
+    wrapped = parallelize_model(model, parallel_mesh=mesh, device=torch.device("cpu"),
+                                backend_kwargs={"impl": "native", "sequence_parallel": sp, "comm": {"fused": False},
+                                                "reshard_after_forward": reshard})
+    loss = wrapped(input_ids=ids, labels=ids.clone(), position_ids=pos, cu_seq_lens_q=cu,
+                   max_length_q=mx)["loss"].sum()
+    loss.backward()
+    total = loss.detach().clone()
+    if sp:
+        dist.all_reduce(total, group=mesh.tp.group)  # each tensor rank holds the losses of 1/tp of the tokens
+    return float(total), float(wrapped.clip_grad_norm_(1e9)), wrapped.rep_world
+
+
+@pytest.mark.parametrize("sp,reshard", [(False, False), (True, True)])
+def test_hsdp_composes_with_tensor_parallel(sp, reshard):
+    """replicate 2 x shard 2 x tensor 2 (8 gloo ranks): HSDP is active and loss and gradient norm equal
+    the one-process run."""
+    single = spawn_workers(_hsdp_tp_step, 1, 1, 1, 1, False, False, timeout=300)[0]
+    for loss, gn, rep_world in spawn_workers(_hsdp_tp_step, 8, 2, 2, 2, sp, reshard, timeout=600):
+        assert rep_world == 2
+        assert abs(loss - single[0]) < 1e-4 * abs(single[0]) and abs(gn - single[1]) < 2e-4 * single[1]
