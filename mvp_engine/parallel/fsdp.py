@@ -429,8 +429,15 @@ class NativeFSDP(nn.Module):
                     # Materialise straight into the flat buffers, one parameter at a time.
                     if init is None:
                         raise RuntimeError(f"{e.fqns[0]} is on the meta device and the model has no init_param_")
-                    tmp = torch.empty(e.shape, dtype=torch.float32, device=dev)
-                    init(e.fqns[0], tmp, seed)
+                    cut = getattr(p, "_mvp_tp_slice", None)  # a tensor-parallel slice of a larger weight
+                    if cut is None:
+                        tmp = torch.empty(e.shape, dtype=torch.float32, device=dev)
+                        init(e.fqns[0], tmp, seed)
+                    else:
+                        full_shape, dim, start, stop = cut
+                        tmp = torch.empty(full_shape, dtype=torch.float32, device=dev)
+                        init(e.fqns[0], tmp, seed)
+                        tmp = tmp.narrow(dim, start, stop - start).contiguous()
                     flat = tmp.reshape(-1)
                 else:
                     flat = p.detach().reshape(-1)

@@ -130,10 +130,20 @@ def _shard_rows(t: torch.Tensor, parts: list[tuple[int, int]]) -> torch.Tensor:
     return torch.cat([t[a:b] for a, b in parts], dim=0)
 
 
-def _replace(mod: nn.Module, name: str, value: torch.Tensor) -> None:
+def _replace(mod: nn.Module, name: str, dim: int, start: int, stop: int) -> None:
+    """Replace ``mod.<name>`` by its ``[start, stop)`` slice along ``dim``.  A parameter still on the meta
+    device records the slice (``_mvp_tp_slice``): the data-parallel runtime then initialises the full
+    tensor and keeps this slice, so a tensor-parallel model starts from exactly the weights of the unsharded
+    one (initialising the slice by itself would give every rank the same values)."""
     p = getattr(mod, name)
-    new = nn.Parameter(value.detach().clone() if value.device.type != "meta" else value, requires_grad=p.requires_grad)
+    value = p.narrow(dim, start, stop - start)
+    meta = value.device.type == "meta"
+    new = nn.Parameter(value if meta else value.detach().clone(), requires_grad=p.requires_grad)
     new._mvp_tp_sharded = True
+    if meta:
+        if getattr(p, "_mvp_tp_slice", None) is not None:  # one slice per parameter is all that is recorded
+            raise RuntimeError(f"{name} is already tensor-parallel sharded")
+        new._mvp_tp_slice = (tuple(p.shape), dim, start, stop)
     setattr(mod, name, new)
 
 
@@ -154,17 +164,17 @@ def apply_native_tensor_parallel(model: nn.Module, parallel_mesh: Any = None, *,
         if Hq % W or Hkv % W:
             raise ValueError(f"tensor parallel {W} needs query ({Hq}) and key/value ({Hkv}) heads divisible by it")
         hq, hkv = Hq // W, Hkv // W
-        _replace(a.q_proj, "weight", a.q_proj.weight[r * hq * D:(r + 1) * hq * D])
-        _replace(a.k_proj, "weight", a.k_proj.weight[r * hkv * D:(r + 1) * hkv * D])
-        _replace(a.v_proj, "weight", a.v_proj.weight[r * hkv * D:(r + 1) * hkv * D])
-        _replace(a.o_proj, "weight", a.o_proj.weight[:, r * hq * D:(r + 1) * hq * D])
+        _replace(a.q_proj, "weight", 0, r * hq * D, (r + 1) * hq * D)
+        _replace(a.k_proj, "weight", 0, r * hkv * D, (r + 1) * hkv * D)
+        _replace(a.v_proj, "weight", 0, r * hkv * D, (r + 1) * hkv * D)
+        _replace(a.o_proj, "weight", 1, r * hq * D, (r + 1) * hq * D)
         F = m.gate_proj.weight.shape[0]
         if F % W:
             raise ValueError(f"tensor parallel {W} needs the FFN width ({F}) divisible by it")
         f = F // W
-        _replace(m.gate_proj, "weight", m.gate_proj.weight[r * f:(r + 1) * f])
-        _replace(m.up_proj, "weight", m.up_proj.weight[r * f:(r + 1) * f])
-        _replace(m.down_proj, "weight", m.down_proj.weight[:, r * f:(r + 1) * f])
+        _replace(m.gate_proj, "weight", 0, r * f, (r + 1) * f)
+        _replace(m.up_proj, "weight", 0, r * f, (r + 1) * f)
+        _replace(m.down_proj, "weight", 1, r * f, (r + 1) * f)
         a.num_heads, a.num_kv_heads = hq, hkv
         a.q_norm.weight._mvp_tp_partial = True  # per-head norms see only this rank's heads
         a.k_norm.weight._mvp_tp_partial = True
