@@ -1,7 +1,9 @@
 """The Qwen3 recipe engine end to end on gloo ranks: tensor parallelism (with and without sequence
-parallelism) and context parallelism (ring, Ulysses) reproduce the one-process loss curve over three
-optimizer steps -- data distribution, host-side batch cut, loss / token reductions, meta-device init of
-sharded weights and the optimizer included."""
+parallelism) and context parallelism (ring, Ulysses) -- layouts whose ranks all read the one data stream --
+reproduce the one-process loss curve over three optimizer steps -- data distribution, host-side batch cut, loss / token reductions, meta-device init of
+sharded weights and the optimizer included.  (Data-parallel ranks read different shards of the stream, so
+their curves differ from one process's by design; the runtime-level tests in ``test_fsdp_gloo.py`` feed
+them identical rows instead.)"""
 
 from __future__ import annotations
 
@@ -17,7 +19,7 @@ _TINY = ("loop.total_steps=3", "checkpoint.interval=100000", "log.backends=[term
          "model.config_overrides.num_hidden_layers=2", "optim.mixed_precision=fp32",
          "data.train_path=synthetic://text?vocab=512&min_len=16&max_len=96", "data.max_seq_len=128",
          "optim.global_batch_size=2", "model.gradient_checkpointing.enabled=false", "optim.warmup_ratio=0.0",
-         "parallel.mesh.shard=1")
+         "parallel.mesh.replicate=1", "parallel.mesh.shard=1")
 
 
 def _run(rank, world, port, overrides, out_dir):
@@ -42,19 +44,27 @@ def _run(rank, world, port, overrides, out_dir):
     return losses
 
 
-@pytest.fixture(scope="module")
-def single(tmp_path_factory):
-    return spawn_workers(_run, 1, (), str(tmp_path_factory.mktemp("single")), timeout=600)[0]
+_SINGLE: dict = {}
 
 
-@pytest.mark.parametrize("overrides", [
-    ("parallel.mesh.tensor=2", "parallel.backend_kwargs.sequence_parallel=false"),
-    ("parallel.mesh.tensor=2", "parallel.backend_kwargs.sequence_parallel=true"),
-    ("parallel.mesh.context=2", "parallel.backend_kwargs.context_parallel.impl=ring"),
-    ("parallel.mesh.context=2", "parallel.backend_kwargs.context_parallel.impl=ulysses"),
+def _single(global_batch: int, tmp_path_factory) -> list:
+    if global_batch not in _SINGLE:
+        out = str(tmp_path_factory.mktemp(f"single{global_batch}"))
+        _SINGLE[global_batch] = spawn_workers(_run, 1, (f"optim.global_batch_size={global_batch}",), out,
+                                              timeout=600)[0]
+    return _SINGLE[global_batch]
+
+
+@pytest.mark.parametrize("world,overrides", [
+    (2, ("parallel.mesh.tensor=2", "parallel.backend_kwargs.sequence_parallel=false")),
+    (2, ("parallel.mesh.tensor=2", "parallel.backend_kwargs.sequence_parallel=true")),
+    (2, ("parallel.mesh.context=2", "parallel.backend_kwargs.context_parallel.impl=ring")),
+    (2, ("parallel.mesh.context=2", "parallel.backend_kwargs.context_parallel.impl=ulysses")),
 ], ids=["tp", "tp-sp", "cp-ring", "cp-ulysses"])
-def test_engine_two_ranks_reproduce_one_process(single, overrides, tmp_path):
-    for losses in spawn_workers(_run, 2, overrides, str(tmp_path), timeout=600):
+def test_engine_ranks_reproduce_one_process(world, overrides, tmp_path, tmp_path_factory):
+    batch = next((int(o.split("=")[1]) for o in overrides if o.startswith("optim.global_batch_size=")), 2)
+    single = _single(batch, tmp_path_factory)
+    for losses in spawn_workers(_run, world, overrides, str(tmp_path), timeout=600):
         assert len(losses) == len(single) == 3
         for a, b in zip(losses, single):
             assert abs(a - b) <= 2e-5 * abs(b), (overrides, losses, single)
