@@ -1,9 +1,10 @@
 """The Qwen3 recipe engine end to end on gloo ranks: tensor parallelism (with and without sequence
-parallelism) and context parallelism (ring, Ulysses) -- layouts whose ranks all read the one data stream --
-reproduce the one-process loss curve over three optimizer steps -- data distribution, host-side batch cut, loss / token reductions, meta-device init of
-sharded weights and the optimizer included.  (Data-parallel ranks read different shards of the stream, so
-their curves differ from one process's by design; the runtime-level tests in ``test_fsdp_gloo.py`` feed
-them identical rows instead.)"""
+parallelism) and context parallelism (ring, Ulysses) -- layouts whose ranks all read the one data
+stream -- reproduce the one-process loss curve over three optimizer steps: data distribution, host-side
+batch cut, loss / token reductions, meta-device init of sharded weights and the optimizer included.
+
+Data-parallel ranks read different shards of the stream, so their curves differ from one process's by
+design; the runtime-level tests in ``test_fsdp_gloo.py`` feed them identical rows instead."""
 
 from __future__ import annotations
 
