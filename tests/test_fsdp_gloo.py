@@ -6,7 +6,7 @@ import torch
 from mvp_engine.testing import spawn_workers
 
 
-def _train(rank, world, port, steps, seed):
+def _train(rank, world, port, steps, seed, tied=False):
     import os
 
     import torch.distributed as dist
@@ -20,7 +20,9 @@ def _train(rank, world, port, steps, seed):
         initialize_process_group()
     group = dist.group.WORLD if world > 1 else None
     model = build_qwen3("mvp/qwen3-tiny", seed=seed, vocab_size=256, hidden_size=128, intermediate_size=256,
-                        num_attention_heads=2, num_key_value_heads=1)
+                        num_attention_heads=2, num_key_value_heads=1, tie_word_embeddings=tied)
+    if tied:
+        assert model.lm_head.weight is model.model.embed_tokens.weight
     fsdp = NativeFSDP(model, group=group, device=torch.device("cpu"), param_dtype=torch.float32)
     opt = FlatAdamW(fsdp, lr=1e-3, weight_decay=0.1)
     g = torch.Generator().manual_seed(123)
@@ -43,9 +45,12 @@ def _train(rank, world, port, steps, seed):
     return losses, {k: v.clone() for k, v in list(sd.items())[:4]}
 
 
-def test_fsdp_world2_matches_single_process():
-    single = spawn_workers(_train, 1, 5, 7)[0]
-    multi = spawn_workers(_train, 2, 5, 7)
+@pytest.mark.parametrize("tied", [False, True])
+def test_fsdp_world2_matches_single_process(tied):
+    """World 2 against one process over 5 AdamW steps with clipping; ``tied``: the LM head shares the
+    embedding matrix (the small Qwen3 presets), one flat-buffer entry under two names."""
+    single = spawn_workers(_train, 1, 5, 7, tied)[0]
+    multi = spawn_workers(_train, 2, 5, 7, tied)
     for a, b in zip(single[0], multi[0][0]):
         assert abs(a - b) < 2e-3 * max(1.0, abs(a)), (single[0], multi[0][0])
     assert multi[0][0] == multi[1][0]
