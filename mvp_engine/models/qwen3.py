@@ -327,6 +327,7 @@ class Qwen3ForCausalLM(nn.Module):
     """HF-compatible Qwen3 causal LM; ``forward`` returns per-token loss when labels are given."""
 
     _no_split_modules = ["Qwen3DecoderLayer"]
+    supports_sequence_parallel = True  # the embedding / loss work on this tensor rank's token slice
     base_model_prefix = "model"
 
     def __init__(self, config: Qwen3Config):

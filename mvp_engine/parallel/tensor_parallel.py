@@ -153,6 +153,9 @@ def apply_native_tensor_parallel(model: nn.Module, parallel_mesh: Any = None, *,
     runtime as ``model._mvp_tp``; returns it."""
     from ..models.qwen3 import Qwen3DecoderLayer
 
+    if sequence_parallel and not getattr(model, "supports_sequence_parallel", False):
+        raise ValueError(f"{type(model).__name__} does not implement sequence parallelism (the token slicing around "
+                         "its embedding and loss); use tensor parallelism without it")
     grp = group if group is not None else parallel_mesh.tp.group
     tp = TensorParallel(grp, sequence_parallel=sequence_parallel, fused=fused)
     W, r = tp.world, tp.rank

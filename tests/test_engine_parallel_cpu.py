@@ -69,3 +69,43 @@ def test_engine_ranks_reproduce_one_process(world, overrides, tmp_path, tmp_path
         assert len(losses) == len(single) == 3
         for a, b in zip(losses, single):
             assert abs(a - b) <= 2e-5 * abs(b), (overrides, losses, single)
+
+
+def _run_vl(rank, world, port, overrides, out_dir):
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = ROOT / "recipes" / "qwen3_vl"
+    import_recipe_modules(root)
+    cfg = load_smoke_test_config(root, "synthetic_tiny", output_dir=Path(out_dir), run_id=f"v{rank}",
+                                 config_overrides=("loop.total_steps=2", "checkpoint.interval=1000000",
+                                                   "optim.global_batch_size=2", "optim.mixed_precision=fp32",
+                                                   "parallel.mesh.shard=1") + tuple(overrides))
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    losses = []
+    post = eng.train_post_step
+
+    def record(ctx):
+        post(ctx)
+        losses.append(eng.last_logs["train/loss"])
+
+    eng.train_post_step = record
+    eng.train()
+    return losses
+
+
+def test_vl_engine_tensor_parallel_reproduces_one_process(tmp_path):
+    single = spawn_workers(_run_vl, 1, (), str(tmp_path / "one"), timeout=600)[0]
+    for losses in spawn_workers(_run_vl, 2, ("parallel.mesh.tensor=2",), str(tmp_path / "tp"), timeout=600):
+        for a, b in zip(losses, single):
+            assert abs(a - b) <= 2e-5 * abs(b), (losses, single)
+
+
+def test_sequence_parallel_is_refused_where_the_model_lacks_it():
+    from mvp_engine.models.qwen3_vl import build_qwen3_vl
+    from mvp_engine.parallel.tensor_parallel import apply_native_tensor_parallel
+
+    model = build_qwen3_vl("mvp/qwen3-vl-tiny", device="meta")
+    with pytest.raises(ValueError, match="sequence parallelism"):
+        apply_native_tensor_parallel(model, sequence_parallel=True)
