@@ -42,6 +42,10 @@ class Qwen3VLEngine(Engine):
 
     def __init__(self, config):
         super().__init__(config)
+        if self.parallel_mesh.has_dim("context") and self.parallel_mesh.cp.active:
+            # the packed rows carry image features at placeholder positions; cutting them into context
+            # chunks would need the vision outputs scattered per chunk, which this recipe does not do
+            raise ValueError("the Qwen3-VL recipe does not support context parallelism (parallel.mesh.context)")
         self.config.resolve_batching_config(data_parallel_world_size=self.parallel_mesh.dp.world_size)
         self.data_kit = MLLMDataKit()
         self.model_kit = MLLMModelKit()

@@ -109,3 +109,16 @@ def test_sequence_parallel_is_refused_where_the_model_lacks_it():
     model = build_qwen3_vl("mvp/qwen3-vl-tiny", device="meta")
     with pytest.raises(ValueError, match="sequence parallelism"):
         apply_native_tensor_parallel(model, sequence_parallel=True)
+
+
+def _vl_with_context(rank, world, port, out_dir):
+    try:
+        _run_vl(rank, world, port, ("parallel.mesh.context=2",), out_dir)
+    except ValueError as exc:
+        return str(exc)
+    return "ran"
+
+
+def test_vl_engine_refuses_context_parallelism(tmp_path):
+    for msg in spawn_workers(_vl_with_context, 2, str(tmp_path), timeout=300):
+        assert "context parallelism" in msg
