@@ -159,9 +159,10 @@ def apply_native_tensor_parallel(model: nn.Module, parallel_mesh: Any = None, *,
     grp = group if group is not None else parallel_mesh.tp.group
     tp = TensorParallel(grp, sequence_parallel=sequence_parallel, fused=fused)
     W, r = tp.world, tp.rank
-    for layer in model.modules():
-        if not isinstance(layer, Qwen3DecoderLayer):
-            continue
+    layers = [m for m in model.modules() if isinstance(m, Qwen3DecoderLayer)]
+    if not layers:
+        raise ValueError(f"native tensor parallelism shards Qwen3 decoder layers; {type(model).__name__} has none")
+    for layer in layers:
         a, m = layer.self_attn, layer.mlp
         Hq, Hkv, D = a.num_heads, a.num_kv_heads, a.head_dim
         if Hq % W or Hkv % W:
