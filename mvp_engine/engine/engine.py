@@ -244,6 +244,12 @@ class Engine(ABC):
         getter = getattr(loader, "state_dict", None)
         return getter() if callable(getter) else None
 
+    def _data_coord(self) -> tuple[int, int]:
+        """(rank, size) of this rank's share of the data stream: ranks of one data-parallel coordinate
+        (tensor and context ranks) read the same stream."""
+        dp = self.parallel_mesh.dp
+        return int(dp.rank), int(dp.world_size)
+
     def save(self, force: bool = False) -> None:
         due = force or self.step % self.config.checkpoint.interval == 0
         if self.config.dev_mode or not due:
@@ -256,7 +262,8 @@ class Engine(ABC):
         target = store.begin(tag)
         save_checkpoint(self.parallel_mesh.device_mesh, target, self.model, self.optimizer, scheduler=self.scheduler,
                         scaler=self.scaler, step=self.step, epoch=self.epoch, _accumulate_step=self._accumulate_step,
-                        hf_enable=self.config.checkpoint.hf_enable, data_state=self._data_state())
+                        hf_enable=self.config.checkpoint.hf_enable, data_state=self._data_state(),
+                        data_coord=self._data_coord())
         store.commit(tag, self.step)
 
     def load(self, ckpt_path: Union[str, PathLike], restore_training_state: bool = True,
@@ -269,7 +276,7 @@ class Engine(ABC):
                                 scheduler=self.scheduler if restore else None,
                                 scaler=self.scaler if restore else None,
                                 restore_engine_state=restore, restore_rng_state=restore_rng_state,
-                                hf_enable=self.config.checkpoint.hf_enable)
+                                hf_enable=self.config.checkpoint.hf_enable, data_coord=self._data_coord())
         if state is None:
             return
         self.step, self.epoch = int(state["step"]), int(state["epoch"])

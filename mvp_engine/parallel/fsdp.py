@@ -77,6 +77,12 @@ class _Entry:
     requires_grad: bool
     tp_partial: bool = False  # replicated over tensor parallelism, gradient summed over the tensor group
     tp_replicated: bool = False  # same value on every tensor rank (partial or not)
+    tp_slice: Optional[tuple] = None  # (full shape, dim, start, stop): this rank's slice of a sharded weight
+
+    @property
+    def logical_shape(self) -> torch.Size:
+        """Shape of the parameter as checkpoints store it (the full tensor for tensor-parallel slices)."""
+        return torch.Size(self.tp_slice[0]) if self.tp_slice is not None else self.shape
 
 
 @dataclass
@@ -272,7 +278,8 @@ class NativeFSDP(nn.Module):
                 unit = self.units[owning_unit(fqn)]
                 e = _Entry([fqn], [(mod, pname)], p.shape, p.numel(), 0, p.requires_grad,
                            tp_partial=self.tp_world > 1 and bool(getattr(p, "_mvp_tp_partial", False)),
-                           tp_replicated=self.tp_world > 1 and not getattr(p, "_mvp_tp_sharded", False))
+                           tp_replicated=self.tp_world > 1 and not getattr(p, "_mvp_tp_sharded", False),
+                           tp_slice=getattr(p, "_mvp_tp_slice", None) if self.tp_world > 1 else None)
                 seen[id(p)] = e
                 unit.entries.append(e)
         # Frozen parameters of a unit move to a sibling unit without optimizer state.
@@ -893,6 +900,16 @@ class NativeFSDP(nn.Module):
         dist.all_gather(parts, flat_shard.contiguous(), group=self.group)
         return torch.cat(parts)
 
+    @torch.no_grad()
+    def _tp_full(self, e: _Entry, t: torch.Tensor) -> torch.Tensor:
+        """The full logical tensor of a tensor-parallel slice: the tensor ranks' equal slices, in rank
+        order, concatenated along the sharded dimension (every tensor rank calls this in the same order)."""
+        if e.tp_slice is None:
+            return t
+        parts = [torch.empty_like(t) for _ in range(self.tp_world)]
+        dist.all_gather(parts, t.contiguous(), group=self.tp_group)
+        return torch.cat(parts, dim=e.tp_slice[1])
+
     def _iter_tensors(self, which: str, full: bool):
         for u in self.units:
             if which != "param" and not u.trainable:
@@ -902,11 +919,20 @@ class NativeFSDP(nn.Module):
             else:
                 src = self._full_fp32(u, getattr(u, which))
             for e in u.entries:
-                t = src[e.offset:e.offset + e.numel].view(e.shape)
+                t = self._tp_full(e, src[e.offset:e.offset + e.numel].view(e.shape))
                 if full or self.world == 1:
                     yield e, t.detach().to("cpu", copy=True)
                 else:
-                    yield e, self._to_dtensor(self._shard_rows(t).detach().clone().cpu(), e.shape)
+                    yield e, self._to_dtensor(self._shard_rows(t).detach().clone().cpu(), e.logical_shape)
+
+    def _local_value(self, e: _Entry, v: Any) -> torch.Tensor:
+        """A checkpoint value (full logical tensor or DTensor) as this rank's entry: cut to the tensor
+        rank's slice for tensor-parallel weights."""
+        t = self._full_from_value(v, e.logical_shape)
+        if e.tp_slice is not None:
+            _, dim, start, stop = e.tp_slice
+            t = t.narrow(dim, start, stop - start)
+        return t.reshape(-1)
 
     @torch.no_grad()
     def checkpoint_state_dict(self, full: bool = False) -> dict[str, Any]:
@@ -924,7 +950,7 @@ class NativeFSDP(nn.Module):
                 key = next((f for f in e.fqns if f in sd), None)
                 if key is None:
                     continue
-                stage[e.offset:e.offset + e.numel].copy_(self._full_from_value(sd[key], e.shape).reshape(-1))
+                stage[e.offset:e.offset + e.numel].copy_(self._local_value(e, sd[key]))
             lo, hi = u.local_range(self.rank)
             if u.trainable:
                 u.master.copy_(stage[lo:hi])
@@ -962,8 +988,7 @@ class NativeFSDP(nn.Module):
                 for e in u.entries:
                     key = next((f for f in e.fqns if f in state and name in state[f]), None)
                     if key is not None:
-                        stage[e.offset:e.offset + e.numel].copy_(
-                            self._full_from_value(state[key][name], e.shape).reshape(-1))
+                        stage[e.offset:e.offset + e.numel].copy_(self._local_value(e, state[key][name]))
                 lo, hi = u.local_range(self.rank)
                 getattr(u, name).copy_(stage[lo:hi])
 

@@ -131,19 +131,20 @@ def _shard_rows(t: torch.Tensor, parts: list[tuple[int, int]]) -> torch.Tensor:
 
 
 def _replace(mod: nn.Module, name: str, dim: int, start: int, stop: int) -> None:
-    """Replace ``mod.<name>`` by its ``[start, stop)`` slice along ``dim``.  A parameter still on the meta
-    device records the slice (``_mvp_tp_slice``): the data-parallel runtime then initialises the full
-    tensor and keeps this slice, so a tensor-parallel model starts from exactly the weights of the unsharded
-    one (initialising the slice by itself would give every rank the same values)."""
+    """Replace ``mod.<name>`` by its ``[start, stop)`` slice along ``dim`` and record the slice
+    (``_mvp_tp_slice`` = full shape, dim, start, stop).  The data-parallel runtime uses it twice: a
+    parameter still on the meta device is initialised as the full tensor and then cut, so a tensor-parallel
+    model starts from exactly the weights of the unsharded one (initialising the slice by itself would give
+    every rank the same values); and checkpoints store the full logical tensor, assembled from the tensor
+    ranks' slices, under the parameter's name."""
     p = getattr(mod, name)
+    if getattr(p, "_mvp_tp_slice", None) is not None:  # one slice per parameter is all that is recorded
+        raise RuntimeError(f"{name} is already tensor-parallel sharded")
     value = p.narrow(dim, start, stop - start)
     meta = value.device.type == "meta"
     new = nn.Parameter(value if meta else value.detach().clone(), requires_grad=p.requires_grad)
     new._mvp_tp_sharded = True
-    if meta:
-        if getattr(p, "_mvp_tp_slice", None) is not None:  # one slice per parameter is all that is recorded
-            raise RuntimeError(f"{name} is already tensor-parallel sharded")
-        new._mvp_tp_slice = (tuple(p.shape), dim, start, stop)
+    new._mvp_tp_slice = (tuple(p.shape), dim, start, stop)
     setattr(mod, name, new)
 
 

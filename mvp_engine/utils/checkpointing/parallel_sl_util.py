@@ -131,9 +131,11 @@ def _restore_rng(st: dict[str, Any]) -> None:
 # -------------------------------------------------------------------- save
 def save_checkpoint(mesh, cur_checkpoint_dir: Path, model: nn.Module, optimizer=None, scheduler=None, scaler=None,
                     step: int = 0, epoch: int = 0, _accumulate_step: int = 0, prefix: str = "",
-                    hf_enable: bool = False, data_state: Optional[dict] = None) -> None:
+                    hf_enable: bool = False, data_state: Optional[dict] = None,
+                    data_coord: Optional[tuple[int, int]] = None) -> None:
     """Write one checkpoint directory.  ``data_state`` (this rank's data-loader position, when the
-    loader reports one) is stored beside the rank's RNG state in ``engine/rank_<r>.pt``."""
+    loader reports one) is stored beside the rank's RNG state in ``engine/rank_<r>.pt``, with
+    ``data_coord`` = (data-parallel rank, data-parallel size) of the stream it belongs to."""
     cur = Path(cur_checkpoint_dir)
     backend = infer_checkpoint_backend(mesh)
     if prefix == "":
@@ -142,6 +144,8 @@ def save_checkpoint(mesh, cur_checkpoint_dir: Path, model: nn.Module, optimizer=
         per_rank = _rng_state()
         if data_state is not None:
             per_rank["data_state"] = data_state
+        if data_coord is not None:
+            per_rank["data_coord"] = tuple(int(x) for x in data_coord)
         torch.save(per_rank, cur / "engine" / f"rank_{get_rank()}.pt")
 
     if backend == "ddp":
@@ -207,7 +211,7 @@ def save_hf_checkpoint(model: nn.Module, hf_dir: Path) -> None:
 # -------------------------------------------------------------------- load
 def load_checkpoint(mesh, ckpt_path, model: nn.Module, optimizer=None, scheduler=None, scaler=None,
                     prefix: str = "", restore_engine_state: bool = True, restore_rng_state: bool = True,
-                    hf_enable: bool = False) -> Optional[dict[str, int]]:
+                    hf_enable: bool = False, data_coord: Optional[tuple[int, int]] = None) -> Optional[dict[str, int]]:
     cur = Path(ckpt_path)
     backend = infer_checkpoint_backend(mesh)
     base = _base(model)
@@ -262,14 +266,39 @@ def load_checkpoint(mesh, ckpt_path, model: nn.Module, optimizer=None, scheduler
     if scaler is not None and "scaler" in state:
         scaler.load_state_dict(state["scaler"])
     out = {"step": state["step"], "epoch": state["epoch"], "_accumulate_step": state["_accumulate_step"]}
-    per_rank_path = cur / "engine" / f"rank_{get_rank()}.pt"
-    if os.path.exists(per_rank_path):
-        per_rank = torch.load(per_rank_path, map_location="cpu", weights_only=False)
-        if restore_rng_state:
-            _restore_rng(per_rank)
-        if "data_state" in per_rank:
-            out["data_state"] = per_rank["data_state"]
+    own, stream = _per_rank_states(cur, data_coord)
+    if own is not None and restore_rng_state:
+        _restore_rng(own)
+    if stream is not None and "data_state" in stream:
+        out["data_state"] = stream["data_state"]
     return out
+
+
+def _per_rank_states(cur: Path, data_coord: Optional[tuple[int, int]]) -> tuple[Optional[dict], Optional[dict]]:
+    """(RNG state to restore, state holding this rank's data position).
+
+    The rank's own file serves both when its data coordinate matches (or either side has none: older
+    checkpoints).  After a change of layout -- e.g. a checkpoint of one process resumed by two tensor-parallel
+    ranks, which read the same stream -- the data position comes from a file with the same (data-parallel
+    rank, size); a rank without a file of its own takes that file's RNG state too.  When no file matches
+    (the data-parallel size changed, so the stream is split differently), no position is restored."""
+    def read(path: Path) -> Optional[dict]:
+        return torch.load(path, map_location="cpu", weights_only=False) if path.exists() else None
+
+    own = read(cur / "engine" / f"rank_{get_rank()}.pt")
+    want = tuple(data_coord) if data_coord is not None else None
+    if own is not None and (want is None or own.get("data_coord") in (None, want)):
+        return own, own
+    for path in sorted((cur / "engine").glob("rank_*.pt")):
+        other = read(path)
+        if other is not None and other.get("data_coord") == want:
+            return (own if own is not None else other), other
+    if own is not None or want is not None:
+        from ..log import simple_info
+
+        simple_info("data-loader position not restored: no checkpointed rank read the same share of the stream "
+                    f"(data-parallel rank / size {want})", level="warning")
+    return own, None
 
 
 def _load_model_full(base: nn.Module, sd: dict[str, torch.Tensor]) -> None:

@@ -1,0 +1,70 @@
+"""Checkpoints of parallel layouts on gloo ranks: a run that dies after step 3 and resumes from its step-2
+checkpoint continues the uninterrupted loss curve, and a checkpoint written under one layout resumes under
+another (tensor-parallel weights are stored as the full logical tensors)."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import pytest
+
+from mvp_engine.testing.utils import spawn_workers
+
+ROOT = Path(__file__).resolve().parent.parent
+_TINY = ("checkpoint.keep_n=5", "checkpoint.interval=2", "log.backends=[terminal]", "dev_mode=false",
+         "model.pretrained_model_name_or_path=mvp/qwen3-tiny", "model.config_overrides.vocab_size=512",
+         "model.config_overrides.num_hidden_layers=2", "optim.mixed_precision=fp32",
+         "data.train_path=synthetic://text?vocab=512&min_len=16&max_len=96", "data.max_seq_len=128",
+         "optim.global_batch_size=2", "model.gradient_checkpointing.enabled=false",
+         "parallel.mesh.replicate=1", "parallel.mesh.shard=1", "loop.total_steps=4")
+
+
+class _Crash(RuntimeError):
+    pass
+
+
+def _run(rank, world, port, out_dir, layout, resume, crash_at):
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = ROOT / "recipes" / "qwen3"
+    import_recipe_modules(root)
+    over = _TINY + tuple(layout) + (("resume=latest",) if resume else ())
+    cfg = load_smoke_test_config(root, "synthetic_8b", output_dir=Path(out_dir), run_id="ck", config_overrides=over)
+    eng = ENGINE_REGISTRY.get(cfg["engine"])(cfg)
+    losses = {}
+    post = eng.train_post_step
+
+    def record(ctx):
+        post(ctx)
+        losses[eng.step] = float(eng.last_logs["train/loss"])
+        if crash_at is not None and eng.step == crash_at:
+            raise _Crash  # dies after this step's update, before any later checkpoint
+
+    eng.train_post_step = record
+    eng.before_train()
+    try:
+        eng.do_train()
+    except _Crash:
+        return losses
+    eng.after_train()
+    return losses
+
+
+_TP = ("parallel.mesh.tensor=2",)
+_ONE = ()
+
+
+@pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP)], ids=["tp-tp", "tp-one", "one-tp"])
+def test_resume_across_layouts_continues_the_curve(first, second, tmp_path):
+    def world(layout):
+        return 2 if layout else 1
+
+    full = spawn_workers(_run, world(first), str(tmp_path / "full"), first, False, None, timeout=600)[0]
+    spawn_workers(_run, world(first), str(tmp_path / "run"), first, False, 3, timeout=600)
+    resumed = spawn_workers(_run, world(second), str(tmp_path / "run"), second, True, None, timeout=600)
+    for losses in resumed[:1]:
+        assert sorted(losses) == [3, 4]
+        for step in (3, 4):
+            assert abs(losses[step] - full[step]) <= 2e-5 * abs(full[step]), (step, losses, full)
