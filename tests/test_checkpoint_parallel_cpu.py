@@ -54,12 +54,14 @@ def _run(rank, world, port, out_dir, layout, resume, crash_at):
 
 _TP = ("parallel.mesh.tensor=2",)
 _ONE = ()
+_DP_TP = ("parallel.mesh.shard=2", "parallel.mesh.tensor=2")  # DCP shards over the data ranks
 
 
-@pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP)], ids=["tp-tp", "tp-one", "one-tp"])
+@pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP), (_DP_TP, _DP_TP)],
+                         ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp"])
 def test_resume_across_layouts_continues_the_curve(first, second, tmp_path):
     def world(layout):
-        return 2 if layout else 1
+        return {0: 1, 1: 2, 2: 4}[len(layout)]
 
     full = spawn_workers(_run, world(first), str(tmp_path / "full"), first, False, None, timeout=600)[0]
     spawn_workers(_run, world(first), str(tmp_path / "run"), first, False, 3, timeout=600)
