@@ -70,3 +70,29 @@ def test_resume_across_layouts_continues_the_curve(first, second, tmp_path):
         assert sorted(losses) == [3, 4]
         for step in (3, 4):
             assert abs(losses[step] - full[step]) <= 2e-5 * abs(full[step]), (step, losses, full)
+
+
+def _export(rank, world, port, out_dir, layout):
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+    from mvp_engine.testing.utils import load_smoke_test_config
+
+    root = ROOT / "recipes" / "qwen3"
+    import_recipe_modules(root)
+    over = _TINY + tuple(layout) + ("loop.total_steps=2", "checkpoint.hf_enable=true")
+    cfg = load_smoke_test_config(root, "synthetic_8b", output_dir=Path(out_dir), run_id="hf", config_overrides=over)
+    ENGINE_REGISTRY.get(cfg["engine"])(cfg).train()
+
+
+def test_hf_export_of_a_tensor_parallel_run_holds_full_weights(tmp_path):
+    """The HF export of a TP=2 run has the unsharded shapes and the one-process run's values."""
+    from safetensors.torch import load_file
+
+    spawn_workers(_export, 1, str(tmp_path / "one"), _ONE, timeout=600)
+    spawn_workers(_export, 2, str(tmp_path / "tp"), _TP, timeout=600)
+    one = load_file(str(tmp_path / "one" / "hf" / "checkpoints" / "iter_2" / "hf_model" / "model.safetensors"))
+    tp = load_file(str(tmp_path / "tp" / "hf" / "checkpoints" / "iter_2" / "hf_model" / "model.safetensors"))
+    assert one.keys() == tp.keys()
+    for k, v in one.items():
+        assert tp[k].shape == v.shape, k
+        assert ((tp[k].float() - v.float()).norm() / (v.float().norm() + 1e-12)).item() < 1e-5, k
