@@ -55,13 +55,17 @@ def _run(rank, world, port, out_dir, layout, resume, crash_at):
 _TP = ("parallel.mesh.tensor=2",)
 _ONE = ()
 _DP_TP = ("parallel.mesh.shard=2", "parallel.mesh.tensor=2")  # DCP shards over the data ranks
+_DP = ("parallel.mesh.shard=2", "parallel.backend_kwargs.reshard_after_forward=false")
+_DP_RESHARD = ("parallel.mesh.shard=2", "parallel.backend_kwargs.reshard_after_forward=true")
+_WORLD = {_TP: 2, _ONE: 1, _DP_TP: 4, _DP: 2, _DP_RESHARD: 2}
 
 
-@pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP), (_DP_TP, _DP_TP)],
-                         ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp"])
+@pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP), (_DP_TP, _DP_TP),
+                                          (_DP_RESHARD, _DP_RESHARD), (_DP_RESHARD, _DP)],
+                         ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp", "reshard-reshard", "reshard-resident"])
 def test_resume_across_layouts_continues_the_curve(first, second, tmp_path):
     def world(layout):
-        return {0: 1, 1: 2, 2: 4}[len(layout)]
+        return _WORLD[layout]
 
     full = spawn_workers(_run, world(first), str(tmp_path / "full"), first, False, None, timeout=600)[0]
     spawn_workers(_run, world(first), str(tmp_path / "run"), first, False, 3, timeout=600)
