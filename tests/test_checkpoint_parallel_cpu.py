@@ -60,20 +60,33 @@ _DP_RESHARD = ("parallel.mesh.shard=2", "parallel.backend_kwargs.reshard_after_f
 _WORLD = {_TP: 2, _ONE: 1, _DP_TP: 4, _DP: 2, _DP_RESHARD: 2}
 
 
+_CACHE: dict = {}
+
+
+def _full_and_crashed(layout, tmp_path_factory):
+    """(uninterrupted losses, directory of a run that died after step 3) for a layout, computed once."""
+    if layout not in _CACHE:
+        base = tmp_path_factory.mktemp("layout")
+        full = spawn_workers(_run, _WORLD[layout], str(base / "full"), layout, False, None, timeout=600)[0]
+        spawn_workers(_run, _WORLD[layout], str(base / "run"), layout, False, 3, timeout=600)
+        _CACHE[layout] = (full, base / "run")
+    return _CACHE[layout]
+
+
 @pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP), (_DP_TP, _DP_TP),
                                           (_DP_RESHARD, _DP_RESHARD), (_DP_RESHARD, _DP)],
                          ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp", "reshard-reshard", "reshard-resident"])
-def test_resume_across_layouts_continues_the_curve(first, second, tmp_path):
-    def world(layout):
-        return _WORLD[layout]
+def test_resume_across_layouts_continues_the_curve(first, second, tmp_path, tmp_path_factory):
+    import shutil
 
-    full = spawn_workers(_run, world(first), str(tmp_path / "full"), first, False, None, timeout=600)[0]
-    spawn_workers(_run, world(first), str(tmp_path / "run"), first, False, 3, timeout=600)
-    resumed = spawn_workers(_run, world(second), str(tmp_path / "run"), second, True, None, timeout=600)
-    for losses in resumed[:1]:
-        assert sorted(losses) == [3, 4]
-        for step in (3, 4):
-            assert abs(losses[step] - full[step]) <= 2e-5 * abs(full[step]), (step, losses, full)
+    full, crashed = _full_and_crashed(first, tmp_path_factory)
+    run_dir = tmp_path / "run"
+    shutil.copytree(crashed, run_dir)  # every resume starts from the same crashed run
+    resumed = spawn_workers(_run, _WORLD[second], str(run_dir), second, True, None, timeout=600)
+    losses = resumed[0]
+    assert sorted(losses) == [3, 4]
+    for step in (3, 4):
+        assert abs(losses[step] - full[step]) <= 2e-5 * abs(full[step]), (step, losses, full)
 
 
 def _export(rank, world, port, out_dir, layout):
