@@ -57,7 +57,11 @@ _ONE = ()
 _DP_TP = ("parallel.mesh.shard=2", "parallel.mesh.tensor=2")  # DCP shards over the data ranks
 _DP = ("parallel.mesh.shard=2", "parallel.backend_kwargs.reshard_after_forward=false")
 _DP_RESHARD = ("parallel.mesh.shard=2", "parallel.backend_kwargs.reshard_after_forward=true")
-_WORLD = {_TP: 2, _ONE: 1, _DP_TP: 4, _DP: 2, _DP_RESHARD: 2}
+# torch FSDP2, as the reference wraps models; fp32 compute, as the native runtime uses on CPU
+_TORCH = ("parallel.mesh.shard=2", "parallel.backend_kwargs.impl=torch",
+          "parallel.backend_kwargs.fsdp2.mp_policy.param_dtype=float32",
+          "parallel.backend_kwargs.fsdp2.mp_policy.output_dtype=float32")
+_WORLD = {_TP: 2, _ONE: 1, _DP_TP: 4, _DP: 2, _DP_RESHARD: 2, _TORCH: 2}
 
 
 _CACHE: dict = {}
@@ -74,8 +78,10 @@ def _full_and_crashed(layout, tmp_path_factory):
 
 
 @pytest.mark.parametrize("first,second", [(_TP, _TP), (_TP, _ONE), (_ONE, _TP), (_DP_TP, _DP_TP),
-                                          (_DP_RESHARD, _DP_RESHARD), (_DP_RESHARD, _DP)],
-                         ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp", "reshard-reshard", "reshard-resident"])
+                                          (_DP_RESHARD, _DP_RESHARD), (_DP_RESHARD, _DP), (_TORCH, _TORCH), (_TORCH, _DP),
+                                          (_DP, _TORCH)],
+                         ids=["tp-tp", "tp-one", "one-tp", "dp_tp-dp_tp", "reshard-reshard", "reshard-resident",
+                              "torch-torch", "torch-native", "native-torch"])
 def test_resume_across_layouts_continues_the_curve(first, second, tmp_path, tmp_path_factory):
     import shutil
 
@@ -85,8 +91,12 @@ def test_resume_across_layouts_continues_the_curve(first, second, tmp_path, tmp_
     resumed = spawn_workers(_run, _WORLD[second], str(run_dir), second, True, None, timeout=600)
     losses = resumed[0]
     assert sorted(losses) == [3, 4]
-    for step in (3, 4):
-        assert abs(losses[step] - full[step]) <= 2e-5 * abs(full[step]), (step, losses, full)
+    # step 3's loss comes from the restored weights alone; step 4 follows an update the resumed runtime
+    # computes itself -- across runtimes (native <-> torch FSDP2) its gradient sums run in another order,
+    # which Adam's early, nearly sign-valued updates turn into differences of order 1e-4 in the loss
+    cross_runtime = (_TORCH in (first, second)) and first != second
+    for step, tol in ((3, 2e-5), (4, 1e-3 if cross_runtime else 2e-5)):
+        assert abs(losses[step] - full[step]) <= tol * abs(full[step]), (step, losses, full)
 
 
 def _export(rank, world, port, out_dir, layout):
