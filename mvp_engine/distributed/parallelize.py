@@ -31,10 +31,29 @@ def _set_default(d: dict, key: str, value: Any) -> dict:
     return d
 
 
+def resolve_impl(kw: Any) -> str:
+    """Runtime that wraps the model: ``kw["impl"]`` (default ``"native"``), except that a request for
+    ``fsdp2.offload_policy`` goes to torch FSDP2 with ``CPUOffloadPolicy``.  The native runtime keeps
+    its flat shards, fp32 masters and AdamW moments in device memory (an 8B model's optimizer state is
+    12 bytes per parameter over the shard group, a few GB per GPU of 180 GB) and has no host-resident
+    mode; routing the request keeps reference configs that offload working instead of ignoring the key."""
+    kw = to_container(kw) if not isinstance(kw, dict) else kw
+    impl = kw.get("impl", "native")
+    fsdp2 = kw.get("fsdp2") or {}
+    if impl == "native" and isinstance(fsdp2, dict) and fsdp2.get("offload_policy"):
+        return "torch"
+    if impl not in ("native", "torch"):
+        raise ValueError(f"parallel.backend_kwargs.impl must be 'native' or 'torch', got {impl!r}")
+    return impl
+
+
 def parallelize_model(model: nn.Module, parallel_mesh: ParallelMesh, backend_kwargs: Optional[dict] = None,
                       device: Optional[torch.device] = None) -> nn.Module:
     kw = dict(to_container(backend_kwargs) if backend_kwargs is not None else {})
-    impl = kw.pop("impl", "native")
+    impl = resolve_impl(kw)
+    if kw.pop("impl", "native") != impl:
+        logger.warning("fsdp2.offload_policy=true: wrapping with torch FSDP2 + CPUOffloadPolicy "
+                       "(the native runtime keeps its shards in device memory)")
     sequence_parallel = bool(kw.pop("sequence_parallel", False))
     cp_cfg = kw.pop("context_parallel", {}) or {}
     comm_cfg = kw.pop("comm", {}) or {}

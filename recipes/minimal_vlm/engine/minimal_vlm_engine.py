@@ -13,7 +13,7 @@ import math
 import torch
 
 from mvp_engine.data import TorchLoader
-from mvp_engine.distributed.parallelize import parallelize_model
+from mvp_engine.distributed.parallelize import parallelize_model, resolve_impl
 from mvp_engine.engine import ENGINE_REGISTRY, Engine, TrainStepContext
 from mvp_engine.kit import OptimKit
 from mvp_engine.kit.llm.data.collator import varlen_metadata
@@ -45,7 +45,7 @@ class MinimalVLMEngine(Engine):
                             collate_fn=MinimalVLMCollator(pad_token_id=int(self.processor.tokenizer.pad_token_id)))
 
     def prepare_model(self) -> torch.nn.Module:
-        native = self.config.parallel.backend_kwargs.impl == "native"
+        native = resolve_impl(self.config.parallel.backend_kwargs) == "native"
         meta = native and not self.config.model.load_pretrained_model
         model = build_qwen3_vl_model(self.config.model, seed=int(self.config.seed),
                                      device="meta" if meta else self.device)

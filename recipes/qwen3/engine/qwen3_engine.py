@@ -18,7 +18,7 @@ from typing import Any
 
 import torch
 
-from mvp_engine.distributed.parallelize import parallelize_model
+from mvp_engine.distributed.parallelize import parallelize_model, resolve_impl
 from mvp_engine.engine import ENGINE_REGISTRY, Engine, TrainStepContext
 from mvp_engine.kit import (LLMDataKit, LLMDataSpec, LLMLoaderSpec, LLMModelKit, LLMPackingSpec,
                             LLMPretrainTextSchemaHandler, LLMPretrainTextTokenizationHandler, LLMSampleSpec,
@@ -99,7 +99,7 @@ class Qwen3Engine(Engine):
 
     # -------------------------------------------------------------- model
     def _native(self) -> bool:
-        return self.config.parallel.backend_kwargs.impl == "native"
+        return resolve_impl(self.config.parallel.backend_kwargs) == "native"
 
     def prepare_model(self) -> torch.nn.Module:
         m = self.config.model

@@ -21,7 +21,7 @@ from pathlib import Path
 
 import torch
 
-from mvp_engine.distributed.parallelize import parallelize_model
+from mvp_engine.distributed.parallelize import parallelize_model, resolve_impl
 from mvp_engine.engine import ENGINE_REGISTRY, Engine, TrainStepContext
 from mvp_engine.kit import MFUKit, OptimKit, TokenNormedLossKit
 from mvp_engine.kit.mllm import (MLLMDataKit, MLLMDataSpec, MLLMLoaderSpec, MLLMModelKit, MLLMPackingSpec,
@@ -111,7 +111,7 @@ class Qwen3VLEngine(Engine):
 
     # -------------------------------------------------------------- model
     def _native(self) -> bool:
-        return self.config.parallel.backend_kwargs.impl == "native"
+        return resolve_impl(self.config.parallel.backend_kwargs) == "native"
 
     def prepare_model(self) -> torch.nn.Module:
         m = self.config.model

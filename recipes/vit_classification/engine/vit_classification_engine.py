@@ -14,6 +14,7 @@ from typing import TypedDict
 
 import torch
 
+from mvp_engine.distributed.parallelize import resolve_impl
 from mvp_engine.distributed.utils import is_main_process
 from mvp_engine.engine import ENGINE_REGISTRY, TrainStepContext
 from mvp_engine.engine.map_style import MapStyleEngine
@@ -52,7 +53,7 @@ class ViTClassificationEngine(MapStyleEngine):
         return kw
 
     def build_model(self) -> torch.nn.Module:
-        on_meta = self.config.parallel.backend_kwargs.impl == "native" and not self.config.model.load_pretrained_weights
+        on_meta = resolve_impl(self.config.parallel.backend_kwargs) == "native" and not self.config.model.load_pretrained_weights
         model = build_vit_model(self.config.model, seed=int(self.config.seed), device="meta" if on_meta else None)
         return model if on_meta else model.to(self.device)
 
