@@ -13,6 +13,8 @@ from typing import Literal, Optional
 
 from pydantic import BaseModel, ConfigDict, Field, field_validator
 
+from ..utils.tracing import TraceConfig
+
 
 class BaseLogConfig(BaseModel):
     model_config = ConfigDict(frozen=False)
@@ -160,6 +162,8 @@ class BaseEngineConfig(BaseModel):
     optim: BaseOptimConfig = Field(default_factory=BaseOptimConfig)
     loop: BaseLoopConfig = Field(default_factory=BaseLoopConfig)
     checkpoint: BaseCheckpointConfig = Field(default_factory=BaseCheckpointConfig)
+    # NVTX ranges per phase / block and an opt-in torch.profiler window (all off by default)
+    trace: TraceConfig = Field(default_factory=TraceConfig)
     # A checkpoint directory to resume from, or "latest": the newest complete checkpoint of this
     # project (none -> fresh start), for automatic restarts after a failure.
     resume: Optional[str] = None

@@ -57,6 +57,7 @@ from ..utils.log import init_logger, logger
 from ..utils.log.backend import FileBackend, TerminalBackend, WandbBackend
 from ..utils.log.timer import CudaStepTimer, Timer
 from ..utils.misc import calculate_model_size, get_device, get_git_info
+from ..utils.tracing import StepTracer, TraceConfig
 from ..utils.training import GradientAccumulationState, GradientScaler, accumulate_gradients, clip_grad_norm_
 from .checkpoint_store import COMPLETE_MARKER, CheckpointStore, latest_complete_checkpoint
 
@@ -126,6 +127,8 @@ class Engine(ABC):
         self._cuda_timer = CudaStepTimer()
         self._step_timer_running = False
         self._watchdog = None
+        # phase ranges only (MVP_NVTX=1 or trace.nvtx) until before_train builds the configured tracer
+        self.tracer = StepTracer(TraceConfig(nvtx=self.config.trace.nvtx))
 
     # ------------------------------------------------------------ properties
     def prepare_config(self, config: Any) -> BaseEngineConfig:
@@ -333,6 +336,12 @@ class Engine(ABC):
         from ..distributed.watchdog import start_default_watchdog
 
         self._watchdog = start_default_watchdog()
+        rank = dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+        self.tracer.close()
+        self.tracer = StepTracer(self.config.trace, out_dir=self.project_dir / "profile", rank=rank)
+        hooked = self.tracer.attach_blocks(self.unwrapped_model)
+        if hooked:
+            logger.info(f"NVTX ranges on {hooked} blocks")
         logger.info("Initializing Timer...")
         self.timer = Timer(total_progress=self.total_steps, window_size=self.config.log.timer_window_size)
 
@@ -364,7 +373,8 @@ class Engine(ABC):
         self.timer.set_progress(self.step)
         stream = self._micro_batches()
         while self.progress < 1.0:
-            with self.timer.scope("data_time"):
+            self.tracer.begin_step(self.step)
+            with self.timer.scope("data_time"), self.tracer.range("data"):
                 ctx = self._stage(next(stream))
             if self._watchdog is not None:
                 self._watchdog.check()  # a silent peer ends the run before the next collective
@@ -372,6 +382,7 @@ class Engine(ABC):
                 self.train_exec_step(ctx)
             if ctx.optimizer_step_completed:
                 assert ctx.outputs is not None, "The forward step must populate ctx.outputs."
+                self.tracer.end_step(self.step)
                 self.step += 1
                 self.timer.tick()
                 self.train_post_step(ctx)
@@ -387,12 +398,15 @@ class Engine(ABC):
         if len(micro_batches) != expected:
             raise ValueError(f"expected {expected} micro-batches, got {len(micro_batches)}")
         contexts = []
+        self.tracer.begin_step(self.step)
         for data in micro_batches:
-            ctx = self._stage(data)
+            with self.tracer.range("data"):
+                ctx = self._stage(data)
             self.train_exec_step(ctx)
             contexts.append(ctx)
         if not contexts[-1].optimizer_step_completed:
             raise RuntimeError("the last micro-batch did not complete an optimizer step")
+        self.tracer.end_step(self.step)
         self.step += 1
         return contexts[-1].outputs or {}
 
@@ -403,9 +417,12 @@ class Engine(ABC):
         if not self._step_timer_running:
             self._cuda_timer.start()
             self._step_timer_running = True
-        self.forward_step(ctx)
-        self.backward_step(ctx)
-        self.optimizer_step(ctx)
+        with self.tracer.range("forward"):
+            self.forward_step(ctx)
+        with self.tracer.range("backward"):
+            self.backward_step(ctx)
+        with self.tracer.range("optimizer"):
+            self.optimizer_step(ctx)
         if ctx.optimizer_step_completed:
             self._step_timer_running = False
             self.step_time_ms = CudaStepTimer.max_over_ranks(self._cuda_timer.stop())
@@ -462,6 +479,7 @@ class Engine(ABC):
     def after_train(self) -> None:
         if self._watchdog is not None:
             self._watchdog.stop()
+        self.tracer.close()
         if not self.config.dev_mode:
             self.save(force=True)
         logger.info("Training finished!")
