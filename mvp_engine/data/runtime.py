@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import array
+import bisect
 import hashlib
 import itertools
 import json
@@ -102,38 +104,126 @@ def register_source(name: str) -> Callable[[SourceFn], SourceFn]:
     return deco
 
 
-def _read_rows(path: str) -> list[dict]:
+class _JsonlRows:
+    """Rows of a ``.jsonl`` file, parsed on demand: the index holds the byte offset of each non-blank
+    line (8 bytes per row), so a corpus is never held as Python objects, on any rank."""
+
+    def __init__(self, path: str) -> None:
+        self.path = path
+        offsets, pos = [], 0
+        with open(path, "rb") as f:
+            for line in f:
+                if line.strip():
+                    offsets.append(pos)
+                pos += len(line)
+        self.offsets = array.array("q", offsets)
+
+    def __len__(self) -> int:
+        return len(self.offsets)
+
+    def take(self, indices: Sequence[int]) -> list[dict]:
+        out = []
+        with open(self.path, "rb") as f:
+            for i in indices:
+                f.seek(self.offsets[i])
+                out.append(json.loads(f.readline()))
+        return out
+
+
+class _ParquetRows:
+    """Rows of a ``.parquet`` file: one memory-mapped Arrow table, rows converted per chunk."""
+
+    def __init__(self, path: str) -> None:
+        import pyarrow.parquet as pq
+
+        self.table = pq.read_table(path, memory_map=True)
+
+    def __len__(self) -> int:
+        return self.table.num_rows
+
+    def take(self, indices: Sequence[int]) -> list[dict]:
+        return self.table.take(list(indices)).to_pylist()
+
+
+class _ListRows:
+    def __init__(self, rows: list) -> None:
+        self.rows = rows
+
+    def __len__(self) -> int:
+        return len(self.rows)
+
+    def take(self, indices: Sequence[int]) -> list[dict]:
+        return [self.rows[i] for i in indices]
+
+
+class _ConcatRows:
+    """Several row sources seen as one, global index = offset of the part + index within it."""
+
+    def __init__(self, parts: list) -> None:
+        self.parts = parts
+        self.starts = list(itertools.accumulate((len(p) for p in parts), initial=0))
+
+    def __len__(self) -> int:
+        return self.starts[-1]
+
+    def take(self, indices: Sequence[int]) -> list[dict]:
+        out = []
+        for i in indices:
+            k = bisect.bisect_right(self.starts, i) - 1
+            out.extend(self.parts[k].take([i - self.starts[k]]))
+        return out
+
+
+_ROW_SOURCES: dict[tuple, Any] = {}
+
+
+def _open_rows(path: str):
+    """Row source of a file (``.jsonl``, ``.parquet``, ``.json`` list, or a ``.json`` manifest
+    ``{"files": [...]}`` of such files, relative to the manifest), built once per process and file
+    version and shared by every epoch."""
+    st = os.stat(path)
+    key = (os.path.abspath(path), st.st_size, st.st_mtime_ns)
+    src = _ROW_SOURCES.get(key)
+    if src is not None:
+        return src
     if path.endswith(".jsonl"):
-        with open(path) as f:
-            return [json.loads(line) for line in f if line.strip()]
-    if path.endswith(".json"):
+        src = _JsonlRows(path)
+    elif path.endswith(".parquet"):
+        src = _ParquetRows(path)
+    elif path.endswith(".json"):
         with open(path) as f:
             data = json.load(f)
         if isinstance(data, dict) and "files" in data:
             base = os.path.dirname(path)
-            rows: list[dict] = []
-            for fp in data["files"]:
-                rows.extend(_read_rows(os.path.join(base, fp)))
-            return rows
-        return list(data)
-    if path.endswith(".parquet"):
-        import pyarrow.parquet as pq
+            src = _ConcatRows([_open_rows(os.path.join(base, fp)) for fp in data["files"]])
+        else:
+            src = _ListRows(list(data))
+    else:
+        raise ValueError(f"Unsupported file source: {path}")
+    _ROW_SOURCES[key] = src
+    return src
 
-        return pq.read_table(path).to_pylist()
-    raise ValueError(f"Unsupported file source: {path}")
+
+def _read_rows(path: str) -> list[dict]:
+    """Every row of a file source, in file order."""
+    src = _open_rows(path)
+    return src.take(range(len(src)))
 
 
 @register_source("jsonl")
 @register_source("json")
 @register_source("parquet")
 def _file_source(path: str, ctx: RuntimeContext, opts: dict) -> Iterator[dict]:
-    rows = _read_rows(path)
-    order = list(range(len(rows)))
+    src = _open_rows(path)
+    order = list(range(len(src)))
     if opts.get("shuffle_mode", "none") != "none":
         ctx_all = RuntimeContext(seed=ctx.seed, epoch=ctx.epoch)
         ctx_all.rng("order").shuffle(order)
-    for i in order[ctx.shard_index::ctx.num_shards]:
-        yield dict(rows[i], __global_index__=i)
+    mine = order[ctx.shard_index::ctx.num_shards]
+    for s in range(0, len(mine), 256):
+        chunk = mine[s:s + 256]
+        for i, row in zip(chunk, src.take(chunk)):
+            yield dict(row, __global_index__=i)
 
 
 @register_source("lance")
