@@ -215,11 +215,12 @@ def _read_rows(path: str) -> list[dict]:
 @register_source("parquet")
 def _file_source(path: str, ctx: RuntimeContext, opts: dict) -> Iterator[dict]:
     src = _open_rows(path)
-    order = list(range(len(src)))
     if opts.get("shuffle_mode", "none") != "none":
-        ctx_all = RuntimeContext(seed=ctx.seed, epoch=ctx.epoch)
-        ctx_all.rng("order").shuffle(order)
-    mine = order[ctx.shard_index::ctx.num_shards]
+        order = list(range(len(src)))
+        RuntimeContext(seed=ctx.seed, epoch=ctx.epoch).rng("order").shuffle(order)
+        mine = order[ctx.shard_index::ctx.num_shards]
+    else:  # file order: this shard's indices without materialising the others
+        mine = range(ctx.shard_index, len(src), ctx.num_shards)
     for s in range(0, len(mine), 256):
         chunk = mine[s:s + 256]
         for i, row in zip(chunk, src.take(chunk)):

@@ -258,7 +258,8 @@ class Engine(ABC):
         if self.config.dev_mode or not due:
             return
         store, tag = self._checkpoint_store(), self._checkpoint_tag()
-        if store.is_current(tag, self.step):
+        # rank 0's view of the file system decides, so every rank takes the same branch (and barriers)
+        if broadcast_from_main(store.is_current(tag, self.step)):
             logger.info(f"Checkpoint {tag} already holds step {self.step}; not rewritten.")
             return
         logger.info(f"Saving checkpoint for step {self.step}...")
@@ -319,8 +320,8 @@ class Engine(ABC):
 
     def _resume_source(self) -> Optional[str]:
         resume = getattr(self.config, "resume", None)
-        if resume == "latest":  # the newest complete checkpoint of this run, if there is one
-            return latest_complete_checkpoint(self.project_dir / "checkpoints")
+        if resume == "latest":  # the newest complete checkpoint of this run (rank 0's view), if there is one
+            return broadcast_from_main(latest_complete_checkpoint(self.project_dir / "checkpoints"))
         return resume
 
     def before_train(self) -> None:
