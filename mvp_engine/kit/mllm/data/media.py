@@ -10,7 +10,7 @@ guards drop it.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, Sequence
+from typing import Any, Mapping, Sequence
 
 import torch
 
@@ -128,4 +128,7 @@ class MLLMMediaHandler:
     def _slot_value(sample: Any, slot: MLLMMediaSlot) -> Any:
         raw = sample._raw if hasattr(sample, "_raw") else sample
         v = raw[slot.field]
-        return v[slot.index] if slot.index is not None else v
+        v = v[slot.index] if slot.index is not None else v
+        if isinstance(v, Mapping) and ("value" in v or slot.media_type in v):  # a `media` column entry
+            return v.get("value", v.get(slot.media_type))
+        return v

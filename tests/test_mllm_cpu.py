@@ -1,5 +1,6 @@
 """Multimodal data kit on CPU: processor geometry, schema, packing, collation, guards."""
 
+import pytest
 import torch
 
 from mvp_engine.kit.mllm import (MLLMDataKit, MLLMDataSpec, MLLMLoaderSpec, MLLMPackingSpec, MLLMSampleSpec,
@@ -80,3 +81,68 @@ def test_chat_row_through_the_handler_interfaces():
     assert any(lab != -100 for lab in labels)  # the assistant reply is supervised
     sample = MLLMSample(row, schema_handler=schema, media_handler=media, tokenization_handler=tok)
     assert sample.input_ids == ids and sample.labels == labels
+
+
+def _png(w, h, colour=(200, 30, 30)):
+    import io
+
+    from PIL import Image
+
+    buf = io.BytesIO()
+    Image.new("RGB", (w, h), colour).save(buf, format="PNG")
+    return buf.getvalue()
+
+
+def test_reference_row_layouts_give_the_same_slots(tmp_path):
+    """Rows in the reference's layouts -- ``img_size`` / ``image_size`` as [width, height] pairs or dicts,
+    or a ``media`` column of {type, value, size} entries -- and rows with no size at all (read from the
+    image header) give image slots of the right [height, width], and the media handler loads their pixels."""
+    from mvp_engine.kit.mllm import QwenVLChatSchemaHandler
+
+    proc = MLLMDataKit().build_processor("synthetic", image_max_pixels=256 * 256)
+    schema = QwenVLChatSchemaHandler(proc, thinking_mode=None)
+    media = QwenVLMediaHandler(proc)
+    png = _png(96, 64)  # width 96, height 64
+    (tmp_path / "i.png").write_bytes(png)
+    msgs = [{"role": "user", "content": "<image> what colour?"}, {"role": "assistant", "content": "red"}]
+    rows = [
+        {"messages": msgs, "images": [png], "img_size": [[96, 64]]},
+        {"messages": msgs, "images": [png], "image_size": [{"width": 96, "height": 64}]},
+        {"messages": msgs, "images": [{"bytes": png}], "image_sizes": [[64, 96]]},
+        {"messages": msgs, "media": [{"type": "image", "value": png, "size": [96, 64]}]},
+        {"messages": msgs, "media": [{"image": str(tmp_path / "i.png"), "img_size": {"width": 96, "height": 64}}]},
+        {"messages": msgs, "images": [png]},  # no size column: the PNG header gives it
+        {"messages": msgs, "images": [str(tmp_path / "i.png")]},
+    ]
+    grids = []
+    for row in rows:
+        assert schema.check_row(row) is None, row
+        segs, slots, _ = schema.normalize(row)
+        assert [s.metadata["size"] for s in slots] == [[64, 96]]
+        values = [media._slot_value(row, slot) for slot in slots]
+        assert all(isinstance(v, (bytes, str, dict)) for v in values)
+        loaded = media.handlers["image"].load(slots, values, processor=proc)
+        grids.append(loaded["image_grid_thw"].tolist())
+        assert loaded["pixel_values"].shape[0] == int(loaded["image_grid_thw"].prod())
+    assert all(g == grids[0] for g in grids)
+
+
+def test_unusable_media_rows_are_dropped_with_a_reason():
+    from mvp_engine.kit.mllm import QwenVLChatSchemaHandler
+
+    proc = MLLMDataKit().build_processor("synthetic", image_max_pixels=256 * 256)
+    schema = QwenVLChatSchemaHandler(proc, thinking_mode=None)
+    msgs = [{"role": "user", "content": "<image> hi"}, {"role": "assistant", "content": "yo"}]
+    png = _png(32, 32)
+    cases = {
+        "raw.image_size_count_mismatch": {"images": [png], "img_size": [[32, 32], [32, 32]]},
+        "raw.invalid_image_size": {"images": [b"not an image"]},
+        "raw.unsupported_media_type": {"media": [{"type": "video", "value": png, "size": [32, 32]}]},
+        "raw.media_without_value": {"media": [{"type": "image", "size": [32, 32]}]},
+        "raw.invalid_media": {"media": "x.png"},
+    }
+    for reason, extra in cases.items():
+        assert schema.check_row({"messages": msgs, **extra}) == reason
+    with pytest.raises(ValueError, match="more_image_placeholders"):
+        schema.normalize({"messages": [{"role": "user", "content": "<image><image>"},
+                                       {"role": "assistant", "content": "a"}], "images": [png]})
