@@ -84,3 +84,27 @@ def test_registry():
     assert r.get("A") is A and r["bee"] is b and "C" in r
     with pytest.raises(KeyError):
         r.get("missing")
+
+
+def _reference_yamls():
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent / "baseline" / "_ref" / "recipes"
+    return sorted(root.glob("*/configs/*.yaml")) if root.is_dir() else []
+
+
+@pytest.mark.skipif(not _reference_yamls(), reason="the reference is not installed under baseline/_ref")
+@pytest.mark.parametrize("path", _reference_yamls(), ids=lambda p: f"{p.parts[-3]}/{p.name}")
+def test_reference_recipe_yaml_validates_unchanged(path):
+    """A recipe YAML of the reference, unmodified, composes with this engine's defaults and validates
+    against the same-named recipe's schema here; its engine name is registered."""
+    from pathlib import Path
+
+    from mvp_engine.engine import ENGINE_REGISTRY
+    from mvp_engine.launch import import_recipe_modules
+
+    import_recipe_modules(Path(__file__).resolve().parent.parent / "recipes" / path.parts[-3])
+    cfg = compose_config(str(path), [])
+    engine_cls = ENGINE_REGISTRY.get(cfg["engine"])
+    parsed = engine_cls.ConfigClass.model_validate(cfg)
+    assert parsed.engine == cfg["engine"]
