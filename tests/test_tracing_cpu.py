@@ -59,7 +59,7 @@ def test_block_hooks_attach_to_blocks_only_and_detach():
     named.close()
 
 
-def _profiled_run(rank, world, port, out_dir):
+def _profiled_run(rank, world, port, out_dir, shard=1):
     from mvp_engine.engine import ENGINE_REGISTRY
     from mvp_engine.launch import import_recipe_modules
     from mvp_engine.testing.utils import load_smoke_test_config
@@ -70,7 +70,7 @@ def _profiled_run(rank, world, port, out_dir):
             "model.config_overrides.num_hidden_layers=2", "optim.mixed_precision=fp32", "log.backends=[terminal]",
             "data.train_path=synthetic://text?vocab=512&min_len=16&max_len=96", "data.max_seq_len=128",
             "optim.global_batch_size=2", "model.gradient_checkpointing.enabled=false",
-            "parallel.mesh.replicate=1", "parallel.mesh.shard=1", "loop.total_steps=3", "dev_mode=true",
+            "parallel.mesh.replicate=1", f"parallel.mesh.shard={shard}", "loop.total_steps=3", "dev_mode=true",
             "trace.profiler.enabled=true", "trace.profiler.wait=0", "trace.profiler.warmup=1",
             "trace.profiler.active=1", "trace.nvtx=true", "trace.nvtx_blocks=true")
     cfg = load_smoke_test_config(root, "synthetic_8b", output_dir=Path(out_dir), run_id="tr", config_overrides=over)
@@ -85,6 +85,12 @@ def test_profiler_window_writes_a_trace_with_phase_labels(tmp_path):
     events = json.loads(Path(traces[0]).read_text())["traceEvents"]
     names = {e.get("name") for e in events}
     assert {"data", "forward", "backward", "optimizer"} <= names, sorted(n for n in names if n)[:40]
+
+
+def test_each_rank_writes_its_own_trace(tmp_path):
+    per_rank = spawn_workers(_profiled_run, 2, str(tmp_path), 2, timeout=300)
+    assert [[Path(p).name for p in t] for t in per_rank] == [["rank0_step2.json"], ["rank1_step2.json"]]
+    assert per_rank[0][0] != per_rank[1][0]
 
 
 def test_profiler_config_bounds():
